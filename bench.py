@@ -1,0 +1,441 @@
+"""Benchmark: fused GGML dequantize x matvec on B200.
+
+Workload (one "step"): the kernel microbench of BASELINE.json configs[1] at
+batch 1 -- y = W x for W in {Q8_0, Q4_K, Q5_K, Q6_K, IQ4_XS} x {4096x4096,
+14336x4096, 4096x14336} (rows x cols), 15 matrices, quantized by the package's
+quantizers (byte-identical to the reference's fixture encoders; IQ4_XS by the
+package's own) from seeded N(0, 0.02) fp32 weights, x ~ N(0, 1) fp32.  A step
+streams 492 MB of weights, far above the 126 MB L2, so every matrix is read
+cold from HBM (inputs > L2; no flush needed).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Metric: weight-stream throughput in GB/s (algorithmic bytes / time), summed
+over ranks (weak scaling: every rank runs the whole step on its own GPU; the
+path shards by independent rows / matrices with no data-path collective).
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s @bs1 + dequant-matvec HBM GB/s (% of B200 peak), 1/2/4/8 GPU"
+TYPES = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ4_XS": 23}
+SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]  # rows x cols
+SEED = 20251201
+
+
+def workload():
+    return [(name, t, rows, cols) for (rows, cols) in SHAPES for name, t in TYPES.items()]
+
+
+def row_bytes(t: int, cols: int) -> int:
+    from pyrite_b200.ggml_types import spec
+    s = spec(t)
+    return cols // s.block_size * s.bytes_per_block
+
+
+def algo_bytes(t: int, rows: int, cols: int, ncols: int = 1) -> int:
+    """Algorithmic bytes of one launch: weights once, x and y once."""
+    return rows * row_bytes(t, cols) + ncols * (rows + cols) * 4
+
+
+def build_payloads() -> dict[tuple[int, int, int], bytes]:
+    from pyrite_b200.quantize import gaussian_weights, quantize
+    out = {}
+    for (rows, cols) in SHAPES:
+        w = gaussian_weights(rows, cols, SEED + rows * 31 + cols)
+        for name, t in TYPES.items():
+            out[(t, rows, cols)] = quantize(t, w)
+    return out
+
+
+def x_vectors() -> dict[int, np.ndarray]:
+    rng = np.random.default_rng(SEED)
+    return {cols: rng.normal(0.0, 1.0, cols).astype(np.float32) for cols in sorted({c for _, c in SHAPES})}
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of this rank's GPU during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- helpers
+def measured_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(kernel_key: str) -> float | None:
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "dram_traffic.json"
+    if not p.is_file():
+        return None
+    try:
+        return json.loads(p.read_text()).get(kernel_key)
+    except ValueError:
+        return None
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus and world > 1:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    return world, rank, local
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args) -> None:
+    import torch
+
+    from pyrite_b200 import _lib
+    from pyrite_b200.kernels import cuda as K
+
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+
+    lib = _lib.require()
+    payloads = build_payloads()
+    xs = x_vectors()
+    wl = workload()
+    W = {key: torch.frombuffer(bytearray(p), dtype=torch.uint8).to(dev) for key, p in payloads.items()}
+    X = {c: torch.from_numpy(v).to(dev) for c, v in xs.items()}
+    Y = {(t, r, c): torch.empty(r, dtype=torch.float32, device=dev) for _, t, r, c in wl}
+    step_bytes = sum(algo_bytes(t, r, c) for _, t, r, c in wl)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        for _, t, r, c in wl:
+            K.matvec(t, W[(t, r, c)], X[c], r, c, out=Y[(t, r, c)], static_weights=True)
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    if K.status() != 0:
+        raise SystemExit("device status word set: a kernel wait timed out")
+
+    # capture one step in a CUDA graph (launch overhead out of the timed loop)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        step()  # warm (function attributes set before capture)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        if pg:
+            pg.barrier()
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    ms = start.elapsed_time(end)
+    if pg:
+        t = torch.tensor([ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * step_bytes / (ms_per_step * 1e-3) / 1e9
+
+    # ---- per-kernel live timing: each matrix alone, rotating over copies so every
+    # launch reads cold HBM (copies total > 4 x L2), timed with events on its stream
+    per_kernel = []
+    if rank == 0:
+        for name, t, r, c in wl:
+            size = r * row_bytes(t, c)
+            copies = max(3, -(-512 * 2**20 // size))
+            src = W[(t, r, c)]
+            bufs = [src.clone() for _ in range(copies)]
+            reps = 2
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(g, stream=stream):
+                    for _ in range(reps):
+                        for b in bufs:
+                            K.matvec(t, b, X[c], r, c, out=Y[(t, r, c)], static_weights=True)
+                g.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+            gbs = algo_bytes(t, r, c) / (us * 1e-6) / 1e9
+            per_kernel.append({"type": name, "rows": r, "cols": c, "us": round(us, 3), "GBps": round(gbs, 1)})
+            del g, bufs
+            torch.cuda.empty_cache()
+
+    # ---- end to end through the reference-facing C ABI (pyrite_matvec):
+    # host payload + host fp64 x in, host fp64 y out, H2D/D2H inside the timing
+    e2e = None
+    if rank == 0 and not args.no_e2e:
+        import ctypes
+        pd = ctypes.POINTER(ctypes.c_double)
+        host = {key: torch.frombuffer(bytearray(p), dtype=torch.uint8).pin_memory() for key, p in payloads.items()}
+        xd = {c: np.ascontiguousarray(v, dtype=np.float64) for c, v in xs.items()}
+        yd = {(t, r, c): np.zeros(r) for _, t, r, c in wl}
+
+        def e2e_step():
+            for _, t, r, c in wl:
+                hb = host[(t, r, c)]
+                rc = lib.pyrite_matvec(t, hb.data_ptr(), hb.numel(), xd[c].ctypes.data_as(pd),
+                                       yd[(t, r, c)].ctypes.data_as(pd), r, c)
+                if rc != 0:
+                    raise SystemExit(f"pyrite_matvec failed ({rc})")
+        e2e_step()
+        t0 = time.perf_counter()
+        e2e_steps = max(1, min(args.steps, 5))
+        for _ in range(e2e_steps):
+            e2e_step()
+        dt = (time.perf_counter() - t0) / e2e_steps
+        h2d = sum(len(payloads[(t, r, c)]) + c * 8 for _, t, r, c in wl)
+        d2h = sum(r * 8 for _, t, r, c in wl)
+        e2e = {"value": round(step_bytes / dt / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "api": "pyrite_matvec (reference-compatible C ABI, fp64 host buffers, "
+               "payload copied to HBM every call; pinned host payload)", "ms_per_step": round(dt * 1e3, 3),
+               "steps": e2e_steps}
+
+    cpu = cpu_baseline(payloads, xs, wl, budget_s=args.cpu_seconds) if (rank == 0 and not args.no_cpu) else None
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        dom = max(per_kernel, key=lambda k: k["us"])
+        dom_bytes = algo_bytes(TYPES[dom["type"]], dom["rows"], dom["cols"])
+        achieved = dom_bytes / (dom["us"] * 1e-6) / 1e9
+        key = f"mv_stream_kernel<{dom['type']}>@{dom['rows']}x{dom['cols']}"
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "u8 codes, fp32 accumulate",
+            "data": "synthetic: seeded N(0,0.02) fp32 weights quantized by pyrite_b200.quantize; x ~ N(0,1)",
+            "config": {"workload": "configs[1] kernel microbench, batch 1: {Q8_0,Q4_K,Q5_K,Q6_K,IQ4_XS} x "
+                                   "{4096x4096,14336x4096,4096x14336}, 15 matvecs per step",
+                       "global_batch": 1, "ncols": 1, "step_bytes": step_bytes,
+                       "l2": "inputs larger than L2 (492 MB of weights per step vs 126 MB L2)",
+                       "parallelism": f"replica x{world} (weak)", "launch": "CUDA graph of 15 PDL launches"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
+                         "kernel": key, "algorithmic_bytes_per_launch": dom_bytes,
+                         "traffic": ncu_traffic(key)},
+            "whole_step_frac_of_peak": round(value / world / peak, 4),
+            "kernels": per_kernel,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps * len(wl),
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------- CPU baseline
+def _ref_kernel():
+    from oracle import oracle as O
+    if O.reference_lib() is None:
+        try:
+            O.build()
+        except Exception:  # noqa: BLE001
+            pass
+    if O.reference_lib() is not None:
+        return O.reference_matvec, "reference"
+    return O.matvec, "port"
+
+
+def cpu_baseline(payloads, xs, wl, budget_s: float = 12.0, threads: int = 1) -> dict:
+    """Reference C kernel (oracle/_ref, built from pyrite/kernels/native.c) on the
+    host cores: a bounded sample -- the first rows of each of the 15 matrices,
+    about budget_s / 15 seconds each -- timed single threaded (the reference
+    kernel is scalar and single threaded)."""
+    fn, kind = _ref_kernel()
+    total_b, total_t = 0, 0.0
+    per = budget_s / len(wl)
+    rows_done = {}
+    for _, t, r, c in wl:
+        rb = row_bytes(t, c)
+        x64 = xs[c].astype(np.float64)
+        # calibrate with 8 rows, then size the sample to ~per seconds
+        t0 = time.perf_counter()
+        fn(t, payloads[(t, r, c)][: 8 * rb], x64, 8, c)
+        dt8 = max(time.perf_counter() - t0, 1e-6)
+        n = int(min(r, max(8, 8 * per / dt8)))
+        t0 = time.perf_counter()
+        fn(t, payloads[(t, r, c)][: n * rb], x64, n, c)
+        dt = time.perf_counter() - t0
+        total_b += n * rb + (n + c) * 4
+        total_t += dt
+        rows_done[f"{t}:{r}x{c}"] = n
+    return {"value": round(total_b / total_t / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": f"first rows of each of the 15 matrices (~{per:.1f} s each, {sum(rows_done.values())} rows "
+                      f"in total), single thread, fp64 as the reference computes", "seconds": round(total_t, 2)}
+
+
+def run_reference(args) -> None:
+    """Reference arm: the reference's own CPU kernel on this box's host cores."""
+    world, rank, _ = dist_setup(args.gpus)
+    if rank != 0:
+        return
+    from concurrent.futures import ThreadPoolExecutor
+    fn, kind = _ref_kernel()
+    payloads = build_payloads()
+    xs = x_vectors()
+    wl = workload()
+    threads = os.cpu_count() or 1
+    # each step: the same fraction of every matrix's rows (a bounded sample)
+    frac = args.ref_fraction
+    jobs = []
+    for _, t, r, c in wl:
+        n = max(threads, int(r * frac))
+        rb = row_bytes(t, c)
+        x64 = xs[c].astype(np.float64)
+        for i in range(threads):
+            a, b = n * i // threads, n * (i + 1) // threads
+            if b > a:
+                jobs.append((t, payloads[(t, r, c)][a * rb:b * rb], x64, b - a, c))
+    step_bytes = sum(len(j[1]) + (j[3] + j[4]) * 4 for j in jobs)
+
+    def step(pool):
+        list(pool.map(lambda j: fn(*j), jobs))
+
+    with ThreadPoolExecutor(threads) as pool:
+        for _ in range(args.warmup):
+            step(pool)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step(pool)
+        dt = (time.perf_counter() - t0) / args.steps
+    value = step_bytes / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp64", "data": "synthetic (same payloads as ours)",
+        "config": {"workload": f"configs[1] kernel microbench, batch 1, each step the first {frac:.0%} of the "
+                               "rows of each of the 15 matrices", "global_batch": 1, "ncols": 1,
+                   "parallelism": f"{threads} host threads over row ranges"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": f"{frac:.0%} of the rows of each matrix per step"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ref-fraction", type=float, default=0.02)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,111 @@
+/*
+ * pyrite_b200.h -- C ABI of libpyrite_b200.so, the B200 implementation of
+ * Pyrite's fused GGML dequantize x matrix-vector kernel library.
+ *
+ * Section 1 is a drop-in for the reference's C kernel library
+ * (pyrite/kernels/native.c, bound by ctypes in pyrite/kernels/native.py:
+ * 126-147): same symbol names, signatures, argument meaning and return codes.
+ * Section 2 is the device-resident path used by the B200 runtime.
+ *
+ * All entry points are plain C: pointers, sizes and an opaque stream handle.
+ * Return codes: 0 on success, negative on error (see PYRITE_E_*).
+ */
+#ifndef PYRITE_B200_H
+#define PYRITE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Error codes.  -1..-3 are the reference's (pyrite/kernels/native.c:496-525);
+ * -4 is new: the CUDA runtime reported an error (no device, launch failure). */
+#define PYRITE_E_TYPE (-1)   /* unknown / non-decodable GGML type id          */
+#define PYRITE_E_SHAPE (-2)  /* rows or cols zero, cols not block aligned,
+                                or the byte size overflows                    */
+#define PYRITE_E_BUFFER (-3) /* NULL pointer, or data_len != rows * row_bytes */
+#define PYRITE_E_CUDA (-4)   /* CUDA error                                    */
+
+/* ---- 1. Reference-compatible entry points (host buffers, fp64) ---------- */
+
+/* Replaces pyrite_native_types (pyrite/kernels/native.c:484-494).
+ * ids == NULL: returns the number of supported GGML type ids.  Otherwise
+ * writes up to `capacity` ids and returns how many were written.  The set is
+ * the reference's 21 decodable types, in the reference's order. */
+int pyrite_native_types(int *ids, size_t capacity);
+
+/* Replaces pyrite_matvec (pyrite/kernels/native.c:518-555).
+ * out[r] = sum_c W[r, c] * x[c] for `rows` consecutive rows of a GGML matrix
+ * whose payload (`data`, `data_len` bytes, host memory, borrowed for the call)
+ * holds rows of cols/block_size blocks each.  x has `cols` doubles, out has
+ * `rows`.  Runs on the current CUDA device, decoding and accumulating in fp64;
+ * blocks until `out` is written. */
+int pyrite_matvec(int type_id, const uint8_t *data, size_t data_len, const double *x,
+                  double *out, size_t rows, size_t cols);
+
+/* Replaces pyrite_dequantize_rows (pyrite/kernels/native.c:557-576).
+ * Writes rows x cols doubles (row-major) decoded from the payload.  Values are
+ * identical to the reference's. */
+int pyrite_dequantize_rows(int type_id, const uint8_t *data, size_t data_len, double *out,
+                           size_t rows, size_t cols);
+
+/* ---- 2. Device-resident path (new; no reference counterpart) ------------- */
+
+/* Geometry of a type: values per block and bytes per block (the reference
+ * keeps this table in pyrite/ggml_types.py:34-73). */
+int pyrite_type_geometry(int type_id, size_t *block_size, size_t *bytes_per_block);
+
+/* Flags of pyrite_cuda_matvec. */
+#define PYRITE_F_STATIC_WEIGHTS 1u /* the payload is not written by the kernel that precedes
+                                      this call in the stream: its HBM stream may start
+                                      before that kernel finishes (programmatic dependent
+                                      launch); x and y are still ordered after it */
+
+/* y[c*ldy + r] = sum_k W[r, k] * x[c*ldx + k] for r < rows, c < ncols.
+ * `weights` (weights_len == rows * row_bytes) , `x` and `y` are device
+ * pointers; fp32 activations, fp32 accumulation.  Enqueued on `stream`
+ * (a cudaStream_t, NULL = legacy default stream); returns without waiting.
+ * Same validation codes as pyrite_matvec.  This is the row-range call of the
+ * reference's executor (pyrite/executor.py:481-509): pass the address of the
+ * first row of the range and the range's row count.  `flags`: PYRITE_F_*. */
+int pyrite_cuda_matvec(int type_id, const void *weights, size_t weights_len, const float *x,
+                       long long ldx, float *y, long long ldy, size_t rows, size_t cols,
+                       size_t ncols, unsigned flags, void *stream);
+
+/* out[r*cols + c] = W[r, c] as fp32 (the correctly rounded value of the
+ * reference's fp64 result).  Device pointers; enqueued on `stream`. */
+int pyrite_cuda_dequantize_rows(int type_id, const void *weights, size_t weights_len, float *out,
+                                size_t rows, size_t cols, void *stream);
+
+/* Number of visible CUDA devices (0 when there is no usable driver/device). */
+int pyrite_cuda_device_count(void);
+
+/* Device status word of the current device: bit 0 set when a kernel gave up
+ * waiting for a copy (bounded waits never hang the GPU).  Synchronous read;
+ * clears the word when `clear` is nonzero.  Returns the word or PYRITE_E_CUDA. */
+int pyrite_cuda_status(int clear);
+
+/* ---- 3. Quantizers (host; new) -------------------------------------------- */
+
+/* Encode `count` values (a multiple of the block size) into GGML blocks at
+ * `dst` (dst_len == count / block_size * bytes_per_block), using `threads`
+ * host threads (<= 0: all).  Q8_0 / Q4_0 reproduce the reference's fixture
+ * encoders byte for byte (scripts/build_vocab_fixture.py:54-92), Q2_K..Q6_K
+ * its naive K-quant encoders (tests/k_quant.py:61-285); IQ4_NL / IQ4_XS are
+ * this library's own (the reference has no quantizer for them). */
+int pyrite_quantize(int type_id, const double *src, size_t count, uint8_t *dst, size_t dst_len,
+                    int threads);
+
+/* Type ids pyrite_quantize accepts (ids == NULL: the count). */
+int pyrite_quantize_types(int *ids, size_t capacity);
+
+/* Static description of a return code. */
+const char *pyrite_error_string(int code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PYRITE_B200_H */

@@ -1,0 +1,225 @@
+// capi.cu -- the C ABI of libpyrite_b200.so.
+//
+// Two families of entry points (declared in include/pyrite_b200.h):
+//   * pyrite_native_types / pyrite_matvec / pyrite_dequantize_rows: the exact
+//     symbols, signatures and return codes of the reference's C kernel
+//     library (pyrite/kernels/native.c:484-576), so the reference's ctypes
+//     shim can load this library unchanged.  Buffers are host memory and fp64;
+//     the work runs on the current CUDA device in fp64.
+//   * pyrite_cuda_*: the device-resident path.  Weights, x and y live in device
+//     memory; fp32 activations; the call enqueues on the caller's stream and
+//     returns without synchronising.
+#include <cstring>
+#include <mutex>
+
+#include "kernels.cuh"
+#include "../../include/pyrite_b200.h"
+
+namespace pyr {
+
+__device__ int g_status_word;
+
+int* device_status_word() {
+  static int* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<int*>(p);
+  }
+  return addr[dev];
+}
+
+namespace {
+
+// Same validation and codes as the reference's matrix_geometry
+// (pyrite/kernels/native.c:496-516): -1 unknown type, -2 bad shape/overflow.
+int geometry(int type_id, size_t rows, size_t cols, size_t* row_bytes, const TypeGeo** out) {
+  const TypeGeo* t = find_type(type_id);
+  if (!t) return PYRITE_E_TYPE;
+  if (rows == 0 || cols == 0 || cols % (size_t)t->bs != 0 || cols / t->bs > SIZE_MAX / t->bpb)
+    return PYRITE_E_SHAPE;
+  *row_bytes = cols / t->bs * t->bpb;
+  if (*row_bytes > SIZE_MAX / rows) return PYRITE_E_SHAPE;
+  // Kernels index rows and columns with 32-bit ints.
+  if (rows > 0x7fffffffu || cols > 0x7fffffffu) return PYRITE_E_SHAPE;
+  if (out) *out = t;
+  return 0;
+}
+
+int cuda_code(cudaError_t e) { return e == cudaSuccess ? 0 : PYRITE_E_CUDA; }
+
+// Library-owned staging for the host-buffer entry points: one stream and one
+// growable device buffer per device, serialised by a mutex.  Nothing is kept
+// between calls except this reusable scratch.
+struct HostStage {
+  std::mutex mu;
+  cudaStream_t stream = nullptr;
+  void* buf = nullptr;
+  size_t cap = 0;
+};
+HostStage g_stage[64];
+
+int stage_reserve(HostStage& st, size_t bytes) {
+  if (!st.stream && cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking) != cudaSuccess)
+    return PYRITE_E_CUDA;
+  if (bytes <= st.cap) return 0;
+  if (st.buf) cudaFree(st.buf);
+  st.buf = nullptr;
+  st.cap = 0;
+  const size_t want = (bytes + 0xFFFFF) & ~(size_t)0xFFFFF;
+  if (cudaMalloc(&st.buf, want) != cudaSuccess) {
+    cudaGetLastError();
+    return PYRITE_E_CUDA;
+  }
+  st.cap = want;
+  return 0;
+}
+
+size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+}  // namespace
+}  // namespace pyr
+
+using namespace pyr;
+
+extern "C" {
+
+int pyrite_native_types(int* ids, size_t capacity) {
+  if (ids == nullptr) return kNumTypes;
+  const size_t n = capacity < (size_t)kNumTypes ? capacity : (size_t)kNumTypes;
+  for (size_t i = 0; i < n; ++i) ids[i] = kTypes[i].id;
+  return (int)n;
+}
+
+int pyrite_type_geometry(int type_id, size_t* block_size, size_t* bytes_per_block) {
+  const TypeGeo* t = find_type(type_id);
+  if (!t) return PYRITE_E_TYPE;
+  if (block_size) *block_size = (size_t)t->bs;
+  if (bytes_per_block) *bytes_per_block = (size_t)t->bpb;
+  return 0;
+}
+
+int pyrite_matvec(int type_id, const uint8_t* data, size_t data_len, const double* x, double* out,
+                  size_t rows, size_t cols) {
+  size_t rb = 0;
+  int rc = geometry(type_id, rows, cols, &rb, nullptr);
+  if (rc) return rc;
+  if (!data || !x || !out || data_len != rb * rows) return PYRITE_E_BUFFER;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return PYRITE_E_CUDA;
+  HostStage& st = g_stage[dev];
+  std::lock_guard<std::mutex> lock(st.mu);
+  const size_t xoff = align256(data_len), yoff = xoff + align256(cols * sizeof(double));
+  if ((rc = stage_reserve(st, yoff + rows * sizeof(double)))) return rc;
+  uint8_t* dw = static_cast<uint8_t*>(st.buf);
+  double* dx = reinterpret_cast<double*>(dw + xoff);
+  double* dy = reinterpret_cast<double*>(dw + yoff);
+  if ((rc = cuda_code(cudaMemcpyAsync(dw, data, data_len, cudaMemcpyHostToDevice, st.stream)))) return rc;
+  if ((rc = cuda_code(cudaMemcpyAsync(dx, x, cols * sizeof(double), cudaMemcpyHostToDevice, st.stream))))
+    return rc;
+  MatvecArgs<double> a{dw, rb, (int)rows, (int)cols, dx, 0, dy, 0};
+  if ((rc = launch_mv_generic<double, 1>(type_id, a, st.stream))) return rc > 0 ? PYRITE_E_CUDA : rc;
+  if ((rc = cuda_code(cudaMemcpyAsync(out, dy, rows * sizeof(double), cudaMemcpyDeviceToHost, st.stream))))
+    return rc;
+  return cuda_code(cudaStreamSynchronize(st.stream));
+}
+
+int pyrite_dequantize_rows(int type_id, const uint8_t* data, size_t data_len, double* out, size_t rows,
+                           size_t cols) {
+  size_t rb = 0;
+  int rc = geometry(type_id, rows, cols, &rb, nullptr);
+  if (rc) return rc;
+  if (!data || !out || data_len != rb * rows || cols > SIZE_MAX / rows) return PYRITE_E_BUFFER;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return PYRITE_E_CUDA;
+  HostStage& st = g_stage[dev];
+  std::lock_guard<std::mutex> lock(st.mu);
+  const size_t ooff = align256(data_len);
+  if ((rc = stage_reserve(st, ooff + rows * cols * sizeof(double)))) return rc;
+  uint8_t* dw = static_cast<uint8_t*>(st.buf);
+  double* dout = reinterpret_cast<double*>(dw + ooff);
+  if ((rc = cuda_code(cudaMemcpyAsync(dw, data, data_len, cudaMemcpyHostToDevice, st.stream)))) return rc;
+  if ((rc = launch_dq_generic<double>(type_id, dw, rb, (int)rows, (int)cols, dout, (long long)cols, st.stream)))
+    return rc > 0 ? PYRITE_E_CUDA : rc;
+  if ((rc = cuda_code(cudaMemcpyAsync(out, dout, rows * cols * sizeof(double), cudaMemcpyDeviceToHost,
+                                      st.stream))))
+    return rc;
+  return cuda_code(cudaStreamSynchronize(st.stream));
+}
+
+int pyrite_cuda_matvec(int type_id, const void* weights, size_t weights_len, const float* x, long long ldx,
+                       float* y, long long ldy, size_t rows, size_t cols, size_t ncols, unsigned flags,
+                       void* stream) {
+  size_t rb = 0;
+  int rc = geometry(type_id, rows, cols, &rb, nullptr);
+  if (rc) return rc;
+  if (!weights || !x || !y || weights_len != rb * rows || ncols == 0) return PYRITE_E_BUFFER;
+  if (ncols > 1 && (ldx < (long long)cols || ldy < (long long)rows)) return PYRITE_E_BUFFER;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* w = static_cast<const uint8_t*>(weights);
+  if (ncols == 1) {
+    MatvecArgs<float> a{w, rb, (int)rows, (int)cols, x, ldx, y, ldy};
+    rc = launch_mv_stream(type_id, a, (flags & PYRITE_F_STATIC_WEIGHTS) != 0, s);
+    if (rc == 1) rc = launch_mv_generic<float, 1>(type_id, a, s);
+    return rc > 0 ? PYRITE_E_CUDA : rc;
+  }
+  // Several columns: as many 8-, 4-, 2- and 1-column passes as needed.
+  size_t c = 0;
+  while (c < ncols) {
+    const size_t left = ncols - c;
+    MatvecArgs<float> a{w, rb, (int)rows, (int)cols, x + c * ldx, ldx, y + c * ldy, ldy};
+    if (left >= 8) { rc = launch_mv_generic<float, 8>(type_id, a, s); c += 8; }
+    else if (left >= 4) { rc = launch_mv_generic<float, 4>(type_id, a, s); c += 4; }
+    else if (left >= 2) { rc = launch_mv_generic<float, 2>(type_id, a, s); c += 2; }
+    else { rc = launch_mv_generic<float, 1>(type_id, a, s); c += 1; }
+    if (rc) return rc > 0 ? PYRITE_E_CUDA : rc;
+  }
+  return 0;
+}
+
+int pyrite_cuda_dequantize_rows(int type_id, const void* weights, size_t weights_len, float* out, size_t rows,
+                                size_t cols, void* stream) {
+  size_t rb = 0;
+  int rc = geometry(type_id, rows, cols, &rb, nullptr);
+  if (rc) return rc;
+  if (!weights || !out || weights_len != rb * rows) return PYRITE_E_BUFFER;
+  rc = launch_dq_generic<float>(type_id, static_cast<const uint8_t*>(weights), rb, (int)rows, (int)cols, out,
+                                (long long)cols, static_cast<cudaStream_t>(stream));
+  return rc > 0 ? PYRITE_E_CUDA : rc;
+}
+
+int pyrite_cuda_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+int pyrite_cuda_status(int clear) {
+  int* p = device_status_word();
+  if (!p) return PYRITE_E_CUDA;
+  int v = 0;
+  if (cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return PYRITE_E_CUDA;
+  if (clear && v) {
+    const int zero = 0;
+    if (cudaMemcpy(p, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) return PYRITE_E_CUDA;
+  }
+  return v;
+}
+
+const char* pyrite_error_string(int code) {
+  switch (code) {
+    case 0: return "ok";
+    case PYRITE_E_TYPE: return "unknown or non-decodable GGML type";
+    case PYRITE_E_SHAPE: return "invalid or overflowing matrix shape";
+    case PYRITE_E_BUFFER: return "null pointer or payload length does not match rows x row_bytes";
+    case PYRITE_E_CUDA: return "CUDA runtime error";
+    default: return "unknown error";
+  }
+}
+
+}  // extern "C"

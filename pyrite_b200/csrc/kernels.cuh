@@ -1,0 +1,67 @@
+// kernels.cuh -- shared launch helpers, PTX wrappers and kernel entry points.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "ggml_blocks.cuh"
+
+namespace pyr {
+
+// One matrix-vector (or matrix x few-columns) problem on device memory.
+// Row r of the matrix starts at w + r * row_bytes; column c of x / y starts at
+// x + c * ldx / y + c * ldy.
+template <typename T> struct MatvecArgs {
+  const uint8_t* w;
+  size_t row_bytes;
+  int rows;
+  int cols;
+  const T* x;
+  long long ldx;
+  T* y;
+  long long ldy;
+};
+
+// Device-side status word: kernels set bits here instead of trapping, so a
+// timed-out wait leaves the context usable and the host can report it.
+enum DeviceStatus : int { kStatusOk = 0, kStatusWaitTimeout = 1 };
+int* device_status_word();  // this device's status word (address valid in kernels)
+
+// ---- programmatic dependent launch (PDL) ------------------------------------
+// Kernels may start (and prefetch weights) while the previous kernel in the
+// stream drains; pdl_wait() orders them after it before touching its outputs.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+               Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  return e == cudaSuccess ? 0 : -100 - (int)e;
+}
+
+// ---- generic kernels (mv_generic.cu) ----------------------------------------
+template <typename T, int NC>
+int launch_mv_generic(int type_id, const MatvecArgs<T>& a, cudaStream_t stream);
+template <typename T>
+int launch_dq_generic(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, T* out,
+                      long long ldo, cudaStream_t stream);
+
+// ---- TMA-staged fp32 matvec (mv_stream.cu) ----------------------------------
+// Returns 1 when the type / alignment has no streamed kernel (caller falls back).
+// early_prefetch: start streaming weights before the preceding kernel ends.
+int launch_mv_stream(int type_id, const MatvecArgs<float>& a, bool early_prefetch, cudaStream_t stream);
+
+}  // namespace pyr
