@@ -21,7 +21,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -38,8 +37,16 @@ SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]  # rows x cols
 SEED = 20251201
 
 
+ONLY: tuple[str, int, int] | None = None  # --only TYPE:ROWSxCOLS (profiling one matrix)
+
+
 def workload():
-    return [(name, t, rows, cols) for (rows, cols) in SHAPES for name, t in TYPES.items()]
+    wl = [(name, t, rows, cols) for (rows, cols) in SHAPES for name, t in TYPES.items()]
+    if ONLY is not None:
+        wl = [w for w in wl if (w[0], w[2], w[3]) == ONLY]
+        if not wl:
+            raise SystemExit(f"--only {ONLY} is not part of the workload")
+    return wl
 
 
 def row_bytes(t: int, cols: int) -> int:
@@ -56,10 +63,14 @@ def algo_bytes(t: int, rows: int, cols: int, ncols: int = 1) -> int:
 def build_payloads() -> dict[tuple[int, int, int], bytes]:
     from pyrite_b200.quantize import gaussian_weights, quantize
     out = {}
+    wl = workload()
     for (rows, cols) in SHAPES:
+        if not any((r, c) == (rows, cols) for _, _, r, c in wl):
+            continue
         w = gaussian_weights(rows, cols, SEED + rows * 31 + cols)
-        for name, t in TYPES.items():
-            out[(t, rows, cols)] = quantize(t, w)
+        for name, t, r, c in wl:
+            if (r, c) == (rows, cols):
+                out[(t, rows, cols)] = quantize(t, w)
     return out
 
 
@@ -70,57 +81,67 @@ def x_vectors() -> dict[int, np.ndarray]:
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples (200 ms) of this rank's GPU during the timed region."""
+    """SM clock and clock-event reasons of this rank's GPU, polled through NVML
+    (about every 2 ms) for the whole timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines: list[str] = []
+    def __init__(self, torch_device):
+        self.dev = torch_device
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self.err = None
+        self._stop = threading.Event()
+
+    def _handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.dev)
+        bus = getattr(props, "pci_bus_id", None)
+        if bus is not None:
+            busid = f"{getattr(props, 'pci_domain_id', 0):08x}:{bus:02x}:{getattr(props, 'pci_device_id', 0):02x}.0"
+            try:
+                return pynvml.nvmlDeviceGetHandleByPciBusId(busid)
+            except pynvml.NVMLError:
+                pass
+        return pynvml.nvmlDeviceGetHandleByIndex(self.dev.index or 0)
+
+    def _run(self):
+        try:
+            import pynvml
+            h = self._handle()
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            while not self._stop.is_set():
+                clk = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                try:
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except AttributeError:
+                    rs = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.samples.append((float(clk), int(rs)))
+                time.sleep(0.002)
+        except Exception as e:  # noqa: BLE001 - clocks are reported, not required
+            self.err = repr(e)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except OSError:
-            self.proc = None
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+        time.sleep(0.05)  # first sample before the timed region starts
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        self.thread.join(timeout=5)
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [c for c, _ in self.samples]
+        reasons = sorted({name for _, r in self.samples for name, bit in self.REASONS.items() if r & bit})
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+               "reasons": reasons, "samples": len(sm), "source": "nvml"}
+        if self.err:
+            out["error"] = self.err
+        return out
 
 
 # ---------------------------------------------------------------- helpers
@@ -183,9 +204,14 @@ def run_ours(args) -> None:
     step_bytes = sum(algo_bytes(t, r, c) for _, t, r, c in wl)
     stream = torch.cuda.Stream(device=dev)
 
+    WS = {c: torch.empty(K.workspace_size(0, c) + 256, dtype=torch.uint8, device=dev) for c in X}
+
     def step():
+        # one encoding of each activation, shared by the five formats of its shape
+        # (as Q/K/V or gate/up share their input in a decode step)
+        px = {c: K.prepare_x(X[c], workspace=WS[c]) for c in X}
         for _, t, r, c in wl:
-            K.matvec(t, W[(t, r, c)], X[c], r, c, out=Y[(t, r, c)], static_weights=True)
+            K.matvec_prepared(t, W[(t, r, c)], px[c], r, c, out=Y[(t, r, c)], static_weights=True)
 
     with torch.cuda.stream(stream):
         step()
@@ -206,7 +232,7 @@ def run_ours(args) -> None:
     if pg:
         pg.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(dev) as clocks:
         torch.cuda.synchronize()
         if pg:
             pg.barrier()
@@ -238,10 +264,11 @@ def run_ours(args) -> None:
             reps = 2
             g = torch.cuda.CUDAGraph()
             with torch.cuda.stream(stream):
+                px = K.prepare_x(X[c], workspace=WS[c])
                 with torch.cuda.graph(g, stream=stream):
                     for _ in range(reps):
                         for b in bufs:
-                            K.matvec(t, b, X[c], r, c, out=Y[(t, r, c)], static_weights=True)
+                            K.matvec_prepared(t, b, px, r, c, out=Y[(t, r, c)], static_weights=True)
                 g.replay()
                 torch.cuda.synchronize()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -310,7 +337,7 @@ def run_ours(args) -> None:
                                    "{4096x4096,14336x4096,4096x14336}, 15 matvecs per step",
                        "global_batch": 1, "ncols": 1, "step_bytes": step_bytes,
                        "l2": "inputs larger than L2 (492 MB of weights per step vs 126 MB L2)",
-                       "parallelism": f"replica x{world} (weak)", "launch": "CUDA graph of 15 PDL launches"},
+                       "parallelism": f"replica x{world} (weak)", "launch": "CUDA graph: 3 x-encodings + 15 matvecs, PDL"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
                          "kernel": key, "algorithmic_bytes_per_launch": dom_bytes,
@@ -319,7 +346,7 @@ def run_ours(args) -> None:
             "kernels": per_kernel,
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": args.steps * len(wl),
+            "gpu_launches": args.steps * (len(wl) + len({c for _, _, _, c in wl})),
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -428,7 +455,13 @@ def main() -> None:
     ap.add_argument("--ref-fraction", type=float, default=0.02)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--only", help="profile one matrix of the workload, e.g. Q4_K:14336x4096")
     args = ap.parse_args()
+    if args.only:
+        global ONLY
+        name, shape = args.only.split(":")
+        r, c = shape.lower().split("x")
+        ONLY = (name, int(r), int(c))
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":

@@ -63,16 +63,39 @@ int pyrite_type_geometry(int type_id, size_t *block_size, size_t *bytes_per_bloc
                                       before that kernel finishes (programmatic dependent
                                       launch); x and y are still ordered after it */
 
+/* Device workspace bytes pyrite_cuda_matvec needs for `ncols` columns of
+ * `cols` values (the activation is re-encoded there before the product). */
+size_t pyrite_cuda_workspace_size(int type_id, size_t cols, size_t ncols);
+
 /* y[c*ldy + r] = sum_k W[r, k] * x[c*ldx + k] for r < rows, c < ncols.
- * `weights` (weights_len == rows * row_bytes) , `x` and `y` are device
- * pointers; fp32 activations, fp32 accumulation.  Enqueued on `stream`
- * (a cudaStream_t, NULL = legacy default stream); returns without waiting.
- * Same validation codes as pyrite_matvec.  This is the row-range call of the
- * reference's executor (pyrite/executor.py:481-509): pass the address of the
- * first row of the range and the range's row count.  `flags`: PYRITE_F_*. */
+ * `weights` (weights_len == rows * row_bytes) , `x`, `y` and `workspace` are
+ * device pointers; fp32 activations, fp32 outputs within 1e-4 of the exact
+ * product relative to sum_k |W[r,k] x[k]|.  `workspace` (256-byte aligned, at
+ * least pyrite_cuda_workspace_size bytes) holds the activation re-encoded as
+ * two int8 digits per value with per-32-value scales; it must not be shared
+ * by calls that overlap on the GPU.  Enqueued on `stream` (a cudaStream_t,
+ * NULL = legacy default stream); returns without waiting.  Same validation
+ * codes as pyrite_matvec.  This is the row-range call of the reference's
+ * executor (pyrite/executor.py:481-509): pass the address of the first row of
+ * the range and the range's row count.  `flags`: PYRITE_F_*. */
 int pyrite_cuda_matvec(int type_id, const void *weights, size_t weights_len, const float *x,
                        long long ldx, float *y, long long ldy, size_t rows, size_t cols,
-                       size_t ncols, unsigned flags, void *stream);
+                       size_t ncols, unsigned flags, void *workspace, size_t workspace_len,
+                       void *stream);
+
+/* Re-encode x (ncols columns of `cols` values, cols a multiple of 32) into
+ * `workspace` for pyrite_cuda_matvec_prepared: several matrices that share
+ * one activation (Q/K/V, gate/up) then pay for the encoding once. */
+int pyrite_cuda_prepare_x(const float *x, long long ldx, size_t cols, size_t ncols, void *workspace,
+                          size_t workspace_len, void *stream);
+
+/* y[r] = sum_k W[r, k] x[k] for one column whose encoding pyrite_cuda_prepare_x
+ * wrote to `workspace` earlier on the same stream (x itself is still passed:
+ * formats without an encoded-x kernel read it directly).  Same results and
+ * codes as pyrite_cuda_matvec. */
+int pyrite_cuda_matvec_prepared(int type_id, const void *weights, size_t weights_len, const float *x,
+                                const void *workspace, size_t workspace_len, float *y, size_t rows,
+                                size_t cols, unsigned flags, void *stream);
 
 /* out[r*cols + c] = W[r, c] as fp32 (the correctly rounded value of the
  * reference's fp64 result).  Device pointers; enqueued on `stream`. */

@@ -21,8 +21,12 @@ SIGNATURES: dict[str, tuple] = {
     "pyrite_matvec": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _PD, _PD, _SZ, _SZ)),
     "pyrite_dequantize_rows": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _PD, _SZ, _SZ)),
     "pyrite_type_geometry": (ctypes.c_int, (ctypes.c_int, ctypes.POINTER(_SZ), ctypes.POINTER(_SZ))),
+    "pyrite_cuda_workspace_size": (_SZ, (ctypes.c_int, _SZ, _SZ)),
     "pyrite_cuda_matvec": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, ctypes.c_longlong, _VP,
-                                          ctypes.c_longlong, _SZ, _SZ, _SZ, ctypes.c_uint, _VP)),
+                                          ctypes.c_longlong, _SZ, _SZ, _SZ, ctypes.c_uint, _VP, _SZ, _VP)),
+    "pyrite_cuda_prepare_x": (ctypes.c_int, (_VP, ctypes.c_longlong, _SZ, _SZ, _VP, _SZ, _VP)),
+    "pyrite_cuda_matvec_prepared": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _VP, _SZ, _VP, _SZ, _SZ,
+                                                   ctypes.c_uint, _VP)),
     "pyrite_cuda_dequantize_rows": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _SZ, _SZ, _VP)),
     "pyrite_cuda_device_count": (ctypes.c_int, ()),
     "pyrite_cuda_status": (ctypes.c_int, (ctypes.c_int,)),

@@ -79,6 +79,9 @@ int stage_reserve(HostStage& st, size_t bytes) {
 
 size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
+// Prepared-x bytes per column, rounded so every column's planes stay aligned.
+size_t ws_col_bytes(int cols) { return align256(lane_workspace_bytes(cols)); }
+
 }  // namespace
 }  // namespace pyr
 
@@ -149,9 +152,15 @@ int pyrite_dequantize_rows(int type_id, const uint8_t* data, size_t data_len, do
   return cuda_code(cudaStreamSynchronize(st.stream));
 }
 
+size_t pyrite_cuda_workspace_size(int type_id, size_t cols, size_t ncols) {
+  (void)type_id;
+  if (cols == 0 || ncols == 0 || cols > 0x7fffffffu) return 0;
+  return ncols * ws_col_bytes((int)cols);
+}
+
 int pyrite_cuda_matvec(int type_id, const void* weights, size_t weights_len, const float* x, long long ldx,
                        float* y, long long ldy, size_t rows, size_t cols, size_t ncols, unsigned flags,
-                       void* stream) {
+                       void* workspace, size_t workspace_len, void* stream) {
   size_t rb = 0;
   int rc = geometry(type_id, rows, cols, &rb, nullptr);
   if (rc) return rc;
@@ -159,13 +168,16 @@ int pyrite_cuda_matvec(int type_id, const void* weights, size_t weights_len, con
   if (ncols > 1 && (ldx < (long long)cols || ldy < (long long)rows)) return PYRITE_E_BUFFER;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint8_t* w = static_cast<const uint8_t*>(weights);
-  if (ncols == 1) {
-    MatvecArgs<float> a{w, rb, (int)rows, (int)cols, x, ldx, y, ldy};
-    rc = launch_mv_stream(type_id, a, (flags & PYRITE_F_STATIC_WEIGHTS) != 0, s);
-    if (rc == 1) rc = launch_mv_generic<float, 1>(type_id, a, s);
+  if (ncols == 1 && lane_supported(type_id, w, rb, (int)cols)) {
+    const size_t need = ws_col_bytes((int)cols);
+    if (!workspace || workspace_len < need || ((uintptr_t)workspace & 255) != 0) return PYRITE_E_BUFFER;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    if ((rc = launch_xprep(x, ldx, (int)cols, 1, ws, (long long)need, s))) return rc > 0 ? PYRITE_E_CUDA : rc;
+    rc = launch_mv_lane(type_id, w, rb, (int)rows, (int)cols, ws, y, (flags & PYRITE_F_STATIC_WEIGHTS) != 0, s);
     return rc > 0 ? PYRITE_E_CUDA : rc;
   }
-  // Several columns: as many 8-, 4-, 2- and 1-column passes as needed.
+  // Other types, unaligned payloads and several columns: the generic kernels,
+  // as many 8-, 4-, 2- and 1-column passes as needed.
   size_t c = 0;
   while (c < ncols) {
     const size_t left = ncols - c;
@@ -177,6 +189,38 @@ int pyrite_cuda_matvec(int type_id, const void* weights, size_t weights_len, con
     if (rc) return rc > 0 ? PYRITE_E_CUDA : rc;
   }
   return 0;
+}
+
+int pyrite_cuda_prepare_x(const float* x, long long ldx, size_t cols, size_t ncols, void* workspace,
+                          size_t workspace_len, void* stream) {
+  if (!x || !workspace || cols == 0 || ncols == 0 || cols > 0x7fffffffu || cols % 32 != 0) return PYRITE_E_BUFFER;
+  if (ncols > 1 && ldx < (long long)cols) return PYRITE_E_BUFFER;
+  const size_t per = ws_col_bytes((int)cols);
+  if (workspace_len < per * ncols || ((uintptr_t)workspace & 255) != 0) return PYRITE_E_BUFFER;
+  const int rc = launch_xprep(x, ncols > 1 ? ldx : (long long)cols, (int)cols, (int)ncols,
+                              static_cast<uint8_t*>(workspace), (long long)per, static_cast<cudaStream_t>(stream));
+  return rc > 0 ? PYRITE_E_CUDA : rc;
+}
+
+int pyrite_cuda_matvec_prepared(int type_id, const void* weights, size_t weights_len, const float* x,
+                                const void* workspace, size_t workspace_len, float* y, size_t rows, size_t cols,
+                                unsigned flags, void* stream) {
+  size_t rb = 0;
+  int rc = geometry(type_id, rows, cols, &rb, nullptr);
+  if (rc) return rc;
+  if (!weights || !x || !y || weights_len != rb * rows) return PYRITE_E_BUFFER;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* w = static_cast<const uint8_t*>(weights);
+  if (lane_supported(type_id, w, rb, (int)cols)) {
+    if (!workspace || workspace_len < ws_col_bytes((int)cols) || ((uintptr_t)workspace & 255) != 0)
+      return PYRITE_E_BUFFER;
+    rc = launch_mv_lane(type_id, w, rb, (int)rows, (int)cols, static_cast<const uint8_t*>(workspace), y,
+                        (flags & PYRITE_F_STATIC_WEIGHTS) != 0, s);
+  } else {
+    MatvecArgs<float> a{w, rb, (int)rows, (int)cols, x, (long long)cols, y, (long long)rows};
+    rc = launch_mv_generic<float, 1>(type_id, a, s);
+  }
+  return rc > 0 ? PYRITE_E_CUDA : rc;
 }
 
 int pyrite_cuda_dequantize_rows(int type_id, const void* weights, size_t weights_len, float* out, size_t rows,

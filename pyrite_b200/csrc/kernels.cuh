@@ -59,9 +59,17 @@ template <typename T>
 int launch_dq_generic(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, T* out,
                       long long ldo, cudaStream_t stream);
 
-// ---- TMA-staged fp32 matvec (mv_stream.cu) ----------------------------------
-// Returns 1 when the type / alignment has no streamed kernel (caller falls back).
-// early_prefetch: start streaming weights before the preceding kernel ends.
-int launch_mv_stream(int type_id, const MatvecArgs<float>& a, bool early_prefetch, cudaStream_t stream);
+// ---- batch-1 dp4a kernels, weights staged by cp.async (mv_tile.cu) -------------
+// Bytes of prepared x one column needs (int8 digit planes, scales, sums).
+size_t lane_workspace_bytes(int cols);
+// True when the type has a lane kernel and the payload alignment suits it.
+bool lane_supported(int type_id, const uint8_t* w, size_t row_bytes, int cols);
+// x (ncols columns, stride ldx) -> prepared digits at ws + c * ws_col_bytes.
+int launch_xprep(const float* x, long long ldx, int cols, int ncols, uint8_t* ws, long long ws_col_bytes,
+                 cudaStream_t stream);
+// y[0..rows) from the prepared column at ws; static_weights enables the L2
+// prefetch of weights before the preceding kernel ends.
+int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const uint8_t* ws,
+                   float* y, bool static_weights, cudaStream_t stream);
 
 }  // namespace pyr

@@ -34,7 +34,7 @@ STATIC_WEIGHTS = 1  # PYRITE_F_STATIC_WEIGHTS
 
 def matvec(ggml_type: int, weights: torch.Tensor, x: torch.Tensor, rows: int, cols: int,
            out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None,
-           static_weights: bool = False) -> torch.Tensor:
+           static_weights: bool = False, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """``out[c, r] = sum_k W[r, k] x[c, k]`` for a device payload of ``rows`` rows.
 
     ``weights``: contiguous uint8 CUDA tensor of exactly ``rows * row_bytes``
@@ -42,6 +42,8 @@ def matvec(ggml_type: int, weights: torch.Tensor, x: torch.Tensor, rows: int, co
     stride along ``cols``.  Returns ``(rows,)`` or ``(ncols, rows)`` float32.
     ``static_weights``: the payload is not written by the kernel just before
     this call on the stream, so its weight stream may overlap that kernel.
+    ``workspace``: uint8 CUDA tensor of at least ``workspace_size(...) + 256``
+    bytes for the re-encoded activation (allocated per call when omitted).
     """
     lib = _lib.require()
     if weights.dtype != torch.uint8 or not weights.is_cuda or not weights.is_contiguous():
@@ -59,12 +61,77 @@ def matvec(ggml_type: int, weights: torch.Tensor, x: torch.Tensor, rows: int, co
         out2 = out.unsqueeze(0) if out.dim() == 1 else out
         if out2.shape != (ncols, rows) or out2.stride(1) != 1 or out2.dtype != torch.float32:
             raise ValueError("out has the wrong shape, dtype or layout")
+    if workspace is None:
+        workspace = torch.empty(int(lib.pyrite_cuda_workspace_size(ggml_type, cols, ncols)) + 256,
+                                dtype=torch.uint8, device=x.device)
+    ws_ptr = workspace.data_ptr()
+    ws_off = (-ws_ptr) % 256
     code = lib.pyrite_cuda_matvec(ggml_type, weights.data_ptr(), weights.numel(), x2.data_ptr(),
                                   x2.stride(0) if ncols > 1 else cols, out2.data_ptr(),
                                   out2.stride(0) if ncols > 1 else rows, rows, cols, ncols,
-                                  STATIC_WEIGHTS if static_weights else 0, _stream_handle(stream))
+                                  STATIC_WEIGHTS if static_weights else 0, ws_ptr + ws_off,
+                                  workspace.numel() - ws_off, _stream_handle(stream))
     _check(code, "cuda matvec")
     return out2[0] if squeeze else out2
+
+
+@dataclass
+class PreparedX:
+    """An activation re-encoded once for several matvecs (see prepare_x)."""
+
+    x: torch.Tensor          # (cols,) float32
+    workspace: torch.Tensor  # uint8, the encoding
+    offset: int              # 256-byte alignment offset inside workspace
+
+    @property
+    def ptr(self) -> int:
+        return self.workspace.data_ptr() + self.offset
+
+    @property
+    def nbytes(self) -> int:
+        return self.workspace.numel() - self.offset
+
+
+def prepare_x(x: torch.Tensor, workspace: torch.Tensor | None = None,
+              stream: torch.cuda.Stream | None = None) -> PreparedX:
+    """Encode one fp32 activation for :func:`matvec_prepared` (enqueued on the stream)."""
+    lib = _lib.require()
+    if x.dtype != torch.float32 or not x.is_cuda or x.dim() != 1 or x.stride(0) != 1:
+        raise ValueError("x must be a contiguous 1-D float32 CUDA tensor")
+    cols = x.shape[0]
+    need = int(lib.pyrite_cuda_workspace_size(0, cols, 1)) + 256
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    off = (-workspace.data_ptr()) % 256
+    code = lib.pyrite_cuda_prepare_x(x.data_ptr(), cols, cols, 1, workspace.data_ptr() + off,
+                                     workspace.numel() - off, _stream_handle(stream))
+    _check(code, "prepare_x")
+    return PreparedX(x, workspace, off)
+
+
+def matvec_prepared(ggml_type: int, weights: torch.Tensor, px: PreparedX, rows: int, cols: int,
+                    out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None,
+                    static_weights: bool = False) -> torch.Tensor:
+    """``out[r] = sum_k W[r, k] x[k]`` with x encoded earlier by :func:`prepare_x`."""
+    lib = _lib.require()
+    if weights.dtype != torch.uint8 or not weights.is_cuda or not weights.is_contiguous():
+        raise ValueError("weights must be a contiguous uint8 CUDA tensor")
+    if px.x.shape[0] != cols:
+        raise ValueError("matrix/vector shape mismatch")
+    if out is None:
+        out = torch.empty(rows, dtype=torch.float32, device=weights.device)
+    elif out.shape != (rows,) or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError("out has the wrong shape, dtype or layout")
+    code = lib.pyrite_cuda_matvec_prepared(ggml_type, weights.data_ptr(), weights.numel(), px.x.data_ptr(),
+                                           px.ptr, px.nbytes, out.data_ptr(), rows, cols,
+                                           STATIC_WEIGHTS if static_weights else 0, _stream_handle(stream))
+    _check(code, "cuda matvec")
+    return out
+
+
+def workspace_size(ggml_type: int, cols: int, ncols: int = 1) -> int:
+    """Bytes of device workspace a matvec needs (pass 256 more for alignment)."""
+    return int(_lib.require().pyrite_cuda_workspace_size(ggml_type, cols, ncols))
 
 
 def dequantize_rows(ggml_type: int, weights: torch.Tensor, rows: int, cols: int,

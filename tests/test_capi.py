@@ -80,9 +80,9 @@ def test_validation_codes_match_the_reference(lib):
     assert mv(8, 68, 1, 64, data=False) == -3
     assert lib.pyrite_dequantize_rows(8, buf.ctypes.data, 68, None, 1, 64) == -3
     dev = ctypes.c_void_p(1 << 20)           # never dereferenced: validation fails first
-    assert lib.pyrite_cuda_matvec(12, dev, 143, dev, 256, dev, 1, 1, 256, 1, 0, None) == -3
-    assert lib.pyrite_cuda_matvec(12, dev, 144, dev, 256, dev, 1, 1, 255, 1, 0, None) == -2
-    assert lib.pyrite_cuda_matvec(12, dev, 144, dev, 256, dev, 1, 1, 256, 0, 0, None) == -3
+    assert lib.pyrite_cuda_matvec(12, dev, 143, dev, 256, dev, 1, 1, 256, 1, 0, None, 0, None) == -3
+    assert lib.pyrite_cuda_matvec(12, dev, 144, dev, 256, dev, 1, 1, 255, 1, 0, None, 0, None) == -2
+    assert lib.pyrite_cuda_matvec(12, dev, 144, dev, 256, dev, 1, 1, 256, 0, 0, None, 0, None) == -3
 
 
 def test_error_strings(lib):

@@ -163,3 +163,22 @@ def test_device_row_ranges_are_independent(cuda_device):
         full = m.matvec(x)
         parts = torch.cat([m.matvec(x, a, b - a) for a, b in [(0, 333), (333, 334), (334, 1000)]])
         assert torch.equal(full, parts)
+
+
+@pytest.mark.parametrize("ggml_type", [8, 12, 13, 14, 23, 2, 30])
+def test_prepared_x_path_matches_one_shot_matvec(cuda_device, ggml_type):
+    """One encoding of x shared by several matrices gives the one-shot results."""
+    torch = _torch()
+    from pyrite_b200.kernels import cuda as K
+    cols = 4096
+    x = torch.randn(cols, device="cuda")
+    px = K.prepare_x(x)
+    for rows, seed in [(300, 1), (4096, 2), (7, 3)]:
+        payload = random_payload(ggml_type, rows, cols, seed=seed)
+        w = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
+        a = K.matvec(ggml_type, w, x, rows, cols)
+        b = K.matvec_prepared(ggml_type, w, px, rows, cols)
+        assert torch.equal(a, b)
+        want = O.matvec(ggml_type, payload, x.double().cpu().numpy(), rows, cols)
+        got = b.cpu().numpy()
+        assert rel_err(got, want, abs_dot(ggml_type, payload, x.cpu().numpy(), rows, cols)) <= FP32_MATVEC_TOL
