@@ -16,15 +16,21 @@
 //    slots; lane l of a slot always handles the same units (32-value pieces)
 //    of a row, so it loads its x digits once, into registers, for the whole
 //    kernel.  Only weights move per row.
-//  * Weights are staged through a ring of S shared-memory stages with
-//    cp.async (16 bytes per thread per copy, fully coalesced, L1 bypassed); a
-//    stage is RS*m consecutive rows, i.e. one contiguous byte range.  Lanes
-//    then decode their units from shared memory, whatever the block alignment.
-//  * Row sums: warp shuffle, then a fixed-order sum of the slot's warps in
-//    shared memory (deterministic; any row partition gives identical rows).
-//  * With static weights each CTA first asks the TMA unit to prefetch its
-//    first stages into L2 (cp.async.bulk.prefetch.L2) before waiting for the
-//    preceding kernel (programmatic dependent launch).
+//  * Weights are staged through a ring of S shared-memory stages; a stage is
+//    RS*M consecutive rows, i.e. one contiguous byte range of up to ~20 KB,
+//    fetched by ONE TMA bulk copy (cp.async.bulk) that completes on the
+//    slot's mbarrier.  (Measured on B200: bulk copies below ~4 KB cannot
+//    saturate HBM, 16 KB copies stream at ~7 TB/s.)  Lanes then decode their
+//    units from shared memory, whatever the block alignment.
+//  * K-quant headers are decoded cooperatively: the 8 lanes of a block decode
+//    one (scale, min) pair each and trade d*sc, dmin*m by shuffle.
+//  * Row sums: a butterfly that reduces M rows at once, then a fixed-order
+//    sum of the slot's warps in shared memory (deterministic; any row
+//    partition gives bit-identical rows).
+//  * With static weights the first stages are requested before waiting for
+//    the preceding kernel (programmatic dependent launch), so the weight
+//    stream overlaps its tail.  Every mbarrier wait is bounded (2 s); on
+//    time-out the kernel sets the device status word and drains its copies.
 #include "kernels.cuh"
 
 namespace pyr {
@@ -52,15 +58,41 @@ __device__ __forceinline__ uint32_t lds16(uint32_t a) {
   asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
   return v;
 }
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N> __device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait for an mbarrier phase for at most 2 s (far above any copy's latency);
+// false on time-out, so a lost copy never hangs the GPU.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer_ns() - t0 > 2000000000ull) return false;
+  return true;
 }
 __device__ __forceinline__ float half_f(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }
 __device__ __forceinline__ uint32_t w4(const uint4& v, int k) { return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w; }
@@ -152,6 +184,51 @@ __device__ __forceinline__ int dot16(const uint32_t (&c)[4], const Dig16& d) {
   return (a0 + a1) * 254 + (b0 + b1);
 }
 
+// As dot16 with the four code bytes read as unsigned (0..255).
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dot16u(const uint32_t (&c)[4], const Dig16& d) {
+  int a0 = dp4a_us(c[0], d.a.x, 0), a1 = dp4a_us(c[1], d.a.y, 0);
+  int b0 = dp4a_us(c[0], d.b.x, 0), b1 = dp4a_us(c[1], d.b.y, 0);
+  a0 = dp4a_us(c[2], d.a.z, a0);
+  a1 = dp4a_us(c[3], d.a.w, a1);
+  b0 = dp4a_us(c[2], d.b.z, b0);
+  b1 = dp4a_us(c[3], d.b.w, b1);
+  return (a0 + a1) * 254 + (b0 + b1);
+}
+
+// Row sums of M per-lane partials with one butterfly: at each level a lane
+// keeps half of its rows and trades the other half with its partner, so M
+// rows cost 5 + M - 1 shuffles instead of 5 M.  Returns the full sum of row
+// lane / (32 / M).
+template <int M>
+__device__ __forceinline__ float reduce_rows(const float (&acc)[M], int lane) {
+  float v[M];
+#pragma unroll
+  for (int i = 0; i < M; ++i) v[i] = acc[i];
+#pragma unroll
+  for (int lvl = 0; lvl < 5; ++lvl) {
+    const int stride = 16 >> lvl;
+    const int n = (M >> lvl) > 1 ? (M >> lvl) : 1;  // rows still held
+    if (n > 1) {
+      const int half = n / 2;
+      const bool up = (lane & stride) != 0;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = up ? v[i] : v[half + i];
+        const float keep = up ? v[half + i] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, stride);
+      }
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], stride);
+    }
+  }
+  return v[0];
+}
+
 // ---- per-type unit decoders ------------------------------------------------------
 // A unit is 32 values of one block.  XU: the x data of one unit, held in
 // registers for the whole kernel.  dot(blk, j, XU): the unit's contribution
@@ -170,11 +247,15 @@ template <int TY> struct UnitK45 {
     u.a = dig16(x, ca);
     u.b = dig16(x, cb);
     u.sa = __ldg(x.scale + (ca >> 5));
-    u.sb = __ldg(x.scale + (cb >> 5));
+    // Q4_K multiplies the high nibbles in place (16 * code): fold the 1/16 here
+    u.sb = __ldg(x.scale + (cb >> 5)) * (TY == Q4_K ? 0.0625f : 1.0f);
     u.ma = __ldg(x.sum16 + (ca >> 4));
     u.mb = __ldg(x.sum16 + (cb >> 4));
   }
-  __device__ static float dot(uint32_t blk, int j, const XU& u) {
+  // The 8 lanes holding the 8 units of one block (lanes 8g..8g+7) decode one
+  // (scale, min) pair each -- pair j for the lane of unit j -- and trade the
+  // products d*sc and dmin*m by shuffle.  Every lane of the warp must call.
+  __device__ static float dot(uint32_t blk, int j, const XU& u, int lane) {
     const int p = j >> 1, h = j & 1;
     const uint4 hdr = lds128(blk);
     const uint4 qv = lds128(blk + (TY == Q4_K ? 16 : 48) + 16 * j);
@@ -191,26 +272,21 @@ template <int TY> struct UnitK45 {
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         lo[k] = w4(qv, k) & 0x0F0F0F0Fu;
-        hi[k] = (w4(qv, k) >> 4) & 0x0F0F0F0Fu;
+        hi[k] = w4(qv, k) & 0xF0F0F0F0u;  // 16 * code, read unsigned
       }
     }
-    const int ia = dot16(lo, u.a), ib = dot16(hi, u.b);
-    // 6-bit (scale, min) pairs 2p and 2p+1 (native.c:52-60)
-    const int sh = 8 * ((2 * p) & 3);
-    int sca, mna, scb, mnb;
-    if (p < 2) {
-      sca = (hdr.y >> sh) & 63;        mna = (hdr.z >> sh) & 63;
-      scb = (hdr.y >> (sh + 8)) & 63;  mnb = (hdr.z >> (sh + 8)) & 63;
-    } else {
-      const uint32_t ca = (hdr.w >> sh) & 0xff, cb = (hdr.w >> (sh + 8)) & 0xff;
-      sca = (ca & 15) | (((hdr.y >> (sh + 6)) & 3) << 4);
-      mna = (ca >> 4) | (((hdr.z >> (sh + 6)) & 3) << 4);
-      scb = (cb & 15) | (((hdr.y >> (sh + 14)) & 3) << 4);
-      mnb = (cb >> 4) | (((hdr.z >> (sh + 14)) & 3) << 4);
-    }
-    const float d = half_f(hdr.x & 0xffff), dmin = half_f(hdr.x >> 16);
-    return d * ((float)sca * u.sa * (float)ia + (float)scb * u.sb * (float)ib) -
-           dmin * ((float)mna * u.ma + (float)mnb * u.mb);
+    const int ia = dot16(lo, u.a);
+    const int ib = (TY == Q4_K) ? dot16u(hi, u.b) : dot16(hi, u.b);
+    // this lane's pair j (native.c:52-60): bytes j, j+4 (j < 4) or j+4, j-4, j (j >= 4)
+    const int k8 = 8 * (j & 3);
+    const uint32_t y8 = hdr.y >> k8, z8 = hdr.z >> k8, w8 = hdr.w >> k8;
+    const uint32_t sc = j < 4 ? (y8 & 63) : ((w8 & 15) | ((y8 >> 2) & 0x30));
+    const uint32_t mn = j < 4 ? (z8 & 63) : (((w8 >> 4) & 15) | ((z8 >> 2) & 0x30));
+    const float dsc = half_f(hdr.x & 0xffff) * (float)sc, dmn = half_f(hdr.x >> 16) * (float)mn;
+    const int g = lane & ~7;
+    const float dsa = __shfl_sync(0xffffffffu, dsc, g + 2 * p), dsb = __shfl_sync(0xffffffffu, dsc, g + 2 * p + 1);
+    const float dma = __shfl_sync(0xffffffffu, dmn, g + 2 * p), dmb = __shfl_sync(0xffffffffu, dmn, g + 2 * p + 1);
+    return dsa * u.sa * (float)ia + dsb * u.sb * (float)ib - (dma * u.ma + dmb * u.mb);
   }
 };
 
@@ -224,7 +300,7 @@ struct UnitQ80 {
     u.b = dig16(x, 32 * unit + 16);
     u.s = __ldg(x.scale + unit);
   }
-  __device__ static float dot(uint32_t blk, int, const XU& u) {
+  __device__ static float dot(uint32_t blk, int, const XU& u, int) {
     uint32_t q[8];
     lds_32b(blk + 2, q);
     const float d = half_f(lds16(blk));
@@ -247,7 +323,7 @@ struct UnitQ6K {
     u.m0 = __ldg(x.sum16 + 2 * unit);
     u.m1 = __ldg(x.sum16 + 2 * unit + 1);
   }
-  __device__ static float dot(uint32_t blk, int j, const XU& u) {
+  __device__ static float dot(uint32_t blk, int j, const XU& u, int) {
     const int h = j >> 2, t = j & 3;
     uint32_t ql[8], qh[8];
     lds_32b(blk + 64 * h + 32 * (t & 1), ql);
@@ -287,7 +363,7 @@ struct UnitIQ4XS {
     }
     u.s = __ldg(x.scale + unit);
   }
-  __device__ static float dot(uint32_t blk, int j, const XU& u) {
+  __device__ static float dot(uint32_t blk, int j, const XU& u, int) {
     const uint2 hdr = lds64(blk);  // d | scales_h | scales_l[4]
     const uint2 q01 = lds64(blk + 8 + 16 * j), q23 = lds64(blk + 16 + 16 * j);
     const uint32_t qw[4] = {q01.x, q01.y, q23.x, q23.y};
@@ -319,7 +395,7 @@ template <> struct UnitOf<Q8_0> { using T = UnitQ80; };
 template <> struct UnitOf<Q6_K> { using T = UnitQ6K; };
 template <> struct UnitOf<IQ4_XS> { using T = UnitIQ4XS; };
 
-constexpr int kThreads = 256, kWarps = 8, kMaxRowsPerStage = 16;
+constexpr int kThreads = 256, kWarps = 8, kMaxRowsPerStage = 64;
 
 struct TileArgs {
   const uint8_t* w;
@@ -335,65 +411,65 @@ struct TileArgs {
 };
 
 template <int TY, int UL, int M>
-__global__ void __launch_bounds__(kThreads, 3) mv_tile_kernel(TileArgs a) {
+__global__ void __launch_bounds__(kThreads, 3) mv_tile_kernel(TileArgs a, int* status) {
   using U = typename UnitOf<TY>::T;
   constexpr int BPB = Geo<TY>::bpb;
   extern __shared__ __align__(128) uint8_t smem[];
-  float* red = reinterpret_cast<float*>(smem + (size_t)a.stages * a.stage_bytes);  // [2][kWarps][M]
+  const int S = a.stages;
+  float* red = reinterpret_cast<float*>(smem + (size_t)S * a.stage_bytes);  // [2][kWarps][M]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * kWarps * M);        // [S] full barriers
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lps = kThreads / a.rs, slot = tid / lps, ls = tid % lps;
   const int rows_per_stage = a.rs * M;
   const int nstages = (a.rows + rows_per_stage - 1) / rows_per_stage;
   const int units = a.cols / 32;
   const uint32_t ring = smem_addr(smem);
-  const size_t stage_stride = (size_t)rows_per_stage * a.row_bytes;  // bytes between stages
-  const int S = a.stages;
+  const size_t stage_stride = (size_t)rows_per_stage * a.row_bytes;
 
-  // per-thread constants: this lane's units, their offsets inside a row
+  // this lane's units (inactive ones point at block 0 and are masked out, so
+  // every lane runs the same instructions -- the K-quant decode shuffles)
   int uoff[UL], uj[UL];
-  bool uon[UL];
+  float uon[UL];
 #pragma unroll
   for (int k = 0; k < UL; ++k) {
     const int u = ls + k * lps;
-    uon[k] = u < units;
-    uoff[k] = (u / U::UPB) * BPB;
-    uj[k] = u % U::UPB;
+    uon[k] = u < units ? 1.f : 0.f;
+    uoff[k] = u < units ? (u / U::UPB) * BPB : 0;
+    uj[k] = u < units ? u % U::UPB : 0;
   }
 
   auto stage_rows = [&](int st) { return min(rows_per_stage, a.rows - st * rows_per_stage); };
-  // the CTA's k-th stage -> ring slot k % S: one contiguous byte range
-  auto issue = [&](int k) {
+  // the CTA's k-th stage -> ring slot k % S, one bulk copy of its contiguous bytes
+  auto issue = [&](int k) {  // thread 0
     const int st = blockIdx.x + k * gridDim.x;
-    if (st < nstages) {
-      const uintptr_t src = (uintptr_t)a.w + (uintptr_t)st * stage_stride;
-      const uintptr_t al = src & ~(uintptr_t)15;
-      const uint32_t len = (uint32_t)(((src - al) + (uintptr_t)stage_rows(st) * a.row_bytes + 15) & ~(uintptr_t)15);
-      const uint32_t dst = ring + (uint32_t)((k % S) * a.stage_bytes);
-      for (uint32_t c = (uint32_t)tid * 16; c < len; c += kThreads * 16)
-        cp_async16(dst + c, reinterpret_cast<const void*>(al + c));
-    }
-    cp_async_commit();  // one group per k, empty or not, keeps the wait count uniform
+    if (st >= nstages) return;
+    const uintptr_t src = (uintptr_t)a.w + (uintptr_t)st * stage_stride;
+    const uintptr_t al = src & ~(uintptr_t)15;
+    const uint32_t len = (uint32_t)(((src - al) + (uintptr_t)stage_rows(st) * a.row_bytes + 15) & ~(uintptr_t)15);
+    const uint32_t bar = smem_addr(&bars[k % S]);
+    mbar_expect_tx(bar, len);
+    bulk_g2s(ring + (uint32_t)((k % S) * a.stage_bytes), reinterpret_cast<const void*>(al), len, bar);
   };
 
   const int my = blockIdx.x < nstages ? (nstages - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  if (a.static_weights && tid < min(my, S)) {
-    // pull the first stages into L2 while the preceding kernel drains
-    const int st = blockIdx.x + tid * gridDim.x;
-    const uintptr_t src = (uintptr_t)a.w + (uintptr_t)st * stage_stride;
-    const uintptr_t s0 = (src + 15) & ~(uintptr_t)15;
-    const uintptr_t e0 = (src + (uintptr_t)stage_rows(st) * a.row_bytes) & ~(uintptr_t)15;
-    if (e0 > s0) prefetch_l2(reinterpret_cast<const void*>(s0), (uint32_t)(e0 - s0));
+  if (tid == 0) {
+    for (int k = 0; k < S; ++k) mbar_init(smem_addr(&bars[k]), 1);
+    fence_mbar_init();
   }
-  pdl_wait();  // x (prepared by the preceding kernel) and y are ordered after it
+  __syncthreads();
+  // Weights are read-only: with static weights the first stages stream while
+  // the preceding kernel drains; x and y are touched only after pdl_wait().
+  if (a.static_weights && tid == 0)
+    for (int k = 0; k < min(my, S - 1); ++k) issue(k);
+  pdl_wait();
   pdl_launch_dependents();
+  if (!a.static_weights && tid == 0)
+    for (int k = 0; k < min(my, S - 1); ++k) issue(k);
 
   typename U::XU xu[UL];  // this lane's x, for the whole kernel
   const XView xv = xview(a.ws, a.cols);
 #pragma unroll
-  for (int k = 0; k < UL; ++k)
-    if (uon[k]) U::load_x(xv, ls + k * lps, xu[k]);
-
-  for (int k = 0; k < S - 1; ++k) issue(k);
+  for (int k = 0; k < UL; ++k) U::load_x(xv, ls + k * lps < units ? ls + k * lps : 0, xu[k]);
 
   auto finalize = [&](int k) {  // fixed-order sum of the slot warps' partials
     const int st = blockIdx.x + k * gridDim.x;
@@ -406,13 +482,20 @@ __global__ void __launch_bounds__(kThreads, 3) mv_tile_kernel(TileArgs a) {
     }
   };
 
-  for (int k = 0; k < my; ++k) {
-    // stage k landed (own copies), then visible to all (barrier); the barrier
-    // also retires iteration k-1, whose slot the refill below reuses
-    if (S >= 4) cp_async_wait<2>(); else cp_async_wait<1>();
+  int k = 0;
+  for (; k < my; ++k) {
+    // stage k landed; the barrier also retires iteration k-1, whose slot the
+    // refill below reuses
+    if (!mbar_wait_bounded(smem_addr(&bars[k % S]), (uint32_t)(k / S) & 1u)) {
+      if (lane == 0) atomicOr(status, (int)kStatusWaitTimeout);
+      break;
+    }
     __syncthreads();
     if (k > 0) finalize(k - 1);
-    issue(k + S - 1);
+    if (tid == 0 && k + S - 1 < my) {
+      fence_proxy_async();  // generic reads of the slot precede its async refill
+      issue(k + S - 1);
+    }
     const int st = blockIdx.x + k * gridDim.x;
     const int nr = stage_rows(st);
     const uint32_t base = ring + (uint32_t)((k % S) * a.stage_bytes) +
@@ -421,26 +504,24 @@ __global__ void __launch_bounds__(kThreads, 3) mv_tile_kernel(TileArgs a) {
     float acc[M];
 #pragma unroll
     for (int i = 0; i < M; ++i) {
-      acc[i] = 0.f;
-      if (slot * M + i < nr) {
-        const uint32_t rowa = base + (uint32_t)i * (uint32_t)a.row_bytes;
+      // rows past the matrix end decode stale shared bytes and are dropped
+      const float on = slot * M + i < nr ? 1.f : 0.f;
+      const uint32_t rowa = base + (uint32_t)i * (uint32_t)a.row_bytes;
+      float v = 0.f;
 #pragma unroll
-        for (int kk = 0; kk < UL; ++kk)
-          if (uon[kk]) acc[i] += U::dot(rowa + (uint32_t)uoff[kk], uj[kk], xu[kk]);
-      }
+      for (int kk = 0; kk < UL; ++kk) v += uon[kk] * U::dot(rowa + (uint32_t)uoff[kk], uj[kk], xu[kk], lane);
+      acc[i] = on * v;
     }
     float* r = red + (size_t)(k & 1) * kWarps * M;
-#pragma unroll
-    for (int i = 0; i < M; ++i) {
-      float v = acc[i];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) r[warp * M + i] = v;
-    }
+    const float v = reduce_rows<M>(acc, lane);
+    if ((lane & (32 / M - 1)) == 0) r[warp * M + lane / (32 / M)] = v;
   }
   __syncthreads();
-  if (my > 0) finalize(my - 1);
-  cp_async_wait<0>();  // no copy may still target this CTA's shared memory
+  if (k == my && my > 0) finalize(my - 1);
+  if (k < my && tid == 0) {
+    // a copy timed out: wait (bounded) for every copy still in flight
+    for (int t = k; t < min(my, k + S - 1); ++t) (void)mbar_wait_bounded(smem_addr(&bars[t % S]), (uint32_t)(t / S) & 1u);
+  }
 }
 
 struct TilePlan { int rs, m, stages, stage_bytes, ul; size_t smem; };
@@ -453,13 +534,15 @@ TilePlan plan_tile(size_t row_bytes, int cols) {
   p.rs = kThreads / pow2;  // row slots: 1..8, each 32..256 lanes
   const int lps = kThreads / p.rs;
   p.ul = (units + lps - 1) / lps;
-  // rows per slot per stage (1, 2 or 4): about 8-12 KB per stage
-  const size_t per = (size_t)p.rs * row_bytes;
-  p.m = per * 4 <= 12 * 1024 ? 4 : per * 2 <= 12 * 1024 ? 2 : 1;
+  // rows per slot per stage (1, 2, 4 or 8): stages of up to ~20 KB amortise
+  // the per-stage barrier, copy issue and row reduction
+  const size_t per = (size_t)p.rs * row_bytes, cap = 20 * 1024;
+  p.m = per * 8 <= cap ? 8 : per * 4 <= cap ? 4 : per * 2 <= cap ? 2 : 1;
+  if (p.rs * p.m > kMaxRowsPerStage) p.m = kMaxRowsPerStage / p.rs;
   const size_t sb = ((size_t)p.rs * p.m * row_bytes + 16 + 32 + 127) & ~(size_t)127;
   p.stage_bytes = (int)sb;
-  p.stages = sb <= 16 * 1024 ? 4 : 3;
-  p.smem = (size_t)p.stages * sb + 2 * kWarps * p.m * sizeof(float);
+  p.stages = sb <= 12 * 1024 ? 4 : 3;
+  p.smem = (size_t)p.stages * sb + 2 * kWarps * p.m * sizeof(float) + (size_t)p.stages * 8;
   return p;
 }
 
@@ -486,14 +569,14 @@ int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
   if (per_sm < 1) per_sm = 1;
   int grid = sms[dev] * per_sm;
   if (grid > nstages) grid = nstages;
-  return launch_pdl(mv_tile_kernel<TY, UL, M>, dim3(grid), dim3(kThreads), smem, stream, ta);
+  return launch_pdl(mv_tile_kernel<TY, UL, M>, dim3(grid), dim3(kThreads), smem, stream, ta, device_status_word());
 }
 
 template <int TY>
 int launch_tile_type(const TileArgs& ta, int ul, size_t smem, cudaStream_t stream) {
 #define PYR_UM(UL_, M_) \
   if (ul == UL_ && ta.m == M_) return launch_tile_t<TY, UL_, M_>(ta, smem, stream);
-  PYR_UM(1, 1) PYR_UM(1, 2) PYR_UM(1, 4) PYR_UM(2, 1) PYR_UM(2, 2) PYR_UM(2, 4)
+  PYR_UM(1, 1) PYR_UM(1, 2) PYR_UM(1, 4) PYR_UM(1, 8) PYR_UM(2, 1) PYR_UM(2, 2) PYR_UM(2, 4)
   PYR_UM(3, 1) PYR_UM(3, 2) PYR_UM(4, 1) PYR_UM(4, 2)
 #undef PYR_UM
   return 1;
