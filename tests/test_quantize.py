@@ -1,0 +1,55 @@
+"""Host quantizers: byte identity with the reference's fixture encoders.
+
+The golden bytes were written by the reference's own encoders
+(tests/k_quant.py for Q2_K..Q6_K, scripts/build_vocab_fixture.py for Q8_0 and
+Q4_0; see tests/golden/make_golden.py) over smooth, Gaussian N(0,0.02) and
+edge-case inputs (all-zero block, constant block, a lone spike).  IQ4_NL and
+IQ4_XS have no reference encoder; their bytes are checked for validity:
+decoded by the oracle they land near the input, and the independent gguf
+dequantizer decodes them identically.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from pyrite_b200.quantize import gaussian_weights, quantize, quantize_types
+
+REF_TYPES = [2, 8, 10, 11, 12, 13, 14]
+
+
+def test_quantizer_table():
+    assert set(quantize_types()) == {2, 8, 10, 11, 12, 13, 14, 20, 23}
+
+
+@pytest.mark.parametrize("name", ["smooth", "gauss", "edge"])
+@pytest.mark.parametrize("ggml_type", REF_TYPES)
+def test_bytes_equal_the_reference_encoder(golden_encoders, ggml_type, name):
+    values = golden_encoders[f"input_{name}"]
+    want = golden_encoders[f"enc_{ggml_type}_{name}"].tobytes()
+    assert quantize(ggml_type, values) == want
+
+
+@pytest.mark.parametrize("ggml_type,gname", [(23, "IQ4_XS"), (20, "IQ4_NL")])
+def test_iq4_encoders_write_valid_blocks(ggml_type, gname):
+    w = gaussian_weights(16, 1024, seed=3)
+    payload = quantize(ggml_type, w)
+    dec = O.dequantize_rows(ggml_type, payload, 16, 1024).ravel()
+    assert np.sqrt(np.mean((dec - w) ** 2)) < 0.1 * np.std(w)
+    quants = pytest.importorskip("gguf.quants")
+    ref = quants.dequantize(np.frombuffer(payload, dtype=np.uint8), getattr(quants.GGMLQuantizationType, gname))
+    assert np.array_equal(ref.ravel().astype(np.float64), dec)
+
+
+def test_quantizer_rejects_ragged_input():
+    with pytest.raises(ValueError):
+        quantize(12, np.zeros(255))
+    with pytest.raises(ValueError):
+        quantize(8, np.zeros(33))
+
+
+def test_multithreaded_equals_single_threaded():
+    w = gaussian_weights(64, 4096, seed=9)
+    for t in (8, 12, 14, 23):
+        assert quantize(t, w, threads=1) == quantize(t, w, threads=7)
