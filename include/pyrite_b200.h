@@ -97,6 +97,26 @@ int pyrite_cuda_matvec_prepared(int type_id, const void *weights, size_t weights
                                 const void *workspace, size_t workspace_len, float *y, size_t rows,
                                 size_t cols, unsigned flags, void *stream);
 
+/* Largest `cols` pyrite_cuda_matvec_noalloc accepts (the size of its fixed
+ * scratch array: 152 KiB per GPU). */
+#define PYRITE_NOALLOC_MAX_COLS 65536
+
+/* No counterpart in the reference.  pyrite_cuda_matvec for one column, for
+ * callers that cannot allocate device memory (a host runtime that owns all GPU
+ * memory and forbids plugins to cudaMalloc, an allocation-free decode loop, an
+ * FFI host with no device allocator): the activation's encoding goes to a
+ * fixed array inside the library instead of a caller workspace, so this call
+ * allocates nothing.  Same arguments (device pointers), results and codes as
+ * pyrite_cuda_matvec with ncols = 1; cols above PYRITE_NOALLOC_MAX_COLS is
+ * rejected with PYRITE_E_SHAPE before any GPU work.  The first call on each
+ * device looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current -- make that first call before any stream capture.  The one
+ * array is shared by every call on a device and keeps the last call's bytes:
+ * calls that may overlap on the GPU (different streams without ordering)
+ * race on it; calls on one stream are ordered and safe. */
+int pyrite_cuda_matvec_noalloc(int type_id, const void *weights, size_t weights_len, const float *x,
+                               float *y, size_t rows, size_t cols, unsigned flags, void *stream);
+
 /* out[r*cols + c] = W[r, c] as fp32 (the correctly rounded value of the
  * reference's fp64 result).  Device pointers; enqueued on `stream`. */
 int pyrite_cuda_dequantize_rows(int type_id, const void *weights, size_t weights_len, float *out,

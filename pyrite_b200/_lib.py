@@ -27,6 +27,7 @@ SIGNATURES: dict[str, tuple] = {
     "pyrite_cuda_prepare_x": (ctypes.c_int, (_VP, ctypes.c_longlong, _SZ, _SZ, _VP, _SZ, _VP)),
     "pyrite_cuda_matvec_prepared": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _VP, _SZ, _VP, _SZ, _SZ,
                                                    ctypes.c_uint, _VP)),
+    "pyrite_cuda_matvec_noalloc": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _VP, _SZ, _SZ, ctypes.c_uint, _VP)),
     "pyrite_cuda_dequantize_rows": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _SZ, _SZ, _VP)),
     "pyrite_cuda_device_count": (ctypes.c_int, ()),
     "pyrite_cuda_status": (ctypes.c_int, (ctypes.c_int,)),
