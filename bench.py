@@ -319,7 +319,7 @@ def run_ours(args) -> None:
         dom = max(per_kernel, key=lambda k: k["us"])
         dom_bytes = algo_bytes(TYPES[dom["type"]], dom["rows"], dom["cols"])
         achieved = dom_bytes / (dom["us"] * 1e-6) / 1e9
-        key = f"mv_stream_kernel<{dom['type']}>@{dom['rows']}x{dom['cols']}"
+        key = f"mv_tile_kernel<{dom['type']}>@{dom['rows']}x{dom['cols']}"
         line = {
             "metric": METRIC,
             "value": round(value, 2),
