@@ -239,9 +239,9 @@ __device__ __forceinline__ float reduce_rows(const float (&acc)[M], int lane) {
 // low nibbles are values 64p+16h+i (sub-block 2p), high nibbles values
 // 64p+32+16h+i (sub-block 2p+1), p = j/2, h = j%2.  16-byte aligned blocks.
 template <int TY> struct UnitK45 {
-  static constexpr int UPB = 8;
+  static constexpr int UPB = 8, VALS = 32;
   struct XU { Dig16 a, b; float sa, sb, ma, mb; };
-  __device__ static void load_x(const XView& x, int unit, XU& u) {
+  __device__ static void load_x(const XView& x, int unit, XU& u, int) {
     const int j = unit & 7, p = j >> 1, h = j & 1;
     const int ca = 256 * (unit >> 3) + 64 * p + 16 * h, cb = ca + 32;
     u.a = dig16(x, ca);
@@ -290,57 +290,132 @@ template <int TY> struct UnitK45 {
   }
 };
 
-// Q8_0: d | int8 qs[32]  (native.c:330-336).  One unit per block; blocks are
-// 2-byte aligned.
+// Shifted digit words: x digits of a 32-value run laid out to match 9 weight
+// words read from the aligned address below a run that starts `mis` bytes
+// (0 or 2) past a 4-byte boundary.  Word k covers run bytes 4k-mis..4k-mis+3;
+// positions outside the run get digit 0, so the weight bytes there (whatever
+// they are) add nothing.  Built once per lane, so the decoder needs no
+// funnel shifts.
+__device__ __forceinline__ void shift_digits(const uint32_t (&xw)[8], int mis, uint32_t (&sw)[9]) {
+#pragma unroll
+  for (int k = 0; k < 9; ++k) {
+    const uint32_t prev = k > 0 ? xw[k - 1] : 0u, cur = k < 8 ? xw[k] : 0u;
+    sw[k] = mis ? __byte_perm(prev, cur, 0x5432) : cur;
+  }
+}
+__device__ __forceinline__ void words8(const Dig16& lo, const Dig16& hi, bool plane_b, uint32_t (&w)[8]) {
+  const uint4 a = plane_b ? lo.b : lo.a, c = plane_b ? hi.b : hi.a;
+  w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = c.x; w[5] = c.y; w[6] = c.z; w[7] = c.w;
+}
+
+// Q8_0: d | int8 qs[32]  (native.c:330-336).  One unit per block.  34-byte
+// blocks sit 0 or 2 bytes past a word boundary; with the lane's digits
+// shifted to match, the 9 aligned words feed dp4a directly.
 struct UnitQ80 {
-  static constexpr int UPB = 1;
-  struct XU { Dig16 a, b; float s; };
-  __device__ static void load_x(const XView& x, int unit, XU& u) {
-    u.a = dig16(x, 32 * unit);
-    u.b = dig16(x, 32 * unit + 16);
+  static constexpr int UPB = 1, VALS = 32;
+  struct XU { uint32_t a[9], b[9]; float s; };
+  __device__ static void load_x(const XView& x, int unit, XU& u, int wmod4) {
+    const int mis = (wmod4 + 34 * unit + 2) & 3;  // offset of qs past a word boundary
+    const Dig16 lo = dig16(x, 32 * unit), hi = dig16(x, 32 * unit + 16);
+    uint32_t w[8];
+    words8(lo, hi, false, w);
+    shift_digits(w, mis, u.a);
+    words8(lo, hi, true, w);
+    shift_digits(w, mis, u.b);
     u.s = __ldg(x.scale + unit);
   }
   __device__ static float dot(uint32_t blk, int, const XU& u, int) {
-    uint32_t q[8];
-    lds_32b(blk + 2, q);
+    const uint32_t base = (blk + 2) & ~3u;
+    int a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+#pragma unroll
+    for (int k = 0; k < 9; k += 2) {
+      const uint32_t q = lds32(base + 4 * k);
+      a0 = __dp4a((int)q, (int)u.a[k], a0);
+      b0 = __dp4a((int)q, (int)u.b[k], b0);
+      if (k + 1 < 9) {
+        const uint32_t q1 = lds32(base + 4 * k + 4);
+        a1 = __dp4a((int)q1, (int)u.a[k + 1], a1);
+        b1 = __dp4a((int)q1, (int)u.b[k + 1], b1);
+      }
+    }
     const float d = half_f(lds16(blk));
-    const uint32_t c0[4] = {q[0], q[1], q[2], q[3]}, c1[4] = {q[4], q[5], q[6], q[7]};
-    return d * u.s * (float)(dot16(c0, u.a) + dot16(c1, u.b));
+    return d * u.s * (float)((a0 + a1) * 254 + (b0 + b1));
   }
 };
 
-// Q6_K: ql[128] | qh[64] | int8 scales[16] | d  (native.c:199-225).  Unit
-// j = (h = j/4, t = j%4) is values 128h+32t+l: low 4 bits from
-// ql[64h + 32(t&1) + l] (high nibble when t >= 2), two high bits from
-// qh[32h+l] >> 2t, int8 scale 8h + 2t + l/16.  Blocks are 2-byte aligned.
+// Q6_K: ql[128] | qh[64] | int8 scales[16] | d  (native.c:199-225).  Value
+// 128h+32t+l has low 4 bits from ql[64h + 32(t&1) + l] (high nibble when
+// t >= 2), two high bits from qh[32h+l] >> 2t and int8 scale 8h + 2t + l/16.
+// A unit is 64 values, (h, tt) with t = tt and t = tt+2 ("parts" 0 and 1):
+// both parts read the same 32 ql bytes (low / high nibbles) and the same 32
+// qh bytes, so each byte is loaded once.  Blocks are 2-byte aligned; the
+// lane's digits are shifted to its block's alignment (shift_digits) and split
+// at l = 16 where the scale changes, so the 9 aligned words of each field
+// feed dp4a directly.
 struct UnitQ6K {
-  static constexpr int UPB = 8;
-  struct XU { Dig16 a, b; float s, m0, m1; };
-  __device__ static void load_x(const XView& x, int unit, XU& u) {
-    u.a = dig16(x, 32 * unit);
-    u.b = dig16(x, 32 * unit + 16);
-    u.s = __ldg(x.scale + unit);
-    u.m0 = __ldg(x.sum16 + 2 * unit);
-    u.m1 = __ldg(x.sum16 + 2 * unit + 1);
+  static constexpr int UPB = 4, VALS = 64;
+  // [part][group g: l<16 -> words 0..4, l>=16 -> words 4..8] x 5 words, per plane
+  struct XU { uint32_t a[2][10], b[2][10]; float s[2], m[2][2]; };
+  __device__ static void load_x(const XView& x, int unit, XU& u, int wmod4) {
+    const int blk = unit >> 2, j = unit & 3, h = j >> 1, tt = j & 1;
+    const int mis = (wmod4 + 210 * blk) & 3;  // 0 or 2
+    const uint32_t m4g0 = mis ? 0x0000FFFFu : 0u, m4g1 = mis ? 0xFFFF0000u : 0xFFFFFFFFu;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int c = 256 * blk + 128 * h + 64 * p + 32 * tt;
+      const Dig16 lo = dig16(x, c), hi = dig16(x, c + 16);
+      uint32_t w[8], sw[9];
+#pragma unroll
+      for (int plane = 0; plane < 2; ++plane) {
+        words8(lo, hi, plane == 1, w);
+        shift_digits(w, mis, sw);
+        uint32_t* dst = plane ? u.b[p] : u.a[p];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k] = sw[k];
+        dst[4] = sw[4] & m4g0;
+        dst[5] = sw[4] & m4g1;
+#pragma unroll
+        for (int k = 5; k < 9; ++k) dst[k + 1] = sw[k];
+      }
+      u.s[p] = __ldg(x.scale + (c >> 5));
+      u.m[p][0] = __ldg(x.sum16 + (c >> 4));
+      u.m[p][1] = __ldg(x.sum16 + (c >> 4) + 1);
+    }
   }
   __device__ static float dot(uint32_t blk, int j, const XU& u, int) {
-    const int h = j >> 2, t = j & 3;
-    uint32_t ql[8], qh[8];
-    lds_32b(blk + 64 * h + 32 * (t & 1), ql);
-    lds_32b(blk + 128 + 32 * h, qh);
-    const uint32_t sc2 = lds16(blk + 192 + 8 * h + 2 * t);
-    const float d = half_f(lds16(blk + 208));
-    const int lsh = (t >= 2) ? 4 : 0;
-    uint32_t c0[4], c1[4];
+    const int h = j >> 1, tt = j & 1;
+    const uint32_t aql = (blk + 64 * h + 32 * tt) & ~3u, aqh = (blk + 128 + 32 * h) & ~3u;
+    int acc[2][2][2] = {};  // [part][group][plane]
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      c0[k] = ((ql[k] >> lsh) & 0x0F0F0F0Fu) | (((qh[k] >> (2 * t)) & 0x03030303u) << 4);
-      c1[k] = ((ql[k + 4] >> lsh) & 0x0F0F0F0Fu) | (((qh[k + 4] >> (2 * t)) & 0x03030303u) << 4);
+    for (int k = 0; k < 9; ++k) {
+      const uint32_t ql = lds32(aql + 4 * k), s = lds32(aqh + 4 * k) >> (2 * tt);
+      const uint32_t c0 = (ql & 0x0F0F0F0Fu) | ((s & 0x03030303u) << 4);
+      const uint32_t c1 = ((ql >> 4) & 0x0F0F0F0Fu) | (s & 0x30303030u);
+      if (k <= 4) {
+        acc[0][0][0] = __dp4a((int)c0, (int)u.a[0][k], acc[0][0][0]);
+        acc[0][0][1] = __dp4a((int)c0, (int)u.b[0][k], acc[0][0][1]);
+        acc[1][0][0] = __dp4a((int)c1, (int)u.a[1][k], acc[1][0][0]);
+        acc[1][0][1] = __dp4a((int)c1, (int)u.b[1][k], acc[1][0][1]);
+      }
+      if (k >= 4) {
+        acc[0][1][0] = __dp4a((int)c0, (int)u.a[0][k + 1], acc[0][1][0]);
+        acc[0][1][1] = __dp4a((int)c0, (int)u.b[0][k + 1], acc[0][1][1]);
+        acc[1][1][0] = __dp4a((int)c1, (int)u.a[1][k + 1], acc[1][1][0]);
+        acc[1][1][1] = __dp4a((int)c1, (int)u.b[1][k + 1], acc[1][1][1]);
+      }
     }
-    // codes are 0..63, value = d * sc * (code - 32)
-    const float qa = u.s * (float)dot16(c0, u.a) - 32.0f * u.m0;
-    const float qb = u.s * (float)dot16(c1, u.b) - 32.0f * u.m1;
-    return d * ((float)(int8_t)(sc2 & 0xff) * qa + (float)(int8_t)(sc2 >> 8) * qb);
+    const uint32_t sc01 = lds16(blk + 192 + 8 * h + 2 * tt), sc23 = lds16(blk + 196 + 8 * h + 2 * tt);
+    float r = 0.f;
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        const int sc = (int)(int8_t)(((p ? sc23 : sc01) >> (8 * g)) & 0xff);
+        // codes are 0..63 and value = d * sc * (code - 32)
+        const float q = u.s[p] * (float)(acc[p][g][0] * 254 + acc[p][g][1]) - 32.0f * u.m[p][g];
+        r = fmaf((float)sc, q, r);
+      }
+    return half_f(lds16(blk + 208)) * r;
   }
 };
 
@@ -350,9 +425,9 @@ struct UnitQ6K {
 // in the order [lo0, hi0, lo1, hi1], so the x digits are interleaved the same
 // way once, when they are loaded.  8-byte aligned blocks.
 struct UnitIQ4XS {
-  static constexpr int UPB = 8;
+  static constexpr int UPB = 8, VALS = 32;
   struct XU { uint32_t a[8], b[8]; float s; };
-  __device__ static void load_x(const XView& x, int unit, XU& u) {
+  __device__ static void load_x(const XView& x, int unit, XU& u, int) {
     const Dig16 lo = dig16(x, 32 * unit), hi = dig16(x, 32 * unit + 16);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -395,7 +470,7 @@ template <> struct UnitOf<Q8_0> { using T = UnitQ80; };
 template <> struct UnitOf<Q6_K> { using T = UnitQ6K; };
 template <> struct UnitOf<IQ4_XS> { using T = UnitIQ4XS; };
 
-constexpr int kThreads = 256, kWarps = 8, kMaxRowsPerStage = 64;
+constexpr int kThreads = 256, kWarps = 8, kMaxRowsPerStage = 64, kStages = 3;
 
 struct TileArgs {
   const uint8_t* w;
@@ -403,26 +478,29 @@ struct TileArgs {
   int rows, cols;
   const uint8_t* ws;  // prepared x
   float* y;
-  int rs;           // row slots (lanes per slot = 256 / rs, a multiple of 32)
+  int rs_log2;      // row slots rs = 1 << rs_log2 (lanes per slot = 256 / rs, a multiple of 32)
   int m;            // rows per slot per stage
-  int stages;       // ring depth S
   int stage_bytes;  // shared bytes per stage (rs*m rows + alignment slack)
   int static_weights;
 };
 
+// CTAs per SM each format's register budget allows (launch bounds).
+template <int TY> constexpr int tile_min_blocks() { return TY == Q6_K ? 2 : 3; }
+
 template <int TY, int UL, int M>
-__global__ void __launch_bounds__(kThreads, 3) mv_tile_kernel(TileArgs a, int* status) {
+__global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kernel(TileArgs a, int* status) {
   using U = typename UnitOf<TY>::T;
-  constexpr int BPB = Geo<TY>::bpb;
+  constexpr int BPB = Geo<TY>::bpb, S = kStages;
   extern __shared__ __align__(128) uint8_t smem[];
-  const int S = a.stages;
   float* red = reinterpret_cast<float*>(smem + (size_t)S * a.stage_bytes);  // [2][kWarps][M]
   uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * kWarps * M);        // [S] full barriers
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int lps = kThreads / a.rs, slot = tid / lps, ls = tid % lps;
-  const int rows_per_stage = a.rs * M;
+  const int lps_log2 = 8 - a.rs_log2, lps = 1 << lps_log2;
+  const int slot = tid >> lps_log2, ls = tid & (lps - 1);
+  const int rows_per_stage = M << a.rs_log2;
   const int nstages = (a.rows + rows_per_stage - 1) / rows_per_stage;
-  const int units = a.cols / 32;
+  const int units = a.cols / U::VALS;
+  const int wmod4 = (int)((uintptr_t)a.w & 3);
   const uint32_t ring = smem_addr(smem);
   const size_t stage_stride = (size_t)rows_per_stage * a.row_bytes;
 
@@ -469,12 +547,12 @@ __global__ void __launch_bounds__(kThreads, 3) mv_tile_kernel(TileArgs a, int* s
   typename U::XU xu[UL];  // this lane's x, for the whole kernel
   const XView xv = xview(a.ws, a.cols);
 #pragma unroll
-  for (int k = 0; k < UL; ++k) U::load_x(xv, ls + k * lps < units ? ls + k * lps : 0, xu[k]);
+  for (int k = 0; k < UL; ++k) U::load_x(xv, ls + k * lps < units ? ls + k * lps : 0, xu[k], wmod4);
 
   auto finalize = [&](int k) {  // fixed-order sum of the slot warps' partials
     const int st = blockIdx.x + k * gridDim.x;
     if (tid < stage_rows(st)) {
-      const int s_slot = tid / M, i = tid % M, wps = lps / 32;
+      const int s_slot = tid / M, i = tid % M, wps = lps >> 5;
       const float* r = red + (size_t)(k & 1) * kWarps * M;
       float v = 0.f;
       for (int w = 0; w < wps; ++w) v += r[(s_slot * wps + w) * M + i];
@@ -524,25 +602,25 @@ __global__ void __launch_bounds__(kThreads, 3) mv_tile_kernel(TileArgs a, int* s
   }
 }
 
-struct TilePlan { int rs, m, stages, stage_bytes, ul; size_t smem; };
+struct TilePlan { int rs_log2, m, stage_bytes, ul; size_t smem; };
 
-TilePlan plan_tile(size_t row_bytes, int cols) {
+TilePlan plan_tile(size_t row_bytes, int cols, int vals) {
   TilePlan p{};
-  const int units = cols / 32;
+  const int units = cols / vals;
   int pow2 = 32;
   while (pow2 < units && pow2 < kThreads) pow2 *= 2;
-  p.rs = kThreads / pow2;  // row slots: 1..8, each 32..256 lanes
-  const int lps = kThreads / p.rs;
+  const int rs = kThreads / pow2;  // row slots: 1..8, each 32..256 lanes
+  p.rs_log2 = rs == 8 ? 3 : rs == 4 ? 2 : rs == 2 ? 1 : 0;
+  const int lps = kThreads / rs;
   p.ul = (units + lps - 1) / lps;
-  // rows per slot per stage (1, 2, 4 or 8): stages of up to ~20 KB amortise
-  // the per-stage barrier, copy issue and row reduction
-  const size_t per = (size_t)p.rs * row_bytes, cap = 20 * 1024;
+  // rows per slot per stage (1, 2, 4 or 8): stages of up to 20 KB amortise the
+  // per-stage barrier, copy issue and row reduction; 3 slots keep 2 in flight
+  const size_t per = (size_t)rs * row_bytes, cap = 20 * 1024;
   p.m = per * 8 <= cap ? 8 : per * 4 <= cap ? 4 : per * 2 <= cap ? 2 : 1;
-  if (p.rs * p.m > kMaxRowsPerStage) p.m = kMaxRowsPerStage / p.rs;
-  const size_t sb = ((size_t)p.rs * p.m * row_bytes + 16 + 32 + 127) & ~(size_t)127;
+  if (rs * p.m > kMaxRowsPerStage) p.m = kMaxRowsPerStage / rs;
+  const size_t sb = ((size_t)rs * p.m * row_bytes + 16 + 32 + 127) & ~(size_t)127;
   p.stage_bytes = (int)sb;
-  p.stages = sb <= 12 * 1024 ? 4 : 3;
-  p.smem = (size_t)p.stages * sb + 2 * kWarps * p.m * sizeof(float) + (size_t)p.stages * 8;
+  p.smem = (size_t)kStages * sb + 2 * kWarps * p.m * sizeof(float) + (size_t)kStages * 8;
   return p;
 }
 
@@ -554,7 +632,7 @@ int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
   static int sms[64] = {};
   static bool smem_set[64] = {};
   if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-  constexpr int kMaxSmem = 72 * 1024;
+  constexpr int kMaxSmem = 80 * 1024;
   if (!smem_set[dev]) {
     if (cudaFuncSetAttribute(mv_tile_kernel<TY, UL, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
         cudaSuccess)
@@ -562,10 +640,11 @@ int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
     smem_set[dev] = true;
   }
   if (smem > (size_t)kMaxSmem) return 1;
-  const int rows_per_stage = ta.rs * M;
+  const int rows_per_stage = M << ta.rs_log2;
   const int nstages = (ta.rows + rows_per_stage - 1) / rows_per_stage;
   int per_sm = (int)((227 * 1024) / (smem + 1024));
-  if (per_sm > 3) per_sm = 3;
+  const int minb = tile_min_blocks<TY>();
+  if (per_sm > minb) per_sm = minb;
   if (per_sm < 1) per_sm = 1;
   int grid = sms[dev] * per_sm;
   if (grid > nstages) grid = nstages;
@@ -591,7 +670,8 @@ bool lane_supported(int type_id, const uint8_t* w, size_t row_bytes, int cols) {
   const uintptr_t base = (uintptr_t)w;
   switch (type_id) {
     case Q4_K: case Q5_K: return (base & 15) == 0 && (row_bytes & 15) == 0;
-    case Q8_0: case Q6_K: return (base & 1) == 0;
+    // the shifted-digit decoders need each row to keep the word alignment
+    case Q8_0: case Q6_K: return (base & 1) == 0 && (row_bytes & 3) == 0;
     case IQ4_XS: return (base & 7) == 0;
     default: return false;
   }
@@ -608,8 +688,9 @@ int launch_xprep(const float* x, long long ldx, int cols, int ncols, uint8_t* ws
 
 int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const uint8_t* ws,
                    float* y, bool static_weights, cudaStream_t stream) {
-  const TilePlan p = plan_tile(row_bytes, cols);
-  TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs, p.m, p.stages, p.stage_bytes, static_weights ? 1 : 0};
+  const int vals = type_id == Q6_K ? UnitQ6K::VALS : 32;
+  const TilePlan p = plan_tile(row_bytes, cols, vals);
+  TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs_log2, p.m, p.stage_bytes, static_weights ? 1 : 0};
   switch (type_id) {
     case Q4_K: return launch_tile_type<Q4_K>(ta, p.ul, p.smem, stream);
     case Q5_K: return launch_tile_type<Q5_K>(ta, p.ul, p.smem, stream);
