@@ -238,55 +238,90 @@ __device__ __forceinline__ float reduce_rows(const float (&acc)[M], int lane) {
 // Q4_K / Q5_K (native.c:173-197, 410-437).  Unit j = qs bytes 16j..16j+15:
 // low nibbles are values 64p+16h+i (sub-block 2p), high nibbles values
 // 64p+32+16h+i (sub-block 2p+1), p = j/2, h = j%2.  16-byte aligned blocks.
+// 32-value digit words (8 per plane) starting at column c.
+struct Dig32 { uint32_t a[8], b[8]; };
+__device__ __forceinline__ void dig32(const XView& x, int c, Dig32& d) {
+  const Dig16 lo = dig16(x, c), hi = dig16(x, c + 16);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    d.a[k] = w4(lo.a, k); d.a[4 + k] = w4(hi.a, k);
+    d.b[k] = w4(lo.b, k); d.b[4 + k] = w4(hi.b, k);
+  }
+}
+// 254 * dot(codes, x0) + dot(codes, x1) over 32 values (exact int32); U: codes
+// read as unsigned bytes (0..255) instead of signed
+template <bool U>
+__device__ __forceinline__ int dot32(const uint32_t (&c)[8], const Dig32& d) {
+  int a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+#pragma unroll
+  for (int k = 0; k < 8; k += 2) {
+    if constexpr (U) {
+      a0 = dp4a_us(c[k], d.a[k], a0); a1 = dp4a_us(c[k + 1], d.a[k + 1], a1);
+      b0 = dp4a_us(c[k], d.b[k], b0); b1 = dp4a_us(c[k + 1], d.b[k + 1], b1);
+    } else {
+      a0 = __dp4a((int)c[k], (int)d.a[k], a0); a1 = __dp4a((int)c[k + 1], (int)d.a[k + 1], a1);
+      b0 = __dp4a((int)c[k], (int)d.b[k], b0); b1 = __dp4a((int)c[k + 1], (int)d.b[k + 1], b1);
+    }
+  }
+  return (a0 + a1) * 254 + (b0 + b1);
+}
+
+// Q4_K / Q5_K (native.c:173-197, 410-437).  A unit is 64 values: pair p of
+// sub-blocks = qs bytes 32p..32p+31, whose low nibbles are values 64p+i
+// (sub-block 2p) and high nibbles values 64p+32+i (sub-block 2p+1); Q5_K adds
+// bits 2p and 2p+1 of qh[i].  The lane decodes its own two (scale, min)
+// pairs, so the header, the scales and the epilogue are paid once per 64
+// values.  16-byte aligned blocks.
 template <int TY> struct UnitK45 {
-  static constexpr int UPB = 8, VALS = 32;
-  struct XU { Dig16 a, b; float sa, sb, ma, mb; };
+  static constexpr int UPB = 4, VALS = 64;
+  struct XU { Dig32 a, b; float sa, sb, ma, mb; };
   __device__ static void load_x(const XView& x, int unit, XU& u, int) {
-    const int j = unit & 7, p = j >> 1, h = j & 1;
-    const int ca = 256 * (unit >> 3) + 64 * p + 16 * h, cb = ca + 32;
-    u.a = dig16(x, ca);
-    u.b = dig16(x, cb);
+    const int ca = 256 * (unit >> 2) + 64 * (unit & 3), cb = ca + 32;
+    dig32(x, ca, u.a);
+    dig32(x, cb, u.b);
     u.sa = __ldg(x.scale + (ca >> 5));
     // Q4_K multiplies the high nibbles in place (16 * code): fold the 1/16 here
     u.sb = __ldg(x.scale + (cb >> 5)) * (TY == Q4_K ? 0.0625f : 1.0f);
-    u.ma = __ldg(x.sum16 + (ca >> 4));
-    u.mb = __ldg(x.sum16 + (cb >> 4));
+    u.ma = __ldg(x.sum16 + (ca >> 4)) + __ldg(x.sum16 + (ca >> 4) + 1);
+    u.mb = __ldg(x.sum16 + (cb >> 4)) + __ldg(x.sum16 + (cb >> 4) + 1);
   }
-  // The 8 lanes holding the 8 units of one block (lanes 8g..8g+7) decode one
-  // (scale, min) pair each -- pair j for the lane of unit j -- and trade the
-  // products d*sc and dmin*m by shuffle.  Every lane of the warp must call.
-  __device__ static float dot(uint32_t blk, int j, const XU& u, int lane) {
-    const int p = j >> 1, h = j & 1;
+  __device__ static float dot(uint32_t blk, int p, const XU& u, int) {
     const uint4 hdr = lds128(blk);
-    const uint4 qv = lds128(blk + (TY == Q4_K ? 16 : 48) + 16 * j);
-    uint32_t lo[4], hi[4];
+    const uint32_t qa = blk + (TY == Q4_K ? 16 : 48) + 32 * p;
+    const uint4 q0 = lds128(qa), q1 = lds128(qa + 16);
+    uint32_t lo[8], hi[8];
     if constexpr (TY == Q5_K) {
-      const uint4 hv = lds128(blk + 16 + 16 * h);
+      const uint4 h0 = lds128(blk + 16), h1 = lds128(blk + 32);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t q = w4(qv, k), qh = w4(hv, k);
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t q = k < 4 ? w4(q0, k) : w4(q1, k - 4), qh = k < 4 ? w4(h0, k) : w4(h1, k - 4);
         lo[k] = (q & 0x0F0F0F0Fu) | (((qh >> (2 * p)) & 0x01010101u) << 4);
         hi[k] = ((q >> 4) & 0x0F0F0F0Fu) | (((qh >> (2 * p + 1)) & 0x01010101u) << 4);
       }
     } else {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        lo[k] = w4(qv, k) & 0x0F0F0F0Fu;
-        hi[k] = w4(qv, k) & 0xF0F0F0F0u;  // 16 * code, read unsigned
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t q = k < 4 ? w4(q0, k) : w4(q1, k - 4);
+        lo[k] = q & 0x0F0F0F0Fu;
+        hi[k] = q & 0xF0F0F0F0u;  // 16 * code, read unsigned
       }
     }
-    const int ia = dot16(lo, u.a);
-    const int ib = (TY == Q4_K) ? dot16u(hi, u.b) : dot16(hi, u.b);
-    // this lane's pair j (native.c:52-60): bytes j, j+4 (j < 4) or j+4, j-4, j (j >= 4)
-    const int k8 = 8 * (j & 3);
-    const uint32_t y8 = hdr.y >> k8, z8 = hdr.z >> k8, w8 = hdr.w >> k8;
-    const uint32_t sc = j < 4 ? (y8 & 63) : ((w8 & 15) | ((y8 >> 2) & 0x30));
-    const uint32_t mn = j < 4 ? (z8 & 63) : (((w8 >> 4) & 15) | ((z8 >> 2) & 0x30));
-    const float dsc = half_f(hdr.x & 0xffff) * (float)sc, dmn = half_f(hdr.x >> 16) * (float)mn;
-    const int g = lane & ~7;
-    const float dsa = __shfl_sync(0xffffffffu, dsc, g + 2 * p), dsb = __shfl_sync(0xffffffffu, dsc, g + 2 * p + 1);
-    const float dma = __shfl_sync(0xffffffffu, dmn, g + 2 * p), dmb = __shfl_sync(0xffffffffu, dmn, g + 2 * p + 1);
-    return dsa * u.sa * (float)ia + dsb * u.sb * (float)ib - (dma * u.ma + dmb * u.mb);
+    const int ia = dot32<false>(lo, u.a), ib = dot32<TY == Q4_K>(hi, u.b);
+    // (scale, min) pairs 2p and 2p+1 (native.c:52-60): for j < 4 bytes j, j+4;
+    // for j >= 4 the low 4 bits in byte j+4 and the top 2 in bytes j-4 / j
+    const int k8 = 16 * (p & 1);
+    const uint32_t y = hdr.y >> k8, z = hdr.z >> k8, w = hdr.w >> k8;
+    uint32_t sca, mna, scb, mnb;
+    if (p < 2) {
+      sca = y & 63;        mna = z & 63;
+      scb = (y >> 8) & 63; mnb = (z >> 8) & 63;
+    } else {
+      sca = (w & 15) | ((y >> 2) & 0x30);        mna = ((w >> 4) & 15) | ((z >> 2) & 0x30);
+      scb = ((w >> 8) & 15) | ((y >> 10) & 0x30); mnb = ((w >> 12) & 15) | ((z >> 10) & 0x30);
+    }
+    const float d = half_f(hdr.x & 0xffff), dmin = half_f(hdr.x >> 16);
+    return d * ((float)sca * u.sa * (float)ia + (float)scb * u.sb * (float)ib) -
+           dmin * ((float)mna * u.ma + (float)mnb * u.mb);
   }
 };
 
@@ -688,7 +723,7 @@ int launch_xprep(const float* x, long long ldx, int cols, int ncols, uint8_t* ws
 
 int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const uint8_t* ws,
                    float* y, bool static_weights, cudaStream_t stream) {
-  const int vals = type_id == Q6_K ? UnitQ6K::VALS : 32;
+  const int vals = (type_id == Q6_K || type_id == Q4_K || type_id == Q5_K) ? 64 : 32;
   const TilePlan p = plan_tile(row_bytes, cols, vals);
   TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs_log2, p.m, p.stage_bytes, static_weights ? 1 : 0};
   switch (type_id) {
