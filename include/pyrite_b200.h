@@ -62,6 +62,8 @@ int pyrite_type_geometry(int type_id, size_t *block_size, size_t *bytes_per_bloc
                                       this call in the stream: its HBM stream may start
                                       before that kernel finishes (programmatic dependent
                                       launch); x and y are still ordered after it */
+#define PYRITE_F_ACCUMULATE 2u     /* pyrite_cuda_matvec_prepared: y += W x (a residual
+                                      stream) instead of y = W x */
 
 /* Device workspace bytes pyrite_cuda_matvec needs for `ncols` columns of
  * `cols` values (the activation is re-encoded there before the product). */
@@ -143,6 +145,47 @@ int pyrite_quantize(int type_id, const double *src, size_t count, uint8_t *dst, 
 
 /* Type ids pyrite_quantize accepts (ids == NULL: the count). */
 int pyrite_quantize_types(int *ids, size_t capacity);
+
+/* ---- 4. Decode-step glue (new; the reference runs these in Python fp64) -- */
+/* Device pointers; every call only enqueues on `stream`.  The token id and
+ * position are read from device memory (`tokens`, `pos`), so a whole decode
+ * step can be captured in one CUDA graph and replayed without host syncs. */
+
+/* out[0..cols) = row tokens[*pos] of a GGML `rows` x `cols` table
+ * (executor.py:647-652, the embedding lookup). */
+int pyrite_cuda_embed(int type_id, const void *table, size_t rows, size_t cols, const int *tokens,
+                      const int *pos, float *out, void *stream);
+
+/* out = x * w / sqrt(mean(x^2) + eps) (fp64 statistics, executor.py:621-624);
+ * also writes its encoding for pyrite_cuda_matvec_prepared.  out may be NULL. */
+int pyrite_cuda_rmsnorm_encode(const float *x, const float *weight, size_t n, double eps, float *out,
+                               void *workspace, size_t workspace_len, void *stream);
+
+/* qkv = [q (n_heads*128) | k (n_kv_heads*128) | v]: per-head RMSNorm of q and k
+ * (norm weights may be NULL), NEOX RoPE with the fp64 (cos, sin) table row
+ * *pos (rope_table: max_ctx x 64 double pairs), q to q_out, k and v appended
+ * to the fp32 caches at row *pos (executor.py:700-731). */
+int pyrite_cuda_qk_rope_kv(const float *qkv, const float *q_norm, const float *k_norm, int n_heads,
+                           int n_kv_heads, int head_dim, double eps, const int *pos,
+                           const void *rope_table, int max_ctx, float *q_out, float *k_cache,
+                           float *v_cache, void *stream);
+
+/* Grouped-query softmax attention of q over cache rows 0..*pos, scale
+ * 1/sqrt(head_dim) (executor.py:733-755). */
+int pyrite_cuda_attention(const float *q, const float *k_cache, const float *v_cache, const int *pos,
+                          int n_heads, int n_kv_heads, int head_dim, int max_ctx, float *out,
+                          void *stream);
+
+/* act = silu(gate) * up for gate_up = [gate (f) | up (f)] (dense.py:491-494,
+ * tensor_ops.py:509-510), also encoded for the down projection. */
+int pyrite_cuda_silu_mul_encode(const float *gate_up, size_t f, float *act, void *workspace,
+                                size_t workspace_len, void *stream);
+
+/* Greedy sampling (sampler.py:12-15): the first index of the largest logit
+ * is stored at tokens[*pos + 1] unless that position still holds the prompt
+ * (*pos + 1 < prompt_len); then *pos += 1.  scratch: >= 1184 bytes. */
+int pyrite_cuda_argmax_step(const float *logits, size_t n, void *scratch, size_t scratch_len,
+                            int *tokens, int *pos, int prompt_len, int max_ctx, void *stream);
 
 /* Static description of a return code. */
 const char *pyrite_error_string(int code);

@@ -28,6 +28,14 @@ SIGNATURES: dict[str, tuple] = {
     "pyrite_cuda_matvec_prepared": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _VP, _SZ, _VP, _SZ, _SZ,
                                                    ctypes.c_uint, _VP)),
     "pyrite_cuda_matvec_noalloc": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _VP, _SZ, _SZ, ctypes.c_uint, _VP)),
+    "pyrite_cuda_embed": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _SZ, _VP, _VP, _VP, _VP)),
+    "pyrite_cuda_rmsnorm_encode": (ctypes.c_int, (_VP, _VP, _SZ, ctypes.c_double, _VP, _VP, _SZ, _VP)),
+    "pyrite_cuda_qk_rope_kv": (ctypes.c_int, (_VP, _VP, _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_double, _VP, _VP, ctypes.c_int, _VP, _VP, _VP, _VP)),
+    "pyrite_cuda_attention": (ctypes.c_int, (_VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_int, _VP, _VP)),
+    "pyrite_cuda_silu_mul_encode": (ctypes.c_int, (_VP, _SZ, _VP, _VP, _SZ, _VP)),
+    "pyrite_cuda_argmax_step": (ctypes.c_int, (_VP, _SZ, _VP, _SZ, _VP, _VP, ctypes.c_int, ctypes.c_int, _VP)),
     "pyrite_cuda_dequantize_rows": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _SZ, _SZ, _VP)),
     "pyrite_cuda_device_count": (ctypes.c_int, ()),
     "pyrite_cuda_status": (ctypes.c_int, (ctypes.c_int,)),

@@ -215,10 +215,10 @@ int pyrite_cuda_matvec_prepared(int type_id, const void* weights, size_t weights
     if (!workspace || workspace_len < ws_col_bytes((int)cols) || ((uintptr_t)workspace & 255) != 0)
       return PYRITE_E_BUFFER;
     rc = launch_mv_lane(type_id, w, rb, (int)rows, (int)cols, static_cast<const uint8_t*>(workspace), y,
-                        (flags & PYRITE_F_STATIC_WEIGHTS) != 0, s);
+                        (flags & PYRITE_F_STATIC_WEIGHTS) != 0, s, (flags & PYRITE_F_ACCUMULATE) != 0);
   } else {
     MatvecArgs<float> a{w, rb, (int)rows, (int)cols, x, (long long)cols, y, (long long)rows};
-    rc = launch_mv_generic<float, 1>(type_id, a, s);
+    rc = launch_mv_generic<float, 1>(type_id, a, s, (flags & PYRITE_F_ACCUMULATE) != 0);
   }
   return rc > 0 ? PYRITE_E_CUDA : rc;
 }

@@ -54,7 +54,7 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
 
 // ---- generic kernels (mv_generic.cu) ----------------------------------------
 template <typename T, int NC>
-int launch_mv_generic(int type_id, const MatvecArgs<T>& a, cudaStream_t stream);
+int launch_mv_generic(int type_id, const MatvecArgs<T>& a, cudaStream_t stream, bool accumulate = false);
 template <typename T>
 int launch_dq_generic(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, T* out,
                       long long ldo, cudaStream_t stream);
@@ -70,6 +70,6 @@ int launch_xprep(const float* x, long long ldx, int cols, int ncols, uint8_t* ws
 // y[0..rows) from the prepared column at ws; static_weights enables the L2
 // prefetch of weights before the preceding kernel ends.
 int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const uint8_t* ws,
-                   float* y, bool static_weights, cudaStream_t stream);
+                   float* y, bool static_weights, cudaStream_t stream, bool accumulate = false);
 
 }  // namespace pyr

@@ -17,7 +17,7 @@ namespace pyr {
 template <int TY, typename T, int NC>
 __global__ void __launch_bounds__(256)
 mv_generic_kernel(const uint8_t* __restrict__ w, size_t row_bytes, int rows, int cols,
-                  const T* __restrict__ x, long long ldx, T* __restrict__ y, long long ldy) {
+                  const T* __restrict__ x, long long ldx, T* __restrict__ y, long long ldy, int accumulate) {
   constexpr int BS = Geo<TY>::bs, BPB = Geo<TY>::bpb;
   const int lane = threadIdx.x & 31;
   const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -55,7 +55,7 @@ mv_generic_kernel(const uint8_t* __restrict__ w, size_t row_bytes, int rows, int
       T s = acc[c];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) y[c * ldy + r] = s;
+      if (lane == 0) y[c * ldy + r] = accumulate ? y[c * ldy + r] + s : s;
     }
   }
 }
@@ -100,13 +100,13 @@ int grid_for(long long work_items, int per_block) {
 }  // namespace
 
 template <typename T, int NC>
-int launch_mv_generic(int type_id, const MatvecArgs<T>& a, cudaStream_t stream) {
+int launch_mv_generic(int type_id, const MatvecArgs<T>& a, cudaStream_t stream, bool accumulate) {
   const int grid = grid_for((long long)a.rows * 32, 256);
   switch (type_id) {
 #define PYR_CASE(TY)                                                                            \
   case TY:                                                                                      \
     return launch_pdl(mv_generic_kernel<TY, T, NC>, dim3(grid), dim3(256), 0, stream, a.w,     \
-                      a.row_bytes, a.rows, a.cols, a.x, a.ldx, a.y, a.ldy);
+                      a.row_bytes, a.rows, a.cols, a.x, a.ldx, a.y, a.ldy, accumulate ? 1 : 0);
     PYR_FOR_EACH_TYPE(PYR_CASE)
 #undef PYR_CASE
     default:
@@ -133,11 +133,11 @@ int launch_dq_generic(int type_id, const uint8_t* w, size_t row_bytes, int rows,
   }
 }
 
-template int launch_mv_generic<double, 1>(int, const MatvecArgs<double>&, cudaStream_t);
-template int launch_mv_generic<float, 1>(int, const MatvecArgs<float>&, cudaStream_t);
-template int launch_mv_generic<float, 2>(int, const MatvecArgs<float>&, cudaStream_t);
-template int launch_mv_generic<float, 4>(int, const MatvecArgs<float>&, cudaStream_t);
-template int launch_mv_generic<float, 8>(int, const MatvecArgs<float>&, cudaStream_t);
+template int launch_mv_generic<double, 1>(int, const MatvecArgs<double>&, cudaStream_t, bool);
+template int launch_mv_generic<float, 1>(int, const MatvecArgs<float>&, cudaStream_t, bool);
+template int launch_mv_generic<float, 2>(int, const MatvecArgs<float>&, cudaStream_t, bool);
+template int launch_mv_generic<float, 4>(int, const MatvecArgs<float>&, cudaStream_t, bool);
+template int launch_mv_generic<float, 8>(int, const MatvecArgs<float>&, cudaStream_t, bool);
 template int launch_dq_generic<double>(int, const uint8_t*, size_t, int, int, double*, long long, cudaStream_t);
 template int launch_dq_generic<float>(int, const uint8_t*, size_t, int, int, float*, long long, cudaStream_t);
 

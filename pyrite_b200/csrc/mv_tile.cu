@@ -517,6 +517,7 @@ struct TileArgs {
   int m;            // rows per slot per stage
   int stage_bytes;  // shared bytes per stage (rs*m rows + alignment slack)
   int static_weights;
+  int accumulate;   // y += W x (a residual stream) instead of y = W x
 };
 
 // CTAs per SM each format's register budget allows (launch bounds).
@@ -591,7 +592,8 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
       const float* r = red + (size_t)(k & 1) * kWarps * M;
       float v = 0.f;
       for (int w = 0; w < wps; ++w) v += r[(s_slot * wps + w) * M + i];
-      a.y[(size_t)st * rows_per_stage + tid] = v;
+      float* yp = a.y + (size_t)st * rows_per_stage + tid;
+      *yp = a.accumulate ? *yp + v : v;
     }
   };
 
@@ -722,10 +724,11 @@ int launch_xprep(const float* x, long long ldx, int cols, int ncols, uint8_t* ws
 }
 
 int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const uint8_t* ws,
-                   float* y, bool static_weights, cudaStream_t stream) {
+                   float* y, bool static_weights, cudaStream_t stream, bool accumulate) {
   const int vals = (type_id == Q6_K || type_id == Q4_K || type_id == Q5_K) ? 64 : 32;
   const TilePlan p = plan_tile(row_bytes, cols, vals);
-  TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs_log2, p.m, p.stage_bytes, static_weights ? 1 : 0};
+  TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs_log2, p.m, p.stage_bytes, static_weights ? 1 : 0,
+              accumulate ? 1 : 0};
   switch (type_id) {
     case Q4_K: return launch_tile_type<Q4_K>(ta, p.ul, p.smem, stream);
     case Q5_K: return launch_tile_type<Q5_K>(ta, p.ul, p.smem, stream);

@@ -1,0 +1,113 @@
+"""Seeded synthetic dense checkpoints (no public weights).
+
+``dense_tensors(spec)`` yields every tensor of a dense ``qwen3`` / ``llama``
+GGUF checkpoint -- name, GGML dims, GGML type and payload bytes -- in the
+tensor contract the reference's dense executor validates
+(``pyrite/dense.py:349-395``): matrices are seeded N(0, 0.02) float32 weights
+quantized by :mod:`pyrite_b200.quantize` (byte-identical to the reference's
+own encoders), norm weights are F32 ones.  The same bytes feed both the GGUF
+file the reference runs on and the B200 executor, so the two see identical
+weights without shipping the file.
+
+GGML dims are ``(cols, rows)``: ``attn_q.weight`` of a model with hidden size
+h and q dimension q has dims ``(h, q)`` and q rows of h values.
+"""
+from __future__ import annotations
+
+import zlib
+from collections.abc import Iterator
+from dataclasses import dataclass
+
+import numpy as np
+
+from .quantize import quantize
+
+
+@dataclass(frozen=True)
+class DenseSpec:
+    architecture: str = "qwen3"
+    hidden_size: int = 1024
+    num_hidden_layers: int = 28
+    num_attention_heads: int = 16
+    num_key_value_heads: int = 8
+    head_dim: int = 128
+    intermediate_size: int = 3072
+    vocab_size: int = 151936
+    rope_theta: float = 1_000_000.0
+    rms_norm_eps: float = 1e-6
+    qk_norm: bool = True
+    tied_embeddings: bool = True
+    weight_type: int = 8  # Q8_0
+    context_length: int = 40960
+    seed: int = 20240607
+
+    @property
+    def q_dim(self) -> int:
+        return self.num_attention_heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.num_key_value_heads * self.head_dim
+
+    @classmethod
+    def c1(cls) -> "DenseSpec":
+        """Qwen3-0.6B-shaped, all matrices Q8_0."""
+        return cls()
+
+
+def _weights(name: str, count: int, seed: int) -> np.ndarray:
+    rng = np.random.default_rng((zlib.crc32(name.encode()) ^ seed) & 0xFFFFFFFF)
+    return rng.normal(0.0, 0.02, count).astype(np.float32)
+
+
+def metadata(spec: DenseSpec) -> dict[str, object]:
+    """GGUF metadata keys the reference reads (``dense.py:113-186``)."""
+    a = spec.architecture
+    return {
+        f"{a}.embedding_length": spec.hidden_size,
+        f"{a}.block_count": spec.num_hidden_layers,
+        f"{a}.feed_forward_length": spec.intermediate_size,
+        f"{a}.attention.head_count": spec.num_attention_heads,
+        f"{a}.attention.head_count_kv": spec.num_key_value_heads,
+        f"{a}.attention.key_length": spec.head_dim,
+        f"{a}.attention.value_length": spec.head_dim,
+        f"{a}.attention.layer_norm_rms_epsilon": float(spec.rms_norm_eps),
+        f"{a}.rope.freq_base": float(spec.rope_theta),
+        f"{a}.context_length": spec.context_length,
+        f"{a}.tied_word_embeddings": bool(spec.tied_embeddings),
+        f"{a}.attention.qk_norm": bool(spec.qk_norm),
+    }
+
+
+def layer_matrices(spec: DenseSpec) -> list[tuple[str, int, int]]:
+    """(suffix, rows, cols) of each per-layer matrix."""
+    h, q, kv, f = spec.hidden_size, spec.q_dim, spec.kv_dim, spec.intermediate_size
+    return [("attn_q.weight", q, h), ("attn_k.weight", kv, h), ("attn_v.weight", kv, h),
+            ("attn_output.weight", h, q), ("ffn_gate.weight", f, h), ("ffn_up.weight", f, h),
+            ("ffn_down.weight", h, f)]
+
+
+def dense_tensors(spec: DenseSpec) -> Iterator[tuple[str, tuple[int, ...], int, bytes]]:
+    """(name, GGML dims, GGML type, payload) for every tensor of the checkpoint."""
+    ones = lambda n: np.ones(n, dtype=np.float32).tobytes()  # noqa: E731
+    t = spec.weight_type
+    yield ("token_embd.weight", (spec.hidden_size, spec.vocab_size), t,
+           quantize(t, _weights("token_embd.weight", spec.hidden_size * spec.vocab_size, spec.seed)))
+    yield ("output_norm.weight", (spec.hidden_size,), 0, ones(spec.hidden_size))
+    if not spec.tied_embeddings:
+        yield ("output.weight", (spec.hidden_size, spec.vocab_size), t,
+               quantize(t, _weights("output.weight", spec.hidden_size * spec.vocab_size, spec.seed)))
+    for layer in range(spec.num_hidden_layers):
+        p = f"blk.{layer}."
+        yield (p + "attn_norm.weight", (spec.hidden_size,), 0, ones(spec.hidden_size))
+        if spec.qk_norm:
+            yield (p + "attn_q_norm.weight", (spec.head_dim,), 0, ones(spec.head_dim))
+            yield (p + "attn_k_norm.weight", (spec.head_dim,), 0, ones(spec.head_dim))
+        yield (p + "ffn_norm.weight", (spec.hidden_size,), 0, ones(spec.hidden_size))
+        for suffix, rows, cols in layer_matrices(spec):
+            yield (p + suffix, (cols, rows), t, quantize(t, _weights(p + suffix, rows * cols, spec.seed)))
+
+
+def prompt_ids(spec: DenseSpec, n: int = 16, seed: int = 7) -> list[int]:
+    """BASELINE's prompt: ``n`` seeded uniform token ids."""
+    return [int(v) for v in np.random.default_rng(seed).integers(0, spec.vocab_size, n)]

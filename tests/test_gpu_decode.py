@@ -1,0 +1,64 @@
+"""Device-resident decode against the reference executor.
+
+tests/golden/c1_decode.json holds what the reference's DenseExecutor
+(pyrite.executor.open_executor, native kernels, fp64) produced on the seeded
+synthetic Qwen3-0.6B-shaped Q8_0 checkpoint: the greedy continuation of a
+16-token prompt and the top-16 logits of each of its 24 forward passes
+(tests/golden/make_c1_golden.py).  The B200 decoder rebuilds the same weights
+from the same seeds (pyrite_b200.synthetic) and must produce identical greedy
+token ids; its logits must match the reference's within 2e-3 absolute
+(the logits are O(1): fp32 residual stream and the encoded-activation matvec
+against the reference's fp64).  c1_small.json is a 2-layer, 4096-token
+variant that runs in seconds.
+"""
+from __future__ import annotations
+
+import json
+from dataclasses import fields
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+LOGIT_TOL = 2e-3
+
+
+def _spec(d):
+    from pyrite_b200.synthetic import DenseSpec
+    names = {f.name for f in fields(DenseSpec)}
+    return DenseSpec(**{k: v for k, v in d["spec"].items() if k in names})
+
+
+def _check_against(golden_name, cuda_device):
+    import torch
+
+    from pyrite_b200.dense import DenseDecoder
+    from pyrite_b200.kernels import cuda as K
+
+    g = json.loads((GOLDEN / golden_name).read_text())
+    dec = DenseDecoder.synthetic(_spec(g), device=cuda_device, max_ctx=512)
+    prompt, want = g["prompt"], g["generated"]
+    got = dec.generate(prompt, len(want))
+    assert K.status() == 0
+    assert got[len(prompt):] == want, f"greedy ids differ: {got[len(prompt):]} vs {want}"
+    # logits of every forward pass, step by step (the same graph replayed)
+    dec.reset(prompt)
+    worst = 0.0
+    for k, top in enumerate(g["top_logits"][: len(prompt) + len(want) - 1]):
+        dec.run_steps(1)
+        logits = dec.logits.double().cpu()
+        ids = [i for i, _ in top]
+        vals = torch.tensor([v for _, v in top], dtype=torch.float64)
+        assert int(torch.argmax(logits)) == ids[0]
+        worst = max(worst, float((logits[ids] - vals).abs().max()))
+    assert worst <= LOGIT_TOL, f"max |logit - reference| = {worst}"
+
+
+def test_small_dense_decode_matches_reference(cuda_device):
+    _check_against("c1_small.json", cuda_device)
+
+
+def test_c1_qwen3_0p6b_q8_0_decode_matches_reference(cuda_device):
+    _check_against("c1_decode.json", cuda_device)
