@@ -313,6 +313,7 @@ def run_ours(args) -> None:
                "steps": e2e_steps}
 
     cpu = cpu_baseline(payloads, xs, wl, budget_s=args.cpu_seconds) if (rank == 0 and not args.no_cpu) else None
+    decode = decode_leg(dev) if (rank == 0 and not args.no_decode) else None
 
     if rank == 0:
         peak, peak_kind = measured_peak()
@@ -346,6 +347,7 @@ def run_ours(args) -> None:
             "kernels": per_kernel,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "decode": decode,
             "gpu_launches": args.steps * (len(wl) + len({c for _, _, _, c in wl})),
             "clocks": clocks.summary(),
         }
@@ -353,6 +355,52 @@ def run_ours(args) -> None:
     if pg:
         pg.barrier()
         pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------- decode leg
+def decode_leg(dev, reps: int = 5) -> dict:
+    """configs[0] decode tok/s: the Qwen3-0.6B-shaped Q8_0 model, 16-token
+    prompt processed one token at a time (as the reference does), then 8 greedy
+    tokens; the step is one CUDA graph replayed per token.  Timed with CUDA
+    events: decode = the 8 generated tokens' steps."""
+    import torch
+
+    from pyrite_b200.dense import DenseDecoder
+    from pyrite_b200.synthetic import DenseSpec, prompt_ids
+
+    spec = DenseSpec.c1()
+    dec = DenseDecoder.synthetic(spec, device=dev, max_ctx=512)
+    prompt, new = prompt_ids(spec), 8
+    ids = dec.generate(prompt, new)  # capture + warm
+    stream = torch.cuda.current_stream(dev)
+    pre_ms, dec_ms = [], []
+    for _ in range(reps):
+        dec.reset(prompt)
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(stream)
+        dec.run_steps(len(prompt) - 1)   # prompt positions 0..14
+        e1.record(stream)
+        dec.run_steps(new)               # position 15 (first new token) .. 22
+        e2.record(stream)
+        torch.cuda.synchronize(dev)
+        pre_ms.append(e0.elapsed_time(e1))
+        dec_ms.append(e1.elapsed_time(e2))
+    weights = sum(t.numel() for ly in dec.layers for t in (ly.qkv, ly.o, ly.gate_up, ly.down)) + dec.lm_head.numel()
+    ms_tok = statistics.median(dec_ms) / new
+    golden = ROOT / "tests" / "golden" / "c1_decode.json"
+    ref = json.loads(golden.read_text()) if golden.is_file() else {}
+    return {"config": "configs[0]: Qwen3-0.6B-shaped, 28 layers, Q8_0, vocab 151936 tied, 16-token prompt, "
+                      "8 greedy tokens, KV 512, batch 1",
+            "decode_tok_s": round(1000.0 / ms_tok, 1), "ms_per_token": round(ms_tok, 4),
+            "prefill_tok_s": round((len(prompt) - 1) * 1000.0 / statistics.median(pre_ms), 1),
+            "weight_bytes_per_token": weights,
+            "weight_GBps": round(weights / (ms_tok * 1e-3) / 1e9, 1),
+            "generated": ids[len(prompt):],
+            "greedy_matches_reference": ids[len(prompt):] == ref.get("generated"),
+            "reference_tok_s_cpu": round(ref["reference_tokens_per_second"], 3) if ref else None,
+            "reference_note": "reference DenseExecutor (fp64 Python + native C kernels), 24 forward passes "
+                              "incl. the sequential prompt, timed when the golden file was made "
+                              "(tests/golden/make_c1_golden.py, 8-core build host)"}
 
 
 # ---------------------------------------------------------------- CPU baseline
@@ -391,9 +439,11 @@ def cpu_baseline(payloads, xs, wl, budget_s: float = 12.0, threads: int = 1) -> 
         total_b += n * rb + (n + c) * 4
         total_t += dt
         rows_done[f"{t}:{r}x{c}"] = n
+    full = all(rows_done[f"{t}:{r}x{c}"] == r for _, t, r, c in wl)
+    what = ("all rows of all 15 matrices (the whole step)" if full else
+            f"the first rows of each of the 15 matrices ({sum(rows_done.values())} rows, ~{per:.1f} s each)")
     return {"value": round(total_b / total_t / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": kind,
-            "sample": f"first rows of each of the 15 matrices (~{per:.1f} s each, {sum(rows_done.values())} rows "
-                      f"in total), single thread, fp64 as the reference computes", "seconds": round(total_t, 2)}
+            "sample": f"{what}, single thread, fp64 as the reference computes", "seconds": round(total_t, 2)}
 
 
 def run_reference(args) -> None:
@@ -455,6 +505,7 @@ def main() -> None:
     ap.add_argument("--ref-fraction", type=float, default=0.02)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the configs[0] decode tok/s leg")
     ap.add_argument("--only", help="profile one matrix of the workload, e.g. Q4_K:14336x4096")
     args = ap.parse_args()
     if args.only:
