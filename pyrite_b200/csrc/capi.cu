@@ -153,9 +153,13 @@ int pyrite_dequantize_rows(int type_id, const uint8_t* data, size_t data_len, do
 }
 
 size_t pyrite_cuda_workspace_size(int type_id, size_t cols, size_t ncols) {
-  (void)type_id;
-  if (cols == 0 || ncols == 0 || cols > 0x7fffffffu) return 0;
-  return ncols * ws_col_bytes((int)cols);
+  if (cols == 0 || ncols == 0 || cols > 0x7fffffffu || ncols > 0x7fffffffu) return 0;
+  size_t need = ncols * ws_col_bytes((int)cols);
+  if (tc_supported(type_id, (int)cols, (int)ncols)) {
+    const size_t tc = align256(tc_workspace_bytes((int)cols, (int)ncols));
+    if (tc > need) need = tc;
+  }
+  return need;
 }
 
 int pyrite_cuda_matvec(int type_id, const void* weights, size_t weights_len, const float* x, long long ldx,
@@ -174,6 +178,14 @@ int pyrite_cuda_matvec(int type_id, const void* weights, size_t weights_len, con
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     if ((rc = launch_xprep(x, ldx, (int)cols, 1, ws, (long long)need, s))) return rc > 0 ? PYRITE_E_CUDA : rc;
     rc = launch_mv_lane(type_id, w, rb, (int)rows, (int)cols, ws, y, (flags & PYRITE_F_STATIC_WEIGHTS) != 0, s);
+    return rc > 0 ? PYRITE_E_CUDA : rc;
+  }
+  // Several columns of the main formats: the tensor-core product.
+  if (ncols > 1 && ncols <= 0x7fffffffu && tc_supported(type_id, (int)cols, (int)ncols)) {
+    const size_t need = tc_workspace_bytes((int)cols, (int)ncols);
+    if (!workspace || workspace_len < need || ((uintptr_t)workspace & 255) != 0) return PYRITE_E_BUFFER;
+    rc = launch_mm_tc(type_id, w, rb, (int)rows, (int)cols, x, ldx, y, ldy, (int)ncols,
+                      static_cast<uint8_t*>(workspace), false, s);
     return rc > 0 ? PYRITE_E_CUDA : rc;
   }
   // Other types, unaligned payloads and several columns: the generic kernels,

@@ -72,4 +72,14 @@ int launch_xprep(const float* x, long long ldx, int cols, int ncols, uint8_t* ws
 int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const uint8_t* ws,
                    float* y, bool static_weights, cudaStream_t stream, bool accumulate = false);
 
+// ---- several columns on the tensor cores (mm_tc.cu) ---------------------------
+// True when (type, cols, ncols) runs on the tcgen05 path.
+bool tc_supported(int type_id, int cols, int ncols);
+// Workspace bytes for the split activation planes of ncols columns.
+size_t tc_workspace_bytes(int cols, int ncols);
+// Y[c*ldy + r] (+)= sum_k W[r,k] X[c*ldx + k]; ws 256-byte aligned, at least
+// tc_workspace_bytes(cols, ncols).
+int launch_mm_tc(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const float* x, long long ldx,
+                 float* y, long long ldy, int ncols, uint8_t* ws, bool accumulate, cudaStream_t stream);
+
 }  // namespace pyr
