@@ -65,6 +65,46 @@ int pyrite_type_geometry(int type_id, size_t *block_size, size_t *bytes_per_bloc
 #define PYRITE_F_ACCUMULATE 2u     /* pyrite_cuda_matvec_prepared: y += W x (a residual
                                       stream) instead of y = W x */
 
+/* Operations a batch-1 matvec can run on its whole output y (rows values) in
+ * the last of its CTAs to finish (pyrite_cuda_matvec_prepared_post): the glue
+ * between the projections of a decode step without a launch of its own. */
+#define PYRITE_POST_NONE 0
+#define PYRITE_POST_RMSNORM_ENCODE 1  /* out = y * weight / sqrt(mean(y^2) + eps), fp64
+                                         statistics (executor.py:621-624), encoded */
+#define PYRITE_POST_SILU_MUL_ENCODE 2 /* y = [gate | up]: out = silu(gate) * up
+                                         (dense.py:491-494), encoded */
+#define PYRITE_POST_ARGMAX 3          /* tokens[*pos + 1] = first index of max(y) unless
+                                         that position still holds the prompt; *pos += 1
+                                         (sampler.py:12-15) */
+typedef struct pyrite_post_op {
+  int op;               /* PYRITE_POST_* */
+  int prompt_len;       /* ARGMAX */
+  int max_ctx;          /* ARGMAX: length of `tokens` */
+  double eps;           /* RMSNORM_ENCODE */
+  const float *weight;  /* RMSNORM_ENCODE: rows values */
+  float *out;           /* RMSNORM_ENCODE (may be NULL) / SILU_MUL_ENCODE (rows/2 values) */
+  void *workspace;      /* RMSNORM / SILU: the encoding of out (256-byte aligned, at least
+                           pyrite_cuda_workspace_size(0, n, 1) bytes for n = len(out)) */
+  size_t workspace_len;
+  unsigned *ticket;     /* device counter, zero before the call and left zero by it; one per
+                           call that can overlap another on the GPU */
+  void *scratch;        /* ARGMAX: pyrite_cuda_post_scratch_size() bytes */
+  size_t scratch_len;
+  int *tokens;          /* ARGMAX */
+  int *pos;             /* ARGMAX */
+} pyrite_post_op;
+
+/* Scratch bytes PYRITE_POST_ARGMAX needs on the current device. */
+size_t pyrite_cuda_post_scratch_size(void);
+
+/* pyrite_cuda_matvec_prepared followed by `post` on y, in one launch where the
+ * batch-1 kernel takes the format (else the product and a separate kernel).
+ * Same validation codes; a malformed `post` is PYRITE_E_BUFFER. */
+int pyrite_cuda_matvec_prepared_post(int type_id, const void *weights, size_t weights_len,
+                                     const float *x, const void *workspace, size_t workspace_len,
+                                     float *y, size_t rows, size_t cols, unsigned flags,
+                                     const pyrite_post_op *post, void *stream);
+
 /* Device workspace bytes pyrite_cuda_matvec needs for `ncols` columns of
  * `cols` values (the activation is re-encoded there before the product). */
 size_t pyrite_cuda_workspace_size(int type_id, size_t cols, size_t ncols);
@@ -175,6 +215,14 @@ int pyrite_cuda_qk_rope_kv(const float *qkv, const float *q_norm, const float *k
 int pyrite_cuda_attention(const float *q, const float *k_cache, const float *v_cache, const int *pos,
                           int n_heads, int n_kv_heads, int head_dim, int max_ctx, float *out,
                           void *stream);
+
+/* pyrite_cuda_qk_rope_kv and pyrite_cuda_attention in one launch (one CTA per
+ * q head), the output also encoded into `workspace` for the output
+ * projection (pyrite_cuda_matvec_prepared).  Same results. */
+int pyrite_cuda_attention_step(const float *qkv, const float *q_norm, const float *k_norm, int n_heads,
+                               int n_kv_heads, int head_dim, double eps, const int *pos,
+                               const void *rope_table, int max_ctx, float *k_cache, float *v_cache,
+                               float *out, void *workspace, size_t workspace_len, void *stream);
 
 /* act = silu(gate) * up for gate_up = [gate (f) | up (f)] (dense.py:491-494,
  * tensor_ops.py:509-510), also encoded for the down projection. */

@@ -15,6 +15,18 @@ _SZ = ctypes.c_size_t
 _VP = ctypes.c_void_p
 _PD = ctypes.POINTER(ctypes.c_double)
 
+class PostOp(ctypes.Structure):
+    """``pyrite_post_op`` (include/pyrite_b200.h)."""
+
+    _fields_ = [("op", ctypes.c_int), ("prompt_len", ctypes.c_int), ("max_ctx", ctypes.c_int),
+                ("eps", ctypes.c_double), ("weight", ctypes.c_void_p), ("out", ctypes.c_void_p),
+                ("workspace", ctypes.c_void_p), ("workspace_len", ctypes.c_size_t), ("ticket", ctypes.c_void_p),
+                ("scratch", ctypes.c_void_p), ("scratch_len", ctypes.c_size_t), ("tokens", ctypes.c_void_p),
+                ("pos", ctypes.c_void_p)]
+
+
+POST_NONE, POST_RMSNORM_ENCODE, POST_SILU_MUL_ENCODE, POST_ARGMAX = 0, 1, 2, 3
+
 # name -> (restype, argtypes); exactly the symbols of include/pyrite_b200.h
 SIGNATURES: dict[str, tuple] = {
     "pyrite_native_types": (ctypes.c_int, (ctypes.POINTER(ctypes.c_int), _SZ)),
@@ -27,6 +39,9 @@ SIGNATURES: dict[str, tuple] = {
     "pyrite_cuda_prepare_x": (ctypes.c_int, (_VP, ctypes.c_longlong, _SZ, _SZ, _VP, _SZ, _VP)),
     "pyrite_cuda_matvec_prepared": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _VP, _SZ, _VP, _SZ, _SZ,
                                                    ctypes.c_uint, _VP)),
+    "pyrite_cuda_post_scratch_size": (_SZ, ()),
+    "pyrite_cuda_matvec_prepared_post": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _VP, _SZ, _VP, _SZ, _SZ,
+                                                        ctypes.c_uint, ctypes.POINTER(PostOp), _VP)),
     "pyrite_cuda_matvec_noalloc": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _VP, _SZ, _SZ, ctypes.c_uint, _VP)),
     "pyrite_cuda_embed": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _SZ, _VP, _VP, _VP, _VP)),
     "pyrite_cuda_rmsnorm_encode": (ctypes.c_int, (_VP, _VP, _SZ, ctypes.c_double, _VP, _VP, _SZ, _VP)),
@@ -34,6 +49,9 @@ SIGNATURES: dict[str, tuple] = {
                                               ctypes.c_double, _VP, _VP, ctypes.c_int, _VP, _VP, _VP, _VP)),
     "pyrite_cuda_attention": (ctypes.c_int, (_VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                              ctypes.c_int, _VP, _VP)),
+    "pyrite_cuda_attention_step": (ctypes.c_int, (_VP, _VP, _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                  ctypes.c_double, _VP, _VP, ctypes.c_int, _VP, _VP, _VP, _VP, _SZ,
+                                                  _VP)),
     "pyrite_cuda_silu_mul_encode": (ctypes.c_int, (_VP, _SZ, _VP, _VP, _SZ, _VP)),
     "pyrite_cuda_argmax_step": (ctypes.c_int, (_VP, _SZ, _VP, _SZ, _VP, _VP, ctypes.c_int, ctypes.c_int, _VP)),
     "pyrite_cuda_dequantize_rows": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _SZ, _SZ, _VP)),

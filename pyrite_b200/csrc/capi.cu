@@ -235,6 +235,84 @@ int pyrite_cuda_matvec_prepared(int type_id, const void* weights, size_t weights
   return rc > 0 ? PYRITE_E_CUDA : rc;
 }
 
+size_t pyrite_cuda_post_scratch_size(void) {
+  const int g = lane_max_grid();
+  return g > 0 ? (size_t)g * 8 : 0;
+}
+
+int pyrite_cuda_matvec_prepared_post(int type_id, const void* weights, size_t weights_len, const float* x,
+                                     const void* workspace, size_t workspace_len, float* y, size_t rows, size_t cols,
+                                     unsigned flags, const pyrite_post_op* post, void* stream) {
+  if (!post || post->op == PYRITE_POST_NONE)
+    return pyrite_cuda_matvec_prepared(type_id, weights, weights_len, x, workspace, workspace_len, y, rows, cols, flags,
+                                       stream);
+  size_t rb = 0;
+  int rc = geometry(type_id, rows, cols, &rb, nullptr);
+  if (rc) return rc;
+  if (!weights || !x || !y || weights_len != rb * rows) return PYRITE_E_BUFFER;
+  // the post op's own arguments
+  PostArgs pa;
+  pa.ticket = post->ticket;
+  if (!pa.ticket) return PYRITE_E_BUFFER;
+  size_t n_out = 0;
+  switch (post->op) {
+    case PYRITE_POST_RMSNORM_ENCODE:
+      n_out = rows;
+      if (!post->weight || rows % 32) return PYRITE_E_BUFFER;
+      pa.op = kPostRmsnormEncode;
+      break;
+    case PYRITE_POST_SILU_MUL_ENCODE:
+      n_out = rows / 2;
+      if (!post->out || rows % 64) return PYRITE_E_BUFFER;
+      pa.op = kPostSiluMulEncode;
+      break;
+    case PYRITE_POST_ARGMAX:
+      if (!post->scratch || post->scratch_len < pyrite_cuda_post_scratch_size() || !post->tokens || !post->pos)
+        return PYRITE_E_BUFFER;
+      pa.op = kPostArgmax;
+      break;
+    default:
+      return PYRITE_E_BUFFER;
+  }
+  if (n_out && (!post->workspace || post->workspace_len < ws_col_bytes((int)n_out) ||
+                ((uintptr_t)post->workspace & 255) != 0))
+    return PYRITE_E_BUFFER;
+  pa.w = post->weight;
+  pa.eps = post->eps;
+  pa.out = post->out;
+  pa.ws = static_cast<uint8_t*>(post->workspace);
+  const int g = lane_max_grid();
+  pa.pv = static_cast<float*>(post->scratch);
+  pa.pi = post->scratch ? reinterpret_cast<int*>(pa.pv + (g > 0 ? g : 0)) : nullptr;
+  pa.tokens = post->tokens;
+  pa.pos = post->pos;
+  pa.prompt_len = post->prompt_len;
+  pa.max_ctx = post->max_ctx;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* w = static_cast<const uint8_t*>(weights);
+  if (lane_supported(type_id, w, rb, (int)cols)) {
+    if (!workspace || workspace_len < ws_col_bytes((int)cols) || ((uintptr_t)workspace & 255) != 0)
+      return PYRITE_E_BUFFER;
+    rc = launch_mv_lane(type_id, w, rb, (int)rows, (int)cols, static_cast<const uint8_t*>(workspace), y,
+                        (flags & PYRITE_F_STATIC_WEIGHTS) != 0, s, (flags & PYRITE_F_ACCUMULATE) != 0, &pa);
+    return rc > 0 ? PYRITE_E_CUDA : rc;
+  }
+  // formats without the batch-1 kernel: the product, then the operation as its own kernel
+  rc = pyrite_cuda_matvec_prepared(type_id, weights, weights_len, x, workspace, workspace_len, y, rows, cols, flags,
+                                   stream);
+  if (rc) return rc;
+  switch (post->op) {
+    case PYRITE_POST_RMSNORM_ENCODE:
+      return pyrite_cuda_rmsnorm_encode(y, post->weight, rows, post->eps, post->out, post->workspace,
+                                        post->workspace_len, stream);
+    case PYRITE_POST_SILU_MUL_ENCODE:
+      return pyrite_cuda_silu_mul_encode(y, rows / 2, post->out, post->workspace, post->workspace_len, stream);
+    default:
+      return pyrite_cuda_argmax_step(y, rows, post->scratch, post->scratch_len, post->tokens, post->pos,
+                                     post->prompt_len, post->max_ctx, stream);
+  }
+}
+
 int pyrite_cuda_dequantize_rows(int type_id, const void* weights, size_t weights_len, float* out, size_t rows,
                                 size_t cols, void* stream) {
   size_t rb = 0;

@@ -59,6 +59,22 @@ template <typename T>
 int launch_dq_generic(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, T* out,
                       long long ldo, cudaStream_t stream);
 
+// ---- post ops: run by the last CTA of a batch-1 matvec on its whole output -----
+enum PostOp : int { kPostNone = 0, kPostRmsnormEncode = 1, kPostSiluMulEncode = 2, kPostArgmax = 3 };
+struct PostArgs {
+  int op = kPostNone;
+  const float* w = nullptr;  // RMSNorm weight (n values)
+  double eps = 0.0;
+  float* out = nullptr;      // fp32 result (normed vector / activation)
+  uint8_t* ws = nullptr;     // its encoding for the next matvec
+  unsigned* ticket = nullptr;  // device counter, zero between launches
+  float* pv = nullptr;       // argmax: per-CTA partial values / indices
+  int* pi = nullptr;
+  int* tokens = nullptr;     // argmax: the chosen id goes to tokens[*pos + 1]
+  int* pos = nullptr;
+  int prompt_len = 0, max_ctx = 0;
+};
+
 // ---- batch-1 dp4a kernels, weights staged by cp.async (mv_tile.cu) -------------
 // Bytes of prepared x one column needs (int8 digit planes, scales, sums).
 size_t lane_workspace_bytes(int cols);
@@ -70,7 +86,10 @@ int launch_xprep(const float* x, long long ldx, int cols, int ncols, uint8_t* ws
 // y[0..rows) from the prepared column at ws; static_weights enables the L2
 // prefetch of weights before the preceding kernel ends.
 int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const uint8_t* ws,
-                   float* y, bool static_weights, cudaStream_t stream, bool accumulate = false);
+                   float* y, bool static_weights, cudaStream_t stream, bool accumulate = false,
+                   const PostArgs* post = nullptr);
+// Largest grid launch_mv_lane uses (argmax partial slots needed).
+int lane_max_grid();
 
 // ---- several columns on the tensor cores (mm_tc.cu) ---------------------------
 // True when (type, cols, ncols) runs on the tcgen05 path.

@@ -17,7 +17,7 @@
 //    of a row, so it loads its x digits once, into registers, for the whole
 //    kernel.  Only weights move per row.
 //  * Weights are staged through a ring of S shared-memory stages; a stage is
-//    RS*M consecutive rows, i.e. one contiguous byte range of up to ~20 KB,
+//    RS*M consecutive rows, i.e. one contiguous byte range of up to ~32 KB,
 //    fetched by ONE TMA bulk copy (cp.async.bulk) that completes on the
 //    slot's mbarrier.  (Measured on B200: bulk copies below ~4 KB cannot
 //    saturate HBM, 16 KB copies stream at ~7 TB/s.)  Lanes then decode their
@@ -32,6 +32,7 @@
 //    stream overlaps its tail.  Every mbarrier wait is bounded (2 s); on
 //    time-out the kernel sets the device status word and drains its copies.
 #include "kernels.cuh"
+#include "post_ops.cuh"
 #include "ptx.cuh"
 
 namespace pyr {
@@ -452,6 +453,65 @@ template <> struct UnitOf<IQ4_XS> { using T = UnitIQ4XS; };
 
 constexpr int kThreads = 256, kWarps = 8, kMaxRowsPerStage = 64, kStages = 3;
 
+// The last CTA to finish (a ticket counter, no waiting) runs one operation on
+// the complete output vector y (n = rows values).  Every CTA publishes its
+// rows before taking its ticket (__threadfence), so the last one sees them
+// all; it reads them through L2 and leaves the counter at zero.
+__device__ void run_post(const PostArgs& p, const float* y, int n, float best_v, int best_i) {
+  __shared__ double shm[32];
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  __shared__ int last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (p.op == kPostArgmax) {  // this CTA's best row -> its partial slot
+    warp_best(best_v, best_i);
+    if (lane == 0) {
+      bv[warp] = best_v;
+      bi[warp] = best_i;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      best_v = lane < kWarps ? bv[lane] : -FLT_MAX;
+      best_i = lane < kWarps ? bi[lane] : 0x7fffffff;
+      warp_best(best_v, best_i);
+      if (lane == 0) {
+        p.pv[blockIdx.x] = best_v;
+        p.pi[blockIdx.x] = best_i;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    last = atomicAdd(p.ticket, 1u) == gridDim.x - 1 ? 1 : 0;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (p.op == kPostRmsnormEncode) {
+    block_rmsnorm_encode(y, p.w, n, p.eps, p.out, p.ws, shm);
+  } else if (p.op == kPostSiluMulEncode) {
+    warps_silu_mul_encode(y, n / 2, p.out, p.ws, warp, kWarps);
+  } else if (p.op == kPostArgmax) {
+    float v = -FLT_MAX;
+    int idx = 0x7fffffff;
+    for (int c = tid; c < (int)gridDim.x; c += kThreads) better(v, idx, __ldcg(p.pv + c), __ldcg(p.pi + c));
+    warp_best(v, idx);
+    if (lane == 0) {
+      bv[warp] = v;
+      bi[warp] = idx;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      for (int w = 1; w < kWarps; ++w) better(v, idx, bv[w], bi[w]);
+      const int q = *p.pos;
+      if (q + 1 < p.max_ctx && q + 1 >= p.prompt_len) p.tokens[q + 1] = idx;
+      *p.pos = q + 1;
+    }
+  }
+  if (tid == 0) *p.ticket = 0u;
+}
+
 struct TileArgs {
   const uint8_t* w;
   size_t row_bytes;
@@ -463,6 +523,7 @@ struct TileArgs {
   int stage_bytes;  // shared bytes per stage (rs*m rows + alignment slack)
   int static_weights;
   int accumulate;   // y += W x (a residual stream) instead of y = W x
+  PostArgs post;    // operation run on the whole y by the last CTA to finish
 };
 
 // CTAs per SM each format's register budget allows (launch bounds).
@@ -530,6 +591,8 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
 #pragma unroll
   for (int k = 0; k < UL; ++k) U::load_x(xv, ls + k * lps < units ? ls + k * lps : 0, xu[k], wmod4);
 
+  float best_v = -FLT_MAX;  // POST_ARGMAX: this thread's best finalized row
+  int best_i = 0x7fffffff;
   auto finalize = [&](int k) {  // fixed-order sum of the slot warps' partials
     const int st = blockIdx.x + k * gridDim.x;
     if (tid < stage_rows(st)) {
@@ -538,7 +601,9 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
       float v = 0.f;
       for (int w = 0; w < wps; ++w) v += r[(s_slot * wps + w) * M + i];
       float* yp = a.y + (size_t)st * rows_per_stage + tid;
-      *yp = a.accumulate ? *yp + v : v;
+      v = a.accumulate ? *yp + v : v;
+      *yp = v;
+      better(best_v, best_i, v, st * rows_per_stage + tid);
     }
   };
 
@@ -582,11 +647,12 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
     // a copy timed out: wait (bounded) for every copy still in flight
     for (int t = k; t < min(my, k + S - 1); ++t) (void)mbar_wait_bounded(smem_addr(&bars[t % S]), (uint32_t)(t / S) & 1u);
   }
+  if (a.post.op != kPostNone) run_post(a.post, a.y, a.rows, best_v, best_i);
 }
 
 struct TilePlan { int rs_log2, m, stage_bytes, ul; size_t smem; };
 
-TilePlan plan_tile(size_t row_bytes, int cols, int vals) {
+TilePlan plan_tile(size_t row_bytes, int rows, int cols, int vals) {
   TilePlan p{};
   const int units = cols / vals;
   int pow2 = 32;
@@ -595,10 +661,14 @@ TilePlan plan_tile(size_t row_bytes, int cols, int vals) {
   p.rs_log2 = rs == 8 ? 3 : rs == 4 ? 2 : rs == 2 ? 1 : 0;
   const int lps = kThreads / rs;
   p.ul = (units + lps - 1) / lps;
-  // rows per slot per stage (1, 2, 4 or 8): stages of up to 20 KB amortise the
-  // per-stage barrier, copy issue and row reduction; 3 slots keep 2 in flight
-  const size_t per = (size_t)rs * row_bytes, cap = 20 * 1024;
-  p.m = per * 8 <= cap ? 8 : per * 4 <= cap ? 4 : per * 2 <= cap ? 2 : 1;
+  // rows per slot per stage (1, 2, 4 or 8): stages of up to 32 KB amortise the
+  // per-stage barrier, copy issue and row reduction; 3 slots keep 2 in flight.
+  // A matrix too small for a full wave of such stages keeps 20 KB stages, so
+  // more CTAs share it.
+  const size_t per = (size_t)rs * row_bytes;
+  auto m_for = [&](size_t cap) { return per * 8 <= cap ? 8 : per * 4 <= cap ? 4 : per * 2 <= cap ? 2 : 1; };
+  p.m = m_for(32 * 1024);
+  if ((long long)rows / ((long long)rs * p.m) < 148LL * 3) p.m = m_for(20 * 1024);
   if (rs * p.m > kMaxRowsPerStage) p.m = kMaxRowsPerStage / rs;
   const size_t sb = ((size_t)rs * p.m * row_bytes + 16 + 32 + 127) & ~(size_t)127;
   p.stage_bytes = (int)sb;
@@ -614,7 +684,7 @@ int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
   static int sms[64] = {};
   static bool smem_set[64] = {};
   if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-  constexpr int kMaxSmem = 80 * 1024;
+  constexpr int kMaxSmem = 110 * 1024;
   if (!smem_set[dev]) {
     if (cudaFuncSetAttribute(mv_tile_kernel<TY, UL, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
         cudaSuccess)
@@ -645,6 +715,13 @@ int launch_tile_type(const TileArgs& ta, int ul, size_t smem, cudaStream_t strea
 
 }  // namespace
 
+int lane_max_grid() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return -1;
+  return sms * 3;  // tile_min_blocks <= 3 CTAs per SM
+}
+
 size_t lane_workspace_bytes(int cols) { return (size_t)cols * 2 + (size_t)(cols / 32) * 4 + (size_t)(cols / 16) * 4; }
 
 bool lane_supported(int type_id, const uint8_t* w, size_t row_bytes, int cols) {
@@ -669,11 +746,11 @@ int launch_xprep(const float* x, long long ldx, int cols, int ncols, uint8_t* ws
 }
 
 int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const uint8_t* ws,
-                   float* y, bool static_weights, cudaStream_t stream, bool accumulate) {
+                   float* y, bool static_weights, cudaStream_t stream, bool accumulate, const PostArgs* post) {
   const int vals = (type_id == Q6_K || type_id == Q4_K || type_id == Q5_K) ? 64 : 32;
-  const TilePlan p = plan_tile(row_bytes, cols, vals);
+  const TilePlan p = plan_tile(row_bytes, rows, cols, vals);
   TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs_log2, p.m, p.stage_bytes, static_weights ? 1 : 0,
-              accumulate ? 1 : 0};
+              accumulate ? 1 : 0, post ? *post : PostArgs{}};
   switch (type_id) {
     case Q4_K: return launch_tile_type<Q4_K>(ta, p.ul, p.smem, stream);
     case Q5_K: return launch_tile_type<Q5_K>(ta, p.ul, p.smem, stream);

@@ -19,9 +19,17 @@ B200 layout choices:
     sequence of launches, captured once in a CUDA graph and replayed for the
     whole prompt (processed one token at a time, as the reference does) and
     every generated token, with no host synchronisation in between.
+  * Fused step (default): q/k norm, RoPE, KV append, attention and the
+    encoding of its output run as one kernel, and the greedy argmax runs in
+    the last CTA of the LM-head matvec (a post op).  The RMSNorms and SwiGLU
+    stay kernels of their own: run as post ops in the last CTA of their
+    producer they cost more than a launch (measured on B200: 256 threads
+    serialise work a 1024-thread kernel does at once).  ``fused=False`` keeps
+    one launch per operation (same results).
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 
@@ -57,10 +65,11 @@ class DenseDecoder:
     """One sequence, batch 1, weights in HBM; greedy decoding."""
 
     def __init__(self, spec: DenseSpec, tensors: dict[str, tuple[tuple[int, ...], int, bytes]],
-                 device: torch.device | str = "cuda", max_ctx: int = 512):
+                 device: torch.device | str = "cuda", max_ctx: int = 512, fused: bool = True):
         self.spec = spec
         self.dev = torch.device(device)
         self.max_ctx = max_ctx
+        self.fused = fused
         self.lib = _lib.require()
         h, f = spec.hidden_size, spec.intermediate_size
         self.wtype = spec.weight_type
@@ -110,7 +119,10 @@ class DenseDecoder:
         self.vcache = torch.zeros_like(self.kcache)
         self.tokens = torch.zeros(max_ctx, dtype=torch.int32, device=d)
         self.pos = torch.zeros(1, dtype=torch.int32, device=d)
-        self.argmax_scratch = torch.zeros(2048, dtype=torch.uint8, device=d)
+        self.argmax_scratch = torch.zeros(max(2048, int(self.lib.pyrite_cuda_post_scratch_size())),
+                                          dtype=torch.uint8, device=d)
+        # one ticket counter per fused call site (three per layer + the LM head)
+        self.tickets = torch.zeros(3 * spec.num_hidden_layers + 1, dtype=torch.int32, device=d)
         ws = lambda n: _aligned(int(self.lib.pyrite_cuda_workspace_size(0, n, 1)), d)  # noqa: E731
         self.ws_h, self.ws_h_off = ws(h)
         self.ws_q, self.ws_q_off = ws(spec.q_dim)
@@ -125,9 +137,9 @@ class DenseDecoder:
         self.prompt_len = 0
 
     @classmethod
-    def synthetic(cls, spec: DenseSpec, device="cuda", max_ctx: int = 512) -> "DenseDecoder":
+    def synthetic(cls, spec: DenseSpec, device="cuda", max_ctx: int = 512, fused: bool = True) -> "DenseDecoder":
         tensors = {name: (dims, t, payload) for name, dims, t, payload in dense_tensors(spec)}
-        return cls(spec, tensors, device=device, max_ctx=max_ctx)
+        return cls(spec, tensors, device=device, max_ctx=max_ctx, fused=fused)
 
     # ------------------------------------------------------------------ one step
     def _ws(self, which: str) -> tuple[int, int]:
@@ -142,7 +154,67 @@ class DenseDecoder:
                                                     y.data_ptr(), rows, cols, flags | STATIC_WEIGHTS, stream)
         _check(code, "matvec")
 
+    def _post(self, op: int, ticket: int, *, weight=None, out=None, ws: str | None = None) -> _lib.PostOp:
+        p = _lib.PostOp()
+        p.op = op
+        p.eps = float(self.spec.rms_norm_eps)
+        p.weight = weight.data_ptr() if weight is not None else None
+        p.out = out.data_ptr() if out is not None else None
+        if ws is not None:
+            p.workspace, p.workspace_len = self._ws(ws)
+        p.ticket = self.tickets.data_ptr() + 4 * ticket
+        p.scratch = self.argmax_scratch.data_ptr()
+        p.scratch_len = self.argmax_scratch.numel()
+        p.tokens = self.tokens.data_ptr()
+        p.pos = self.pos.data_ptr()
+        p.prompt_len = self.prompt_len
+        p.max_ctx = self.max_ctx
+        return p
+
+    def _matvec_post(self, w: torch.Tensor, x: torch.Tensor, ws: str, y: torch.Tensor, rows: int, cols: int,
+                     flags: int, post: _lib.PostOp, stream: int) -> None:
+        wptr, wlen = self._ws(ws)
+        code = self.lib.pyrite_cuda_matvec_prepared_post(self.wtype, w.data_ptr(), w.numel(), x.data_ptr(), wptr, wlen,
+                                                         y.data_ptr(), rows, cols, flags | STATIC_WEIGHTS,
+                                                         ctypes.byref(post), stream)
+        _check(code, "matvec+post")
+
+    def _step_fused(self, stream: int) -> None:
+        s, L = self.spec, self.lib
+        h, f = s.hidden_size, s.intermediate_size
+        eps = float(s.rms_norm_eps)
+        nl = len(self.layers)
+        _check(L.pyrite_cuda_embed(self.wtype, self.embd.data_ptr(), s.vocab_size, h, self.tokens.data_ptr(),
+                                   self.pos.data_ptr(), self.hidden.data_ptr(), stream), "embed")
+        wh, whl = self._ws("h")
+        _check(L.pyrite_cuda_rmsnorm_encode(self.hidden.data_ptr(), self.layers[0].attn_norm.data_ptr(), h, eps,
+                                            self.normed.data_ptr(), wh, whl, stream), "rmsnorm")
+        for li, ly in enumerate(self.layers):
+            self._matvec(ly.qkv, self.normed, "h", self.qkv, s.q_dim + 2 * s.kv_dim, h, 0, stream)
+            wq, wql = self._ws("q")
+            _check(L.pyrite_cuda_attention_step(
+                self.qkv.data_ptr(), ly.q_norm.data_ptr() if ly.q_norm is not None else None,
+                ly.k_norm.data_ptr() if ly.k_norm is not None else None, s.num_attention_heads,
+                s.num_key_value_heads, s.head_dim, eps, self.pos.data_ptr(), self.rope.data_ptr(), self.max_ctx,
+                self.kcache[li].data_ptr(), self.vcache[li].data_ptr(), self.attn.data_ptr(), wq, wql, stream),
+                "attention_step")
+            self._matvec(ly.o, self.attn, "q", self.hidden, h, s.q_dim, ACCUMULATE, stream)
+            _check(L.pyrite_cuda_rmsnorm_encode(self.hidden.data_ptr(), ly.ffn_norm.data_ptr(), h, eps,
+                                                self.normed.data_ptr(), wh, whl, stream), "rmsnorm")
+            self._matvec(ly.gate_up, self.normed, "h", self.gu, 2 * f, h, 0, stream)
+            wf, wfl = self._ws("f")
+            _check(L.pyrite_cuda_silu_mul_encode(self.gu.data_ptr(), f, self.act.data_ptr(), wf, wfl, stream), "silu")
+            nxt = self.layers[li + 1].attn_norm if li + 1 < nl else self.out_norm
+            self._matvec(ly.down, self.act, "f", self.hidden, h, f, ACCUMULATE, stream)
+            _check(L.pyrite_cuda_rmsnorm_encode(self.hidden.data_ptr(), nxt.data_ptr(), h, eps,
+                                                self.normed.data_ptr(), wh, whl, stream), "rmsnorm")
+        self._matvec_post(self.lm_head, self.normed, "h", self.logits, s.vocab_size, h, 0,
+                          self._post(_lib.POST_ARGMAX, 3 * nl), stream)
+
     def _step(self, stream: int) -> None:
+        if self.fused:
+            self._step_fused(stream)
+            return
         s, L = self.spec, self.lib
         h, f = s.hidden_size, s.intermediate_size
         eps = float(s.rms_norm_eps)

@@ -112,3 +112,22 @@ def test_without_a_device_the_shim_refuses_instead_of_computing_on_cpu():
     out = np.zeros(1)
     buf = np.zeros(34, dtype=np.uint8)
     assert lib.pyrite_matvec(8, buf.ctypes.data, 34, x.ctypes.data_as(pd), out.ctypes.data_as(pd), 1, 32) == -4
+
+
+def test_post_op_struct_layout_matches_the_header(tmp_path):
+    """The ctypes mirror of pyrite_post_op has the C compiler's layout."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    fields = [f for f, _ in _lib.PostOp._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"pyrite_b200.h\"\nint main(void){\n"
+                   + "".join(f'printf("%zu\\n", offsetof(pyrite_post_op, {f}));\n' for f in fields)
+                   + 'printf("%zu\\n", sizeof(pyrite_post_op));\nreturn 0;}\n')
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    want = [getattr(_lib.PostOp, f).offset for f in fields] + [ctypes.sizeof(_lib.PostOp)]
+    assert got == want

@@ -31,14 +31,14 @@ def _spec(d):
     return DenseSpec(**{k: v for k, v in d["spec"].items() if k in names})
 
 
-def _check_against(golden_name, cuda_device):
+def _check_against(golden_name, cuda_device, fused=True):
     import torch
 
     from pyrite_b200.dense import DenseDecoder
     from pyrite_b200.kernels import cuda as K
 
     g = json.loads((GOLDEN / golden_name).read_text())
-    dec = DenseDecoder.synthetic(_spec(g), device=cuda_device, max_ctx=512)
+    dec = DenseDecoder.synthetic(_spec(g), device=cuda_device, max_ctx=512, fused=fused)
     prompt, want = g["prompt"], g["generated"]
     got = dec.generate(prompt, len(want))
     assert K.status() == 0
@@ -56,8 +56,28 @@ def _check_against(golden_name, cuda_device):
     assert worst <= LOGIT_TOL, f"max |logit - reference| = {worst}"
 
 
-def test_small_dense_decode_matches_reference(cuda_device):
-    _check_against("c1_small.json", cuda_device)
+@pytest.mark.parametrize("fused", [True, False])
+def test_small_dense_decode_matches_reference(cuda_device, fused):
+    _check_against("c1_small.json", cuda_device, fused)
+
+
+def test_fused_step_equals_unfused_step(cuda_device):
+    """Post ops and the fused attention step give the one-kernel-per-op logits."""
+    import torch
+
+    from pyrite_b200.dense import DenseDecoder
+    g = json.loads((GOLDEN / "c1_small.json").read_text())
+    a = DenseDecoder.synthetic(_spec(g), device=cuda_device, max_ctx=64, fused=True)
+    b = DenseDecoder.synthetic(_spec(g), device=cuda_device, max_ctx=64, fused=False)
+    prompt = g["prompt"]
+    a.reset(prompt)
+    b.reset(prompt)
+    for _ in range(len(prompt) + 4):
+        a.run_steps(1)
+        b.run_steps(1)
+        torch.cuda.synchronize()
+        assert torch.allclose(a.logits, b.logits, rtol=1e-5, atol=1e-5)
+        assert torch.equal(a.tokens, b.tokens) and torch.equal(a.pos, b.pos)
 
 
 def test_c1_qwen3_0p6b_q8_0_decode_matches_reference(cuda_device):

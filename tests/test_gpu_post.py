@@ -1,0 +1,147 @@
+"""Post ops: a batch-1 matvec that also runs the next decode-step operation on
+its whole output in its last CTA (pyrite_cuda_matvec_prepared_post), through
+the C ABI (B200).
+
+Each fused call must give exactly what the product followed by the operation's
+own kernel gives: RMSNorm + encoding (executor.py:621-624), SiLU * up +
+encoding (dense.py:491-494) and the greedy argmax (sampler.py:12-15), for a
+format with the batch-1 kernel (fused in the last CTA) and one without (the
+product, then the operation's kernel).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from tests.payloads import random_payload
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(ggml_type, rows, cols, seed):
+    import torch
+
+    from pyrite_b200.kernels import cuda as K
+    payload = random_payload(ggml_type, rows, cols, seed=seed)
+    w = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
+    x = torch.randn(cols, device="cuda", generator=torch.Generator("cuda").manual_seed(seed))
+    px = K.prepare_x(x)
+    return w, x, px
+
+
+def _ws(n):
+    import torch
+
+    from pyrite_b200 import _lib
+    lib = _lib.require()
+    need = int(lib.pyrite_cuda_workspace_size(0, n, 1))
+    buf = torch.zeros(need + 256, dtype=torch.uint8, device="cuda")
+    off = (-buf.data_ptr()) % 256
+    return buf, buf.data_ptr() + off, buf.numel() - off, off, need
+
+
+def _run_post(ggml_type, w, x, px, y, rows, cols, post):
+    import torch
+
+    from pyrite_b200 import _lib
+    from pyrite_b200.kernels import cuda as K
+    lib = _lib.require()
+    code = lib.pyrite_cuda_matvec_prepared_post(ggml_type, w.data_ptr(), w.numel(), x.data_ptr(), px.ptr, px.nbytes,
+                                                y.data_ptr(), rows, cols, 0, ctypes.byref(post),
+                                                torch.cuda.current_stream().cuda_stream)
+    assert code == 0, code
+    torch.cuda.synchronize()
+    assert K.status() == 0
+
+
+@pytest.mark.parametrize("ggml_type", [8, 12, 14, 23, 2])
+def test_post_rmsnorm_encode_equals_separate_kernel(cuda_device, ggml_type):
+    import torch
+
+    from pyrite_b200 import _lib
+    from pyrite_b200.kernels import cuda as K
+    lib = _lib.require()
+    rows, cols = 1024, 2048
+    w, x, px = _setup(ggml_type, rows, cols, 3)
+    norm_w = torch.rand(rows, device="cuda") + 0.5
+    y = torch.empty(rows, device="cuda")
+    out = torch.empty(rows, device="cuda")
+    ticket = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ws_buf, ws_ptr, ws_len, ws_off, need = _ws(rows)
+    p = _lib.PostOp()
+    p.op, p.eps, p.weight, p.out = _lib.POST_RMSNORM_ENCODE, 1e-6, norm_w.data_ptr(), out.data_ptr()
+    p.workspace, p.workspace_len, p.ticket = ws_ptr, ws_len, ticket.data_ptr()
+    for _ in range(3):  # repeated: the ticket must come back to zero
+        _run_post(ggml_type, w, x, px, y, rows, cols, p)
+        assert int(ticket.item()) == 0
+    want_y = K.matvec_prepared(ggml_type, w, px, rows, cols)
+    assert torch.equal(y, want_y)
+    ref_out = torch.empty(rows, device="cuda")
+    ref_buf, ref_ptr, ref_len, ref_off, _ = _ws(rows)
+    assert lib.pyrite_cuda_rmsnorm_encode(y.data_ptr(), norm_w.data_ptr(), rows, 1e-6, ref_out.data_ptr(), ref_ptr,
+                                          ref_len, torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    # same fp64 statistics up to the summation order of a 256- vs 1024-thread CTA
+    assert torch.allclose(out, ref_out, rtol=1e-6, atol=0)
+    a = ws_buf[ws_off:ws_off + need].cpu().numpy()
+    b = ref_buf[ref_off:ref_off + need].cpu().numpy()
+    assert np.mean(a == b) > 0.999
+
+
+@pytest.mark.parametrize("ggml_type", [8, 12, 2])
+def test_post_silu_mul_encode_equals_separate_kernel(cuda_device, ggml_type):
+    import torch
+
+    from pyrite_b200 import _lib
+    lib = _lib.require()
+    f, cols = 1536, 1024
+    rows = 2 * f
+    w, x, px = _setup(ggml_type, rows, cols, 5)
+    y = torch.empty(rows, device="cuda")
+    act = torch.empty(f, device="cuda")
+    ticket = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ws_buf, ws_ptr, ws_len, ws_off, need = _ws(f)
+    p = _lib.PostOp()
+    p.op, p.out, p.workspace, p.workspace_len, p.ticket = (_lib.POST_SILU_MUL_ENCODE, act.data_ptr(), ws_ptr, ws_len,
+                                                           ticket.data_ptr())
+    _run_post(ggml_type, w, x, px, y, rows, cols, p)
+    assert int(ticket.item()) == 0
+    ref = torch.empty(f, device="cuda")
+    ref_buf, ref_ptr, ref_len, ref_off, _ = _ws(f)
+    assert lib.pyrite_cuda_silu_mul_encode(y.data_ptr(), f, ref.data_ptr(), ref_ptr, ref_len,
+                                           torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(act, ref)
+    assert torch.equal(ws_buf[ws_off:ws_off + need], ref_buf[ref_off:ref_off + need])
+
+
+@pytest.mark.parametrize("ggml_type", [8, 12, 2])
+@pytest.mark.parametrize("rows", [151936, 4096, 7])
+def test_post_argmax_picks_first_maximum(cuda_device, ggml_type, rows):
+    import torch
+
+    from pyrite_b200 import _lib
+    lib = _lib.require()
+    cols = 1024
+    w, x, px = _setup(ggml_type, rows, cols, rows)
+    y = torch.empty(rows, device="cuda")
+    ticket = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scratch = torch.zeros(int(lib.pyrite_cuda_post_scratch_size()), dtype=torch.uint8, device="cuda")
+    tokens = torch.zeros(16, dtype=torch.int32, device="cuda")
+    pos = torch.tensor([5], dtype=torch.int32, device="cuda")
+    p = _lib.PostOp()
+    p.op, p.ticket, p.scratch, p.scratch_len = _lib.POST_ARGMAX, ticket.data_ptr(), scratch.data_ptr(), scratch.numel()
+    p.tokens, p.pos, p.prompt_len, p.max_ctx = tokens.data_ptr(), pos.data_ptr(), 3, 16
+    _run_post(ggml_type, w, x, px, y, rows, cols, p)
+    ys = y.cpu().numpy()
+    want = int(np.flatnonzero(ys == ys.max())[0])
+    assert int(tokens[6].item()) == want
+    assert int(pos.item()) == 6
+    assert int(ticket.item()) == 0
+    # a prompt position is never overwritten
+    pos.fill_(0)
+    tokens.fill_(-1)
+    _run_post(ggml_type, w, x, px, y, rows, cols, p)
+    assert int(tokens[1].item()) == -1 and int(pos.item()) == 1
