@@ -235,6 +235,41 @@ int pyrite_cuda_silu_mul_encode(const float *gate_up, size_t f, float *act, void
 int pyrite_cuda_argmax_step(const float *logits, size_t n, void *scratch, size_t scratch_len,
                             int *tokens, int *pos, int prompt_len, int max_ctx, void *stream);
 
+/* ---- routed experts (Qwen3-MoE feed-forward, executor.py:672-683, 757-793) ---- */
+
+/* Router softmax (fp64) over n_experts logits, the top_k experts ordered by
+ * (-probability, expert id), their weights renormalised to sum 1 when
+ * norm_topk_prob, then multiplied by scale: expert_ids[top_k] and
+ * expert_weights[top_k] (fp32) in device memory.  n_experts <= 4096,
+ * top_k <= 32. */
+int pyrite_cuda_moe_route(const float *router_logits, int n_experts, int top_k, int norm_topk_prob,
+                          double scale, int *expert_ids, float *expert_weights, void *stream);
+
+/* The batch-1 product over n_sel routed slices of a stacked expert tensor in
+ * one launch: `stacked` holds n_experts matrices of rows x cols back to back
+ * (expert e at e * rows * row_bytes, qwen3_moe.py:364-398); expert_ids
+ * (device, n_sel entries, written by an earlier kernel on the stream) pick the
+ * slices; slice j multiplies the j-th activation -- x + j * x_stride in fp32
+ * and its encoding at workspace + j * ws_stride (strides 0: one x for all, as
+ * pyrite_cuda_prepare_x writes it) -- into y + j * y_stride.  Every decodable
+ * type (the batch-1 kernel where it takes the format and alignment, else the
+ * generic kernel on the fp32 x); an id outside [0, n_experts) reads expert 0
+ * and sets status bit 1. */
+int pyrite_cuda_matvec_experts(int type_id, const void *stacked, size_t stacked_len, size_t n_experts,
+                               const int *expert_ids, size_t n_sel, const float *x, size_t x_stride,
+                               const void *workspace, size_t workspace_len, size_t ws_stride,
+                               float *y, size_t y_stride, size_t rows, size_t cols, unsigned flags,
+                               void *stream);
+
+/* act_j = silu(gate_j) * up_j for the n_sel experts (gate, up, act: n_sel x ff),
+ * each encoded at workspace + j * pyrite_cuda_workspace_size(0, ff, 1). */
+int pyrite_cuda_moe_silu_mul_encode(const float *gate, const float *up, size_t ff, size_t n_sel,
+                                    float *act, void *workspace, size_t workspace_len, void *stream);
+
+/* hidden[i] += sum_j expert_weights[j] * expert_out[j * h + i], j ascending. */
+int pyrite_cuda_moe_combine(const float *expert_out, const float *expert_weights, size_t n_sel, size_t h,
+                            float *hidden, void *stream);
+
 /* Static description of a return code. */
 const char *pyrite_error_string(int code);
 

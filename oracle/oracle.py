@@ -164,3 +164,24 @@ def reference_dequantize_rows(type_id: int, payload, rows: int, cols: int) -> np
     if rc != 0:
         raise ValueError(f"reference dequantize rejected the matrix (error {rc})")
     return out.reshape(rows, cols)
+
+
+def moe_route(logits, top_k: int, norm_topk_prob: bool = True, scale: float = 1.0) -> tuple[list[int], list[float]]:
+    """The reference's routing (pyrite/executor.py:757-772): fp64 softmax
+    (pyrite/tensor_ops.py:513-521), experts ranked by (-p, e), the top_k
+    weights renormalised to sum 1 when norm_topk_prob, then scaled."""
+    import math
+    values = [float(v) for v in logits]
+    m = max(values)
+    exps = [math.exp(v - m) for v in values]
+    total = sum(exps)
+    probs = [e / total for e in exps]
+    chosen = sorted(range(len(probs)), key=lambda e: (-probs[e], e))[:top_k]
+    weights = [probs[e] for e in chosen]
+    if norm_topk_prob:
+        t = sum(weights)
+        if t > 0:
+            weights = [w / t for w in weights]
+    if scale != 1.0:
+        weights = [w * scale for w in weights]
+    return chosen, weights

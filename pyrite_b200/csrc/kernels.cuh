@@ -24,7 +24,7 @@ template <typename T> struct MatvecArgs {
 
 // Device-side status word: kernels set bits here instead of trapping, so a
 // timed-out wait leaves the context usable and the host can report it.
-enum DeviceStatus : int { kStatusOk = 0, kStatusWaitTimeout = 1 };
+enum DeviceStatus : int { kStatusOk = 0, kStatusWaitTimeout = 1, kStatusBadExpert = 2 };
 int* device_status_word();  // this device's status word (address valid in kernels)
 
 // ---- programmatic dependent launch (PDL) ------------------------------------
@@ -52,9 +52,13 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
   return e == cudaSuccess ? 0 : -100 - (int)e;
 }
 
+struct ExpertArgs;
+
 // ---- generic kernels (mv_generic.cu) ----------------------------------------
+// experts: routed slices (ExpertArgs; x advances x_stride values per slice).
 template <typename T, int NC>
-int launch_mv_generic(int type_id, const MatvecArgs<T>& a, cudaStream_t stream, bool accumulate = false);
+int launch_mv_generic(int type_id, const MatvecArgs<T>& a, cudaStream_t stream, bool accumulate = false,
+                      const ExpertArgs* experts = nullptr, long long x_stride = 0);
 template <typename T>
 int launch_dq_generic(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, T* out,
                       long long ldo, cudaStream_t stream);
@@ -85,9 +89,18 @@ int launch_xprep(const float* x, long long ldx, int cols, int ncols, uint8_t* ws
                  cudaStream_t stream);
 // y[0..rows) from the prepared column at ws; static_weights enables the L2
 // prefetch of weights before the preceding kernel ends.
+// Routed experts for launch_mv_lane: w is a stack of n_experts matrices
+// expert_bytes apart; ids[0..n_sel) (device memory, read after the preceding
+// kernel) pick the ones to multiply, each by its own prepared x (ws_stride
+// bytes apart, 0: one shared x) into y + j * y_stride.
+struct ExpertArgs {
+  const int* ids;
+  int n_experts, n_sel;
+  long long expert_bytes, ws_stride, y_stride;
+};
 int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const uint8_t* ws,
                    float* y, bool static_weights, cudaStream_t stream, bool accumulate = false,
-                   const PostArgs* post = nullptr);
+                   const PostArgs* post = nullptr, const ExpertArgs* ex = nullptr);
 // Largest grid launch_mv_lane uses (argmax partial slots needed).
 int lane_max_grid();
 

@@ -1,0 +1,219 @@
+// moe.cu -- the routed-expert feed-forward of a Qwen3-MoE decode step
+// (pyrite/executor.py:672-683 _expert, :757-793 _moe), device resident.
+//
+//   moe_route_kernel        softmax over the router logits (fp64), the top-k
+//                           experts in (-p, e) order, their weights
+//                           (renormalised when norm_topk_prob, then scaled)
+//   pyrite_cuda_matvec_experts
+//                           the batch-1 matvec over the k selected slices of a
+//                           stacked expert tensor in one launch; the expert ids
+//                           are read on the device, so the whole step stays in
+//                           one CUDA graph (qwen3_moe.py:364-398: expert e of a
+//                           stacked (cols, rows, E) tensor is the contiguous
+//                           byte range e * rows * row_bytes)
+//   moe_silu_mul_encode_kernel
+//                           act_j = silu(gate_j) * up_j for every selected
+//                           expert j, each encoded for the down projection
+//   moe_combine_kernel      hidden += sum_j w_j * down_j, summed in rank order
+#include <cfloat>
+
+#include "kernels.cuh"
+#include "post_ops.cuh"
+#include "../../include/pyrite_b200.h"
+
+namespace pyr {
+namespace {
+
+// One CTA (256 threads): n <= 4096 router logits, k <= 32.
+__global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict__ logits, int n, int k, int norm,
+                                                        double scale, int* __restrict__ ids,
+                                                        float* __restrict__ weights) {
+  __shared__ double p[4096];
+  __shared__ double dred[32];
+  __shared__ int wi[32];
+  __shared__ double chosen_p[32];
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // softmax in fp64 (tensor_ops.py:513-521): exp(v - max) / sum
+  double m = -DBL_MAX;
+  for (int e = tid; e < n; e += blockDim.x) m = fmax(m, (double)logits[e]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) dred[warp] = m;
+  __syncthreads();
+  m = dred[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = fmax(m, dred[w]);
+  __syncthreads();
+  double s = 0.0;
+  for (int e = tid; e < n; e += blockDim.x) {
+    const double x = exp((double)logits[e] - m);
+    p[e] = x;
+    s += x;
+  }
+  const double total = block_sum(s, dred);
+  for (int e = tid; e < n; e += blockDim.x) p[e] /= total;
+  __syncthreads();
+  // k rounds of (max p, lowest e); a chosen expert drops out with p = -1
+  for (int r = 0; r < k; ++r) {
+    int bi = 0x7fffffff;
+    double bp = -2.0;
+    for (int e = tid; e < n; e += blockDim.x)
+      if (p[e] > bp || (p[e] == bp && e < bi)) {
+        bp = p[e];
+        bi = e;
+      }
+    // reduce (bp, bi) over the block: compare in fp64
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const double op = __shfl_xor_sync(0xffffffffu, bp, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (op > bp || (op == bp && oi < bi)) {
+        bp = op;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      dred[warp] = bp;
+      wi[warp] = bi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+        if (dred[w] > bp || (dred[w] == bp && wi[w] < bi)) {
+          bp = dred[w];
+          bi = wi[w];
+        }
+      chosen_p[r] = bp;
+      ids[r] = bi;
+      p[bi] = -1.0;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    double tot = 0.0;
+    for (int r = 0; r < k; ++r) tot += chosen_p[r];
+    for (int r = 0; r < k; ++r) {
+      double w = chosen_p[r];
+      if (norm && tot > 0.0) w = w / tot;
+      if (scale != 1.0) w = w * scale;
+      weights[r] = (float)w;
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// act_j = silu(gate_j) * up_j for j < n_sel (gate and up: n_sel x ff), encoded
+// at ws + j * ws_stride.  One warp per 32-value block.
+__global__ void __launch_bounds__(256) moe_silu_mul_encode_kernel(const float* __restrict__ gate,
+                                                                  const float* __restrict__ up, int ff, int n_sel,
+                                                                  float* __restrict__ act, uint8_t* __restrict__ ws,
+                                                                  long long ws_stride) {
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
+  const int per = ff / 32;
+  for (int t = gw; t < per * n_sel; t += nw) {
+    const int j = t / per, b = t - j * per;
+    const int i = 32 * b + lane;
+    const float g = gate[(size_t)j * ff + i], u = up[(size_t)j * ff + i];
+    const float sg = g > -60.0f ? g / (1.0f + expf(-g)) : 0.0f;
+    const float v = sg * u;
+    act[(size_t)j * ff + i] = v;
+    encode_block(v, lane, b, ff, ws + (size_t)j * (size_t)ws_stride);
+  }
+  pdl_launch_dependents();
+}
+
+// hidden[i] += sum_{j < n_sel} w_j * out[j][i], j ascending (executor.py:786-792).
+__global__ void __launch_bounds__(256) moe_combine_kernel(const float* __restrict__ out, const float* __restrict__ w,
+                                                          int n_sel, int h, float* __restrict__ hidden) {
+  pdl_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < h; i += gridDim.x * blockDim.x) {
+    float r = 0.f;
+    for (int j = 0; j < n_sel; ++j) {
+      const float wj = w[j];
+      if (wj != 0.0f) r += wj * out[(size_t)j * h + i];
+    }
+    hidden[i] += r;
+  }
+  pdl_launch_dependents();
+}
+
+int rc(int e) { return e > 0 ? PYRITE_E_CUDA : e; }
+
+}  // namespace
+}  // namespace pyr
+
+using namespace pyr;
+
+extern "C" {
+
+int pyrite_cuda_moe_route(const float* router_logits, int n_experts, int top_k, int norm_topk_prob, double scale,
+                          int* expert_ids, float* expert_weights, void* stream) {
+  if (!router_logits || !expert_ids || !expert_weights || n_experts <= 0 || n_experts > 4096 || top_k <= 0 ||
+      top_k > 32 || top_k > n_experts || !(scale > 0.0))
+    return PYRITE_E_SHAPE;
+  return rc(launch_pdl(moe_route_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), router_logits,
+                       n_experts, top_k, norm_topk_prob ? 1 : 0, scale, expert_ids, expert_weights));
+}
+
+int pyrite_cuda_matvec_experts(int type_id, const void* stacked, size_t stacked_len, size_t n_experts,
+                               const int* expert_ids, size_t n_sel, const float* x, size_t x_stride,
+                               const void* workspace, size_t workspace_len, size_t ws_stride, float* y,
+                               size_t y_stride, size_t rows, size_t cols, unsigned flags, void* stream) {
+  const TypeGeo* t = find_type(type_id);
+  if (!t) return PYRITE_E_TYPE;
+  if (rows == 0 || cols == 0 || cols % (size_t)t->bs || rows > 0x7fffffffu || cols > 0x7fffffffu)
+    return PYRITE_E_SHAPE;
+  const size_t rb = cols / t->bs * t->bpb;
+  const size_t expert_bytes = rb * rows;
+  if (!stacked || !expert_ids || !x || !y || !workspace || n_experts == 0 || n_experts > 0x7fffffffu || n_sel == 0 ||
+      n_sel > 64 || stacked_len != expert_bytes * n_experts)
+    return PYRITE_E_BUFFER;
+  if (y_stride < rows) return PYRITE_E_BUFFER;
+  const size_t per = pyrite_cuda_workspace_size(0, cols, 1);
+  if (((uintptr_t)workspace & 255) || (ws_stride && (ws_stride < per || ws_stride % 256)) ||
+      workspace_len < (ws_stride ? ws_stride * (n_sel - 1) + per : per))
+    return PYRITE_E_BUFFER;
+  const uint8_t* w = static_cast<const uint8_t*>(stacked);
+  ExpertArgs ex{expert_ids, (int)n_experts, (int)n_sel, (long long)expert_bytes, (long long)ws_stride,
+                (long long)y_stride};
+  const bool acc = (flags & PYRITE_F_ACCUMULATE) != 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int r;
+  // every expert keeps the stack's alignment when expert_bytes is a multiple
+  // of 16, so the batch-1 kernel's rule on the base covers them all
+  if (expert_bytes % 16 == 0 && lane_supported(type_id, w, rb, (int)cols)) {
+    r = launch_mv_lane(type_id, w, rb, (int)rows, (int)cols, static_cast<const uint8_t*>(workspace), y, false, s, acc,
+                       nullptr, &ex);
+  } else {  // the generic kernel on the fp32 activations
+    MatvecArgs<float> a{w, rb, (int)rows, (int)cols, x, (long long)cols, y, (long long)rows};
+    r = launch_mv_generic<float, 1>(type_id, a, s, acc, &ex, (long long)x_stride);
+  }
+  return r > 0 ? PYRITE_E_CUDA : r;
+}
+
+int pyrite_cuda_moe_silu_mul_encode(const float* gate, const float* up, size_t ff, size_t n_sel, float* act,
+                                    void* workspace, size_t workspace_len, void* stream) {
+  if (!gate || !up || !act || !workspace || ff == 0 || ff % 32 || ff > 0x7fffffffu || n_sel == 0 || n_sel > 64)
+    return PYRITE_E_SHAPE;
+  const size_t per = pyrite_cuda_workspace_size(0, ff, 1);
+  if (((uintptr_t)workspace & 255) || workspace_len < per * n_sel) return PYRITE_E_BUFFER;
+  const long long blocks = (long long)(ff / 32) * (long long)n_sel;
+  int grid = (int)((blocks + 7) / 8);
+  if (grid > 148 * 8) grid = 148 * 8;
+  return rc(launch_pdl(moe_silu_mul_encode_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), gate,
+                       up, (int)ff, (int)n_sel, act, static_cast<uint8_t*>(workspace), (long long)per));
+}
+
+int pyrite_cuda_moe_combine(const float* expert_out, const float* expert_weights, size_t n_sel, size_t h,
+                            float* hidden, void* stream) {
+  if (!expert_out || !expert_weights || !hidden || n_sel == 0 || n_sel > 64 || h == 0 || h > 0x7fffffffu)
+    return PYRITE_E_SHAPE;
+  int grid = (int)((h + 255) / 256);
+  if (grid > 148 * 4) grid = 148 * 4;
+  return rc(launch_pdl(moe_combine_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), expert_out,
+                       expert_weights, (int)n_sel, (int)h, hidden));
+}
+
+}  // extern "C"

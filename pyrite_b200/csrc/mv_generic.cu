@@ -14,11 +14,32 @@
 
 namespace pyr {
 
+// Routed experts (ex.ids != nullptr): blockIdx.y = j picks stacked matrix
+// ids[j] (expert_bytes apart), x + j * x_stride and y + j * y_stride.
+struct GenericExperts {
+  const int* ids = nullptr;
+  int n_experts = 0;
+  long long expert_bytes = 0, x_stride = 0, y_stride = 0;
+};
+
 template <int TY, typename T, int NC>
 __global__ void __launch_bounds__(256)
 mv_generic_kernel(const uint8_t* __restrict__ w, size_t row_bytes, int rows, int cols,
-                  const T* __restrict__ x, long long ldx, T* __restrict__ y, long long ldy, int accumulate) {
+                  const T* __restrict__ x, long long ldx, T* __restrict__ y, long long ldy, int accumulate,
+                  GenericExperts ex, int* status) {
   constexpr int BS = Geo<TY>::bs, BPB = Geo<TY>::bpb;
+  if (ex.ids) {
+    pdl_wait();  // the ids come from the preceding kernel
+    const int j = blockIdx.y;
+    int e = ex.ids[j];
+    if (e < 0 || e >= ex.n_experts) {  // never read outside the stack
+      if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(status, (int)kStatusBadExpert);
+      e = 0;
+    }
+    w += (size_t)e * (size_t)ex.expert_bytes;
+    x += (size_t)j * (size_t)ex.x_stride;
+    y += (size_t)j * (size_t)ex.y_stride;
+  }
   const int lane = threadIdx.x & 31;
   const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
@@ -100,13 +121,26 @@ int grid_for(long long work_items, int per_block) {
 }  // namespace
 
 template <typename T, int NC>
-int launch_mv_generic(int type_id, const MatvecArgs<T>& a, cudaStream_t stream, bool accumulate) {
-  const int grid = grid_for((long long)a.rows * 32, 256);
+int launch_mv_generic(int type_id, const MatvecArgs<T>& a, cudaStream_t stream, bool accumulate,
+                      const ExpertArgs* experts, long long x_stride) {
+  GenericExperts ex;
+  int n_sel = 1;
+  if (experts) {
+    ex.ids = experts->ids;
+    ex.n_experts = experts->n_experts;
+    ex.expert_bytes = experts->expert_bytes;
+    ex.x_stride = x_stride;
+    ex.y_stride = experts->y_stride;
+    n_sel = experts->n_sel;
+  }
+  int grid = grid_for((long long)a.rows * 32, 256);
+  if (experts && grid * n_sel > 148 * 16) grid = (148 * 16 + n_sel - 1) / n_sel;
   switch (type_id) {
-#define PYR_CASE(TY)                                                                            \
-  case TY:                                                                                      \
-    return launch_pdl(mv_generic_kernel<TY, T, NC>, dim3(grid), dim3(256), 0, stream, a.w,     \
-                      a.row_bytes, a.rows, a.cols, a.x, a.ldx, a.y, a.ldy, accumulate ? 1 : 0);
+#define PYR_CASE(TY)                                                                                       \
+  case TY:                                                                                                 \
+    return launch_pdl(mv_generic_kernel<TY, T, NC>, dim3(grid, n_sel), dim3(256), 0, stream, a.w,         \
+                      a.row_bytes, a.rows, a.cols, a.x, a.ldx, a.y, a.ldy, accumulate ? 1 : 0, ex,          \
+                      device_status_word());
     PYR_FOR_EACH_TYPE(PYR_CASE)
 #undef PYR_CASE
     default:
@@ -133,11 +167,16 @@ int launch_dq_generic(int type_id, const uint8_t* w, size_t row_bytes, int rows,
   }
 }
 
-template int launch_mv_generic<double, 1>(int, const MatvecArgs<double>&, cudaStream_t, bool);
-template int launch_mv_generic<float, 1>(int, const MatvecArgs<float>&, cudaStream_t, bool);
-template int launch_mv_generic<float, 2>(int, const MatvecArgs<float>&, cudaStream_t, bool);
-template int launch_mv_generic<float, 4>(int, const MatvecArgs<float>&, cudaStream_t, bool);
-template int launch_mv_generic<float, 8>(int, const MatvecArgs<float>&, cudaStream_t, bool);
+template int launch_mv_generic<double, 1>(int, const MatvecArgs<double>&, cudaStream_t, bool, const ExpertArgs*,
+                                          long long);
+template int launch_mv_generic<float, 1>(int, const MatvecArgs<float>&, cudaStream_t, bool, const ExpertArgs*,
+                                         long long);
+template int launch_mv_generic<float, 2>(int, const MatvecArgs<float>&, cudaStream_t, bool, const ExpertArgs*,
+                                         long long);
+template int launch_mv_generic<float, 4>(int, const MatvecArgs<float>&, cudaStream_t, bool, const ExpertArgs*,
+                                         long long);
+template int launch_mv_generic<float, 8>(int, const MatvecArgs<float>&, cudaStream_t, bool, const ExpertArgs*,
+                                         long long);
 template int launch_dq_generic<double>(int, const uint8_t*, size_t, int, int, double*, long long, cudaStream_t);
 template int launch_dq_generic<float>(int, const uint8_t*, size_t, int, int, float*, long long, cudaStream_t);
 

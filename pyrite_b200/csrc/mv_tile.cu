@@ -524,6 +524,13 @@ struct TileArgs {
   int static_weights;
   int accumulate;   // y += W x (a residual stream) instead of y = W x
   PostArgs post;    // operation run on the whole y by the last CTA to finish
+  // routed experts (experts != nullptr): w is a stack of n_experts matrices
+  // expert_bytes apart; the CTAs form n_sel equal groups, group j multiplies
+  // matrix experts[j] (read on the device) by the j-th prepared x (ws +
+  // j * ws_stride) into y + j * y_stride.
+  const int* experts;
+  int n_experts, n_sel;
+  long long expert_bytes, ws_stride, y_stride;
 };
 
 // CTAs per SM each format's register budget allows (launch bounds).
@@ -542,7 +549,14 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   const int rows_per_stage = M << a.rs_log2;
   const int nstages = (a.rows + rows_per_stage - 1) / rows_per_stage;
   const int units = a.cols / U::VALS;
-  const int wmod4 = (int)((uintptr_t)a.w & 3);
+  // routed experts: CTA group `sel` takes stacked matrix a.experts[sel]
+  int cta = blockIdx.x, ncta = gridDim.x, sel = 0;
+  if (a.experts) {
+    ncta = gridDim.x / a.n_sel;
+    sel = blockIdx.x / ncta;
+    cta = blockIdx.x - sel * ncta;
+  }
+  const uint8_t* wb = a.w;  // this CTA's matrix (an expert's: set once its id is readable)
   const uint32_t ring = smem_addr(smem);
   const size_t stage_stride = (size_t)rows_per_stage * a.row_bytes;
 
@@ -561,9 +575,9 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   auto stage_rows = [&](int st) { return min(rows_per_stage, a.rows - st * rows_per_stage); };
   // the CTA's k-th stage -> ring slot k % S, one bulk copy of its contiguous bytes
   auto issue = [&](int k) {  // thread 0
-    const int st = blockIdx.x + k * gridDim.x;
+    const int st = cta + k * ncta;
     if (st >= nstages) return;
-    const uintptr_t src = (uintptr_t)a.w + (uintptr_t)st * stage_stride;
+    const uintptr_t src = (uintptr_t)wb + (uintptr_t)st * stage_stride;
     const uintptr_t al = src & ~(uintptr_t)15;
     const uint32_t len = (uint32_t)(((src - al) + (uintptr_t)stage_rows(st) * a.row_bytes + 15) & ~(uintptr_t)15);
     const uint32_t bar = smem_addr(&bars[k % S]);
@@ -571,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
     bulk_g2s(ring + (uint32_t)((k % S) * a.stage_bytes), reinterpret_cast<const void*>(al), len, bar);
   };
 
-  const int my = blockIdx.x < nstages ? (nstages - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int my = cta < nstages ? (nstages - 1 - cta) / ncta + 1 : 0;
   if (tid == 0) {
     for (int k = 0; k < S; ++k) mbar_init(smem_addr(&bars[k]), 1);
     fence_mbar_init();
@@ -579,28 +593,39 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   __syncthreads();
   // Weights are read-only: with static weights the first stages stream while
   // the preceding kernel drains; x and y are touched only after pdl_wait().
-  if (a.static_weights && tid == 0)
+  const bool early = a.static_weights && !a.experts;
+  if (early && tid == 0)
     for (int k = 0; k < min(my, S - 1); ++k) issue(k);
   pdl_wait();
   pdl_launch_dependents();
-  if (!a.static_weights && tid == 0)
+  if (a.experts) {  // written by the routing kernel this one waited for
+    int eid = a.experts[sel];
+    if (eid < 0 || eid >= a.n_experts) {  // never read outside the stack
+      if (tid == 0) atomicOr(status, (int)kStatusBadExpert);
+      eid = 0;
+    }
+    wb = a.w + (size_t)eid * (size_t)a.expert_bytes;
+  }
+  const int wmod4 = (int)((uintptr_t)wb & 3);
+  float* const yb = a.y + (size_t)sel * (size_t)a.y_stride;
+  if (!early && tid == 0)
     for (int k = 0; k < min(my, S - 1); ++k) issue(k);
 
   typename U::XU xu[UL];  // this lane's x, for the whole kernel
-  const XView xv = xview(a.ws, a.cols);
+  const XView xv = xview(a.ws + (size_t)sel * (size_t)a.ws_stride, a.cols);
 #pragma unroll
   for (int k = 0; k < UL; ++k) U::load_x(xv, ls + k * lps < units ? ls + k * lps : 0, xu[k], wmod4);
 
   float best_v = -FLT_MAX;  // POST_ARGMAX: this thread's best finalized row
   int best_i = 0x7fffffff;
   auto finalize = [&](int k) {  // fixed-order sum of the slot warps' partials
-    const int st = blockIdx.x + k * gridDim.x;
+    const int st = cta + k * ncta;
     if (tid < stage_rows(st)) {
       const int s_slot = tid / M, i = tid % M, wps = lps >> 5;
       const float* r = red + (size_t)(k & 1) * kWarps * M;
       float v = 0.f;
       for (int w = 0; w < wps; ++w) v += r[(s_slot * wps + w) * M + i];
-      float* yp = a.y + (size_t)st * rows_per_stage + tid;
+      float* yp = yb + (size_t)st * rows_per_stage + tid;
       v = a.accumulate ? *yp + v : v;
       *yp = v;
       better(best_v, best_i, v, st * rows_per_stage + tid);
@@ -621,10 +646,10 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
       fence_proxy_async();  // generic reads of the slot precede its async refill
       issue(k + S - 1);
     }
-    const int st = blockIdx.x + k * gridDim.x;
+    const int st = cta + k * ncta;
     const int nr = stage_rows(st);
     const uint32_t base = ring + (uint32_t)((k % S) * a.stage_bytes) +
-                          (uint32_t)(((uintptr_t)a.w + (uintptr_t)st * stage_stride) & 15) +
+                          (uint32_t)(((uintptr_t)wb + (uintptr_t)st * stage_stride) & 15) +
                           (uint32_t)(slot * M) * (uint32_t)a.row_bytes;
     float acc[M];
 #pragma unroll
@@ -699,7 +724,14 @@ int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
   if (per_sm > minb) per_sm = minb;
   if (per_sm < 1) per_sm = 1;
   int grid = sms[dev] * per_sm;
-  if (grid > nstages) grid = nstages;
+  if (ta.experts) {  // n_sel equal CTA groups
+    int cpe = grid / ta.n_sel;
+    if (cpe > nstages) cpe = nstages;
+    if (cpe < 1) cpe = 1;
+    grid = cpe * ta.n_sel;
+  } else if (grid > nstages) {
+    grid = nstages;
+  }
   return launch_pdl(mv_tile_kernel<TY, UL, M>, dim3(grid), dim3(kThreads), smem, stream, ta, device_status_word());
 }
 
@@ -746,11 +778,21 @@ int launch_xprep(const float* x, long long ldx, int cols, int ncols, uint8_t* ws
 }
 
 int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const uint8_t* ws,
-                   float* y, bool static_weights, cudaStream_t stream, bool accumulate, const PostArgs* post) {
+                   float* y, bool static_weights, cudaStream_t stream, bool accumulate, const PostArgs* post,
+                   const ExpertArgs* ex) {
   const int vals = (type_id == Q6_K || type_id == Q4_K || type_id == Q5_K) ? 64 : 32;
   const TilePlan p = plan_tile(row_bytes, rows, cols, vals);
   TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs_log2, p.m, p.stage_bytes, static_weights ? 1 : 0,
-              accumulate ? 1 : 0, post ? *post : PostArgs{}};
+              accumulate ? 1 : 0, post ? *post : PostArgs{}, nullptr, 0, 0, 0, 0, 0};
+  if (ex) {
+    ta.experts = ex->ids;
+    ta.n_experts = ex->n_experts;
+    ta.n_sel = ex->n_sel;
+    ta.expert_bytes = ex->expert_bytes;
+    ta.ws_stride = ex->ws_stride;
+    ta.y_stride = ex->y_stride;
+    ta.static_weights = 0;
+  }
   switch (type_id) {
     case Q4_K: return launch_tile_type<Q4_K>(ta, p.ul, p.smem, stream);
     case Q5_K: return launch_tile_type<Q5_K>(ta, p.ul, p.smem, stream);

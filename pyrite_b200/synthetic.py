@@ -111,3 +111,122 @@ def dense_tensors(spec: DenseSpec) -> Iterator[tuple[str, tuple[int, ...], int, 
 def prompt_ids(spec: DenseSpec, n: int = 16, seed: int = 7) -> list[int]:
     """BASELINE's prompt: ``n`` seeded uniform token ids."""
     return [int(v) for v in np.random.default_rng(seed).integers(0, spec.vocab_size, n)]
+
+
+# ---------------------------------------------------------------- MoE (qwen3moe)
+@dataclass(frozen=True)
+class MoESpec:
+    """A ``qwen3moe`` checkpoint: BASELINE configs[3] (Qwen3-30B-A3B-shaped)
+    and smaller variants for parity runs."""
+
+    architecture: str = "qwen3moe"
+    hidden_size: int = 2048
+    num_hidden_layers: int = 48
+    num_attention_heads: int = 32
+    num_key_value_heads: int = 4
+    head_dim: int = 128
+    intermediate_size: int = 6144      # dense feed-forward length (metadata only)
+    moe_intermediate_size: int = 768
+    num_experts: int = 128
+    num_experts_per_tok: int = 8
+    vocab_size: int = 151936
+    rope_theta: float = 1_000_000.0
+    rms_norm_eps: float = 1e-6
+    norm_topk_prob: bool = True
+    tied_embeddings: bool = False
+    context_length: int = 40960
+    seed: int = 20240607
+    qk_norm: bool = True
+
+    @property
+    def q_dim(self) -> int:
+        return self.num_attention_heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.num_key_value_heads * self.head_dim
+
+    @classmethod
+    def c4(cls) -> "MoESpec":
+        """Qwen3-30B-A3B-shaped, Q4_K_M mix."""
+        return cls()
+
+    @classmethod
+    def tiny(cls) -> "MoESpec":
+        """A two-layer model small enough for the reference to run in seconds."""
+        return cls(hidden_size=512, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                   intermediate_size=1024, moe_intermediate_size=256, num_experts=16, num_experts_per_tok=4,
+                   vocab_size=2048)
+
+
+#: Q4_K_M mix as BASELINE states it: Q4_K for most tensors, Q6_K for attn_v,
+#: half of ffn_down (the even layers) and the output projection; the router
+#: (ffn_gate_inp) stays F32 as llama.cpp keeps it.
+Q4_K, Q6_K, F32 = 12, 14, 0
+
+
+def moe_tensor_type(spec: MoESpec, name: str) -> int:
+    if name == "output.weight":
+        return Q6_K
+    if name.endswith("attn_v.weight"):
+        return Q6_K
+    if name.endswith("ffn_down_exps.weight"):
+        layer = int(name.split(".")[1])
+        return Q6_K if layer % 2 == 0 else Q4_K
+    if name.endswith("ffn_gate_inp.weight") or name.endswith("norm.weight"):
+        return F32
+    return Q4_K
+
+
+def moe_metadata(spec: MoESpec) -> dict[str, object]:
+    """GGUF metadata keys the reference reads (``qwen3_moe.py:148-254``)."""
+    a = spec.architecture
+    return {
+        f"{a}.embedding_length": spec.hidden_size,
+        f"{a}.block_count": spec.num_hidden_layers,
+        f"{a}.feed_forward_length": spec.intermediate_size,
+        f"{a}.expert_feed_forward_length": spec.moe_intermediate_size,
+        f"{a}.expert_count": spec.num_experts,
+        f"{a}.expert_used_count": spec.num_experts_per_tok,
+        f"{a}.expert_weights_norm": bool(spec.norm_topk_prob),
+        f"{a}.attention.head_count": spec.num_attention_heads,
+        f"{a}.attention.head_count_kv": spec.num_key_value_heads,
+        f"{a}.attention.key_length": spec.head_dim,
+        f"{a}.attention.value_length": spec.head_dim,
+        f"{a}.attention.layer_norm_rms_epsilon": float(spec.rms_norm_eps),
+        f"{a}.rope.freq_base": float(spec.rope_theta),
+        f"{a}.context_length": spec.context_length,
+        f"{a}.tied_word_embeddings": bool(spec.tied_embeddings),
+    }
+
+
+def moe_tensors(spec: MoESpec) -> Iterator[tuple[str, tuple[int, ...], int, bytes]]:
+    """(name, GGML dims, GGML type, payload) of every tensor of the checkpoint.
+    A stacked expert tensor ``(cols, rows, E)`` is E matrices back to back."""
+    ones = lambda n: np.ones(n, dtype=np.float32).tobytes()  # noqa: E731
+    h, q, kv, ff, E = spec.hidden_size, spec.q_dim, spec.kv_dim, spec.moe_intermediate_size, spec.num_experts
+
+    def mat(name: str, dims: tuple[int, ...]) -> tuple[str, tuple[int, ...], int, bytes]:
+        t = moe_tensor_type(spec, name)
+        count = int(np.prod(dims))
+        w = _weights(name, count, spec.seed)
+        return name, dims, t, (w.tobytes() if t == F32 else quantize(t, w))
+
+    yield mat("token_embd.weight", (h, spec.vocab_size))
+    yield ("output_norm.weight", (h,), F32, ones(h))
+    if not spec.tied_embeddings:
+        yield mat("output.weight", (h, spec.vocab_size))
+    for layer in range(spec.num_hidden_layers):
+        p = f"blk.{layer}."
+        yield (p + "attn_norm.weight", (h,), F32, ones(h))
+        yield mat(p + "attn_q.weight", (h, q))
+        yield mat(p + "attn_k.weight", (h, kv))
+        yield mat(p + "attn_v.weight", (h, kv))
+        yield mat(p + "attn_output.weight", (q, h))
+        yield (p + "attn_q_norm.weight", (spec.head_dim,), F32, ones(spec.head_dim))
+        yield (p + "attn_k_norm.weight", (spec.head_dim,), F32, ones(spec.head_dim))
+        yield (p + "ffn_norm.weight", (h,), F32, ones(h))
+        yield mat(p + "ffn_gate_inp.weight", (h, E))
+        yield mat(p + "ffn_gate_exps.weight", (h, ff, E))
+        yield mat(p + "ffn_up_exps.weight", (h, ff, E))
+        yield mat(p + "ffn_down_exps.weight", (ff, h, E))
