@@ -40,6 +40,7 @@ class DenseSpec:
     weight_type: int = 8  # Q8_0
     context_length: int = 40960
     seed: int = 20240607
+    mix: str = ""         # "q4_k_m": one type per tensor (dense_tensor_type), else weight_type
 
     @property
     def q_dim(self) -> int:
@@ -53,6 +54,14 @@ class DenseSpec:
     def c1(cls) -> "DenseSpec":
         """Qwen3-0.6B-shaped, all matrices Q8_0."""
         return cls()
+
+    @classmethod
+    def c3(cls) -> "DenseSpec":
+        """Llama-3-8B-shaped, Q4_K_M mix."""
+        return cls(architecture="llama", hidden_size=4096, num_hidden_layers=32, num_attention_heads=32,
+                   num_key_value_heads=8, head_dim=128, intermediate_size=14336, vocab_size=128256,
+                   rope_theta=500_000.0, rms_norm_eps=1e-5, qk_norm=False, tied_embeddings=False,
+                   weight_type=12, context_length=8192, mix="q4_k_m")
 
 
 def _weights(name: str, count: int, seed: int) -> np.ndarray:
@@ -87,14 +96,28 @@ def layer_matrices(spec: DenseSpec) -> list[tuple[str, int, int]]:
             ("ffn_down.weight", h, f)]
 
 
+def dense_tensor_type(spec: DenseSpec, name: str) -> int:
+    """GGML type of a matrix: ``weight_type``, or for the Q4_K_M mix (as
+    BASELINE states it) Q6_K for attn_v, ffn_down of the even layers (half of
+    them) and the output projection, Q4_K for the rest."""
+    if spec.mix != "q4_k_m":
+        return spec.weight_type
+    if name == "output.weight" or name.endswith("attn_v.weight"):
+        return 14
+    if name.endswith("ffn_down.weight"):
+        return 14 if int(name.split(".")[1]) % 2 == 0 else 12
+    return 12
+
+
 def dense_tensors(spec: DenseSpec) -> Iterator[tuple[str, tuple[int, ...], int, bytes]]:
     """(name, GGML dims, GGML type, payload) for every tensor of the checkpoint."""
     ones = lambda n: np.ones(n, dtype=np.float32).tobytes()  # noqa: E731
-    t = spec.weight_type
+    t = dense_tensor_type(spec, "token_embd.weight")
     yield ("token_embd.weight", (spec.hidden_size, spec.vocab_size), t,
            quantize(t, _weights("token_embd.weight", spec.hidden_size * spec.vocab_size, spec.seed)))
     yield ("output_norm.weight", (spec.hidden_size,), 0, ones(spec.hidden_size))
     if not spec.tied_embeddings:
+        t = dense_tensor_type(spec, "output.weight")
         yield ("output.weight", (spec.hidden_size, spec.vocab_size), t,
                quantize(t, _weights("output.weight", spec.hidden_size * spec.vocab_size, spec.seed)))
     for layer in range(spec.num_hidden_layers):
@@ -105,6 +128,7 @@ def dense_tensors(spec: DenseSpec) -> Iterator[tuple[str, tuple[int, ...], int, 
             yield (p + "attn_k_norm.weight", (spec.head_dim,), 0, ones(spec.head_dim))
         yield (p + "ffn_norm.weight", (spec.hidden_size,), 0, ones(spec.hidden_size))
         for suffix, rows, cols in layer_matrices(spec):
+            t = dense_tensor_type(spec, p + suffix)
             yield (p + suffix, (cols, rows), t, quantize(t, _weights(p + suffix, rows * cols, spec.seed)))
 
 

@@ -6,10 +6,12 @@ the reference's ``open_executor`` (a ``DenseExecutor``, native C kernels on),
 and records the greedy decode of the seeded prompt plus the top logits of
 every forward pass:
 
-    python tests/golden/make_c1_golden.py [--layers N] [--vocab V] [--out NAME]
+    python tests/golden/make_c1_golden.py [--spec c1|c3] [--layers N] [--vocab V] [--out NAME]
 
 Defaults are configs[0] in full (28 layers, vocab 151936, 16-token prompt,
-8 new tokens, KV limit 512).  Needs the reference tree (``PYRITE_REF_ROOT``,
+8 new tokens, KV limit 512); ``--spec c3`` is the Llama-3-8B-shaped Q4_K_M
+model of configs[2] (use --layers to keep the reference run short), ``c3tiny``
+the same architecture and mix at toy width.  Needs the reference tree (``PYRITE_REF_ROOT``,
 default /root/reference); the committed JSON is what the tests read.
 """
 from __future__ import annotations
@@ -30,6 +32,7 @@ REF = Path(os.environ.get("PYRITE_REF_ROOT", "/root/reference"))
 
 def main() -> None:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--spec", choices=("c1", "c3", "c3tiny"), default="c1")
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--vocab", type=int, default=None)
     ap.add_argument("--new", type=int, default=8)
@@ -38,7 +41,10 @@ def main() -> None:
 
     from pyrite_b200.synthetic import DenseSpec, dense_tensors, metadata, prompt_ids
 
-    spec = DenseSpec.c1()
+    spec = DenseSpec.c1() if args.spec == "c1" else DenseSpec.c3()
+    if args.spec == "c3tiny":  # the configs[2] architecture and mix at toy width
+        spec = replace(spec, hidden_size=512, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                       intermediate_size=1024, vocab_size=2048)
     if args.layers is not None:
         spec = replace(spec, num_hidden_layers=args.layers)
     if args.vocab is not None:

@@ -82,3 +82,33 @@ def test_fused_step_equals_unfused_step(cuda_device):
 
 def test_c1_qwen3_0p6b_q8_0_decode_matches_reference(cuda_device):
     _check_against("c1_decode.json", cuda_device)
+
+
+def _check_mixed(golden_name, cuda_device):
+    """A mixed-type checkpoint (Q4_K_M) through MixedDecoder against the reference."""
+    import torch
+
+    from pyrite_b200.kernels import cuda as K
+    from pyrite_b200.model import MixedDecoder
+
+    g = json.loads((GOLDEN / golden_name).read_text())
+    dec = MixedDecoder.synthetic(_spec(g), device=cuda_device, max_ctx=512)
+    prompt, want = g["prompt"], g["generated"]
+    got = dec.generate(prompt, len(want))
+    assert K.status() == 0
+    assert got[len(prompt):] == want, f"greedy ids differ: {got[len(prompt):]} vs {want}"
+    dec.reset(prompt)
+    worst = 0.0
+    for top in g["top_logits"][: len(prompt) + len(want) - 1]:
+        dec.run_steps(1)
+        logits = dec.logits.double().cpu()
+        ids = [i for i, _ in top]
+        vals = torch.tensor([v for _, v in top], dtype=torch.float64)
+        assert int(torch.argmax(logits)) == ids[0]
+        worst = max(worst, float((logits[ids] - vals).abs().max()))
+    assert worst <= LOGIT_TOL, f"max |logit - reference| = {worst}"
+
+
+def test_llama_q4_k_m_tiny_decode_matches_reference(cuda_device):
+    """configs[2]'s architecture (llama, no QK norm, untied output) and Q4_K_M mix."""
+    _check_mixed("llama_tiny.json", cuda_device)

@@ -53,3 +53,18 @@ def test_multithreaded_equals_single_threaded():
     w = gaussian_weights(64, 4096, seed=9)
     for t in (8, 12, 14, 23):
         assert quantize(t, w, threads=1) == quantize(t, w, threads=7)
+
+
+def test_q4_k_m_mix_rule():
+    """Q6_K for attn_v, ffn_down of the even layers and the output; Q4_K else;
+    the MoE router stays F32."""
+    from pyrite_b200.synthetic import DenseSpec, MoESpec, dense_tensor_type, moe_tensor_type
+    c3, c4 = DenseSpec.c3(), MoESpec.c4()
+    assert dense_tensor_type(c3, "output.weight") == 14
+    assert dense_tensor_type(c3, "blk.3.attn_v.weight") == 14
+    assert [dense_tensor_type(c3, f"blk.{i}.ffn_down.weight") for i in range(4)] == [14, 12, 14, 12]
+    assert dense_tensor_type(c3, "blk.3.attn_q.weight") == 12
+    assert dense_tensor_type(DenseSpec.c1(), "blk.0.attn_v.weight") == 8
+    assert moe_tensor_type(c4, "blk.0.ffn_gate_inp.weight") == 0
+    assert [moe_tensor_type(c4, f"blk.{i}.ffn_down_exps.weight") for i in range(2)] == [14, 12]
+    assert moe_tensor_type(c4, "blk.5.ffn_up_exps.weight") == 12
