@@ -216,13 +216,19 @@ int pyrite_cuda_attention(const float *q, const float *k_cache, const float *v_c
                           int n_heads, int n_kv_heads, int head_dim, int max_ctx, float *out,
                           void *stream);
 
-/* pyrite_cuda_qk_rope_kv and pyrite_cuda_attention in one launch (one CTA per
- * q head), the output also encoded into `workspace` for the output
- * projection (pyrite_cuda_matvec_prepared).  Same results. */
+/* pyrite_cuda_qk_rope_kv and pyrite_cuda_attention in one launch, the context
+ * split over up to 32 CTAs per q head (flash-decoding: per-chunk max, sum and
+ * weighted values, merged by the last CTA of the head), the output also
+ * encoded into `workspace` for the output projection
+ * (pyrite_cuda_matvec_prepared).  `scratch`: 16-byte aligned device memory of
+ * pyrite_cuda_attention_scratch_size() bytes whose first n_heads words are
+ * zero (the call leaves them zero); one per call that can overlap another. */
+size_t pyrite_cuda_attention_scratch_size(int n_heads, int max_ctx);
 int pyrite_cuda_attention_step(const float *qkv, const float *q_norm, const float *k_norm, int n_heads,
                                int n_kv_heads, int head_dim, double eps, const int *pos,
                                const void *rope_table, int max_ctx, float *k_cache, float *v_cache,
-                               float *out, void *workspace, size_t workspace_len, void *stream);
+                               float *out, void *workspace, size_t workspace_len, void *scratch,
+                               size_t scratch_len, void *stream);
 
 /* act = silu(gate) * up for gate_up = [gate (f) | up (f)] (dense.py:491-494,
  * tensor_ops.py:509-510), also encoded for the down projection. */

@@ -182,38 +182,155 @@ __global__ void __launch_bounds__(256) attention_kernel(const float* __restrict_
   pdl_launch_dependents();
 }
 
-// The fused step of one q head (256 threads): its q and its kv head's k
-// normalised and rotated, k and v appended at row pos (the CTAs of one GQA
-// group write identical values), attention over rows 0..pos, and the head's
-// output written and encoded for the output projection (4 blocks of 32).
+// The fused step of one q head, its context split over CTAs (positions
+// [c L, (c+1) L) in CTA c, L = ceil(max_ctx / nsplit)): every CTA with work
+// normalises and rotates q; the CTA holding position pos also normalises and
+// rotates its kv head's k and appends k and v at row pos (the CTAs of one GQA
+// group write identical values).  Each CTA leaves (max score m_c, sum of
+// exp(s - m_c), sum of exp(s - m_c) v) for its positions; the last CTA of the
+// head to finish (a ticket, no waiting) merges them in chunk order, writes the
+// head's output and encodes it for the output projection.  Within a CTA the 8
+// warps take every 8th position, four at a time, so a long context keeps many
+// loads in flight.
+constexpr int kAttnPart = 132;    // floats per partial: m, s, 2 pad, o[128]
+
 __global__ void __launch_bounds__(256) attention_step_kernel(
     const float* __restrict__ qkv, const float* __restrict__ qnw, const float* __restrict__ knw, int nq, int nkv,
-    double eps, const int* __restrict__ pos_ptr, const double2* __restrict__ rope, int max_ctx,
+    double eps, const int* __restrict__ pos_ptr, const double2* __restrict__ rope, int max_ctx, int chunk,
     float* __restrict__ kcache, float* __restrict__ vcache, float scale, float* __restrict__ out,
-    uint8_t* __restrict__ ws) {
+    uint8_t* __restrict__ ws, unsigned* __restrict__ tickets, float* __restrict__ parts) {
   constexpr int HD = 128;
-  extern __shared__ float sh[];  // [max_ctx] scores
-  __shared__ float red[32];
+  extern __shared__ float sh[];  // [chunk] scores
   __shared__ __align__(16) float qs[HD];
+  __shared__ __align__(16) float acc[8][HD];
+  __shared__ float red[32];
+  __shared__ int last;
   pdl_wait();
-  const int h = blockIdx.x, kvh = h / (nq / nkv), kv_dim = nkv * HD;
+  const int c = blockIdx.x, h = blockIdx.y, nsplit = gridDim.x;
+  const int kvh = h / (nq / nkv), kv_dim = nkv * HD;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int pos = *pos_ptr;
-  if (pos < 0 || pos >= max_ctx) return;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const double2* rr = rope + (size_t)pos * (HD / 2);
-  if (warp == 0) head_norm_rope(qkv + (size_t)h * HD, qnw, eps, rr, true, qs, lane);
-  else if (warp == 1)
-    head_norm_rope(qkv + (size_t)(nq + kvh) * HD, knw, eps, rr, true, kcache + (size_t)pos * kv_dim + (size_t)kvh * HD,
-                   lane);
-  else if (warp == 2)
-    head_norm_rope(qkv + (size_t)(nq + nkv + kvh) * HD, nullptr, eps, rr, false,
-                   vcache + (size_t)pos * kv_dim + (size_t)kvh * HD, lane);
+  const bool valid = pos >= 0 && pos < max_ctx;
+  const int T = valid ? pos + 1 : 0;
+  const int t0 = c * chunk, t1 = min(t0 + chunk, T), n = t1 - t0;
+  float* part = parts + ((size_t)h * nsplit + c) * kAttnPart;
+  if (n > 0) {
+    const double2* rr = rope + (size_t)pos * (HD / 2);
+    if (warp == 0) head_norm_rope(qkv + (size_t)h * HD, qnw, eps, rr, true, qs, lane);
+    if (t1 == T) {  // this chunk holds the new position
+      if (warp == 1)
+        head_norm_rope(qkv + (size_t)(nq + kvh) * HD, knw, eps, rr, true,
+                       kcache + (size_t)pos * kv_dim + (size_t)kvh * HD, lane);
+      else if (warp == 2)
+        head_norm_rope(qkv + (size_t)(nq + nkv + kvh) * HD, nullptr, eps, rr, false,
+                       vcache + (size_t)pos * kv_dim + (size_t)kvh * HD, lane);
+    }
+    __syncthreads();
+    // scores of this chunk: warp w takes positions t0 + w, t0 + w + 8, ... four at a time
+    const float4 qv = reinterpret_cast<const float4*>(qs)[lane];
+    for (int i = warp; i < n; i += 32) {
+      float d[4];
+      float4 kk[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = t0 + min(i + 8 * u, n - 1);
+        kk[u] = reinterpret_cast<const float4*>(kcache + (size_t)t * kv_dim + (size_t)kvh * HD)[lane];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        d[u] = qv.x * kk[u].x + qv.y * kk[u].y + qv.z * kk[u].z + qv.w * kk[u].w;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d[u] += __shfl_xor_sync(0xffffffffu, d[u], o);
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i + 8 * u < n) sh[i + 8 * u] = d[u] * scale;
+      }
+    }
+    __syncthreads();
+    float m = -FLT_MAX;
+    for (int i = tid; i < n; i += blockDim.x) m = fmaxf(m, sh[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = red[0];
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
+    __syncthreads();
+    float ssum = 0.f;
+    for (int i = tid; i < n; i += blockDim.x) {
+      const float e = expf(sh[i] - m);
+      sh[i] = e;
+      ssum += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+    if (lane == 0) red[8 + warp] = ssum;
+    __syncthreads();
+    // value mix: warp w sums positions w, w + 8, ...; lane holds dims 4 lane .. 4 lane + 3
+    float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = warp; i < n; i += 32) {
+      float4 vv[4];
+      float pw[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = min(i + 8 * u, n - 1);
+        vv[u] = reinterpret_cast<const float4*>(vcache + (size_t)(t0 + j) * kv_dim + (size_t)kvh * HD)[lane];
+        pw[u] = i + 8 * u < n ? sh[j] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        o4.x += pw[u] * vv[u].x;
+        o4.y += pw[u] * vv[u].y;
+        o4.z += pw[u] * vv[u].z;
+        o4.w += pw[u] * vv[u].w;
+      }
+    }
+    reinterpret_cast<float4*>(acc[warp])[lane] = o4;
+    __syncthreads();
+    if (tid < HD) {
+      float o = 0.f;
+      for (int w = 0; w < 8; ++w) o += acc[w][tid];
+      part[4 + tid] = o;
+    }
+    if (tid == 0) {
+      float st = 0.f;
+      for (int w = 0; w < 8; ++w) st += red[8 + w];
+      part[0] = m;
+      part[1] = st;
+    }
+  } else if (tid == 0) {
+    part[0] = -FLT_MAX;
+    part[1] = 0.f;
+  }
+  // the last CTA of this head merges the chunks
   __syncthreads();
-  const float o = attend_head(qs, kcache, vcache, kvh, kv_dim, pos + 1, scale, sh, red);
-  if (threadIdx.x < HD) {
-    out[(size_t)h * HD + threadIdx.x] = o;
+  if (tid == 0) {
+    __threadfence();
+    last = atomicAdd(tickets + h, 1u) == (unsigned)nsplit - 1 ? 1 : 0;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const float* hp = parts + (size_t)h * nsplit * kAttnPart;
+  float M = -FLT_MAX;
+  for (int k = 0; k < nsplit; ++k) M = fmaxf(M, __ldcg(hp + (size_t)k * kAttnPart));
+  if (tid < HD && T > 0) {
+    float S = 0.f, O = 0.f;
+    for (int k = 0; k < nsplit; ++k) {
+      const float* pk = hp + (size_t)k * kAttnPart;
+      const float sk = __ldcg(pk + 1);
+      if (sk == 0.f) continue;
+      const float f = expf(__ldcg(pk) - M);
+      S += sk * f;
+      O += __ldcg(pk + 4 + tid) * f;
+    }
+    const float o = O / S;
+    out[(size_t)h * HD + tid] = o;
     encode_block(o, lane, h * (HD / 32) + warp, nq * HD, ws);
   }
+  if (tid == 0) tickets[h] = 0u;
   pdl_launch_dependents();
 }
 
@@ -325,20 +442,34 @@ int pyrite_cuda_attention(const float* q, const float* k_cache, const float* v_c
                        v_cache, pos, n_heads, n_kv_heads, (float)(1.0 / sqrt((double)head_dim)), max_ctx, out));
 }
 
+size_t pyrite_cuda_attention_scratch_size(int n_heads, int max_ctx) {
+  if (n_heads <= 0 || max_ctx <= 0) return 0;
+  const int nsplit = (max_ctx + 63) / 64 < 32 ? (max_ctx + 63) / 64 : 32;
+  return 256 + (size_t)n_heads * nsplit * kAttnPart * sizeof(float) + ((size_t)n_heads * 4 + 255) / 256 * 256;
+}
+
 int pyrite_cuda_attention_step(const float* qkv, const float* q_norm, const float* k_norm, int n_heads, int n_kv_heads,
                                int head_dim, double eps, const int* pos, const void* rope_table, int max_ctx,
                                float* k_cache, float* v_cache, float* out, void* workspace, size_t workspace_len,
-                               void* stream) {
+                               void* scratch, size_t scratch_len, void* stream) {
   if (head_dim != 128 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || !qkv || !pos || !rope_table ||
       !k_cache || !v_cache || !out || !workspace || max_ctx <= 0)
     return PYRITE_E_SHAPE;
-  const size_t smem = (size_t)max_ctx * sizeof(float);
-  if (smem > 48 * 1024) return PYRITE_E_SHAPE;
+  // context split: up to 32 CTAs per head, at least 64 positions each
+  const int nsplit = (max_ctx + 63) / 64 < 32 ? (max_ctx + 63) / 64 : 32;
+  const int chunk = (max_ctx + nsplit - 1) / nsplit;
+  const size_t smem = (size_t)chunk * sizeof(float);
+  if (smem > 32 * 1024) return PYRITE_E_SHAPE;
   const size_t n = (size_t)n_heads * head_dim;
   if (workspace_len < pyrite_cuda_workspace_size(0, n, 1) || ((uintptr_t)workspace & 255)) return PYRITE_E_BUFFER;
-  return rc(launch_pdl(attention_step_kernel, dim3(n_heads), dim3(256), smem, static_cast<cudaStream_t>(stream), qkv,
-                       q_norm, k_norm, n_heads, n_kv_heads, eps, pos, static_cast<const double2*>(rope_table), max_ctx,
-                       k_cache, v_cache, (float)(1.0 / sqrt((double)head_dim)), out, static_cast<uint8_t*>(workspace)));
+  if (!scratch || scratch_len < pyrite_cuda_attention_scratch_size(n_heads, max_ctx) || ((uintptr_t)scratch & 15))
+    return PYRITE_E_BUFFER;
+  unsigned* tickets = static_cast<unsigned*>(scratch);
+  float* parts = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + ((size_t)n_heads * 4 + 255) / 256 * 256);
+  return rc(launch_pdl(attention_step_kernel, dim3(nsplit, n_heads), dim3(256), smem, static_cast<cudaStream_t>(stream),
+                       qkv, q_norm, k_norm, n_heads, n_kv_heads, eps, pos, static_cast<const double2*>(rope_table),
+                       max_ctx, chunk, k_cache, v_cache, (float)(1.0 / sqrt((double)head_dim)), out,
+                       static_cast<uint8_t*>(workspace), tickets, parts));
 }
 
 int pyrite_cuda_silu_mul_encode(const float* gate_up, size_t f, float* act, void* workspace, size_t workspace_len,

@@ -121,6 +121,9 @@ class DenseDecoder:
         self.pos = torch.zeros(1, dtype=torch.int32, device=d)
         self.argmax_scratch = torch.zeros(max(2048, int(self.lib.pyrite_cuda_post_scratch_size())),
                                           dtype=torch.uint8, device=d)
+        self.attn_scratch = torch.zeros(int(self.lib.pyrite_cuda_attention_scratch_size(spec.num_attention_heads,
+                                                                                           max_ctx)),
+                                        dtype=torch.uint8, device=d)
         # one ticket counter per fused call site (three per layer + the LM head)
         self.tickets = torch.zeros(3 * spec.num_hidden_layers + 1, dtype=torch.int32, device=d)
         ws = lambda n: _aligned(int(self.lib.pyrite_cuda_workspace_size(0, n, 1)), d)  # noqa: E731
@@ -196,7 +199,8 @@ class DenseDecoder:
                 self.qkv.data_ptr(), ly.q_norm.data_ptr() if ly.q_norm is not None else None,
                 ly.k_norm.data_ptr() if ly.k_norm is not None else None, s.num_attention_heads,
                 s.num_key_value_heads, s.head_dim, eps, self.pos.data_ptr(), self.rope.data_ptr(), self.max_ctx,
-                self.kcache[li].data_ptr(), self.vcache[li].data_ptr(), self.attn.data_ptr(), wq, wql, stream),
+                self.kcache[li].data_ptr(), self.vcache[li].data_ptr(), self.attn.data_ptr(), wq, wql, self.attn_scratch.data_ptr(),
+                self.attn_scratch.numel(), stream),
                 "attention_step")
             self._matvec(ly.o, self.attn, "q", self.hidden, h, s.q_dim, ACCUMULATE, stream)
             _check(L.pyrite_cuda_rmsnorm_encode(self.hidden.data_ptr(), ly.ffn_norm.data_ptr(), h, eps,

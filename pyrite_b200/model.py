@@ -174,6 +174,8 @@ class MixedDecoder:
         self.tokens, self.pos = z(max_ctx, dt=torch.int32), z(1, dt=torch.int32)
         self.argmax_scratch = z(int(L.pyrite_cuda_post_scratch_size()) + 256, dt=torch.uint8)
         self.ticket = z(1, dt=torch.int32)
+        self.attn_scratch = z(int(L.pyrite_cuda_attention_scratch_size(spec.num_attention_heads, max_ctx)),
+                              dt=torch.uint8)
         # the experts each layer routed to in the latest step (rank order)
         self.route_log = z(spec.num_hidden_layers, k, dt=torch.int32) if self.moe else None
 
@@ -252,7 +254,8 @@ class MixedDecoder:
                 self.qkv.data_ptr(), ly.q_norm.data_ptr() if ly.q_norm is not None else None,
                 ly.k_norm.data_ptr() if ly.k_norm is not None else None, s.num_attention_heads,
                 s.num_key_value_heads, s.head_dim, eps, self.pos.data_ptr(), self.rope.data_ptr(), self.max_ctx,
-                self.kcache[li].data_ptr(), self.vcache[li].data_ptr(), self.attn.data_ptr(), wq, wql, stream),
+                self.kcache[li].data_ptr(), self.vcache[li].data_ptr(), self.attn.data_ptr(), wq, wql, self.attn_scratch.data_ptr(),
+                self.attn_scratch.numel(), stream),
                 "attention_step")
             self._mv(ly.o, self.attn, self.ws_q, self.hidden, ACCUMULATE, stream)
             self._norm(self.hidden, ly.ffn_norm, self.normed, self.ws_h, stream)

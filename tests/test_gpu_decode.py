@@ -62,7 +62,8 @@ def test_small_dense_decode_matches_reference(cuda_device, fused):
 
 
 def test_fused_step_equals_unfused_step(cuda_device):
-    """Post ops and the fused attention step give the one-kernel-per-op logits."""
+    """The fused step (split-context attention step, argmax post op) gives the
+    one-kernel-per-op logits and the same tokens."""
     import torch
 
     from pyrite_b200.dense import DenseDecoder
@@ -76,7 +77,8 @@ def test_fused_step_equals_unfused_step(cuda_device):
         a.run_steps(1)
         b.run_steps(1)
         torch.cuda.synchronize()
-        assert torch.allclose(a.logits, b.logits, rtol=1e-5, atol=1e-5)
+        # the split-context attention sums in another order: fp32 rounding only
+        assert torch.allclose(a.logits, b.logits, rtol=1e-4, atol=1e-3)
         assert torch.equal(a.tokens, b.tokens) and torch.equal(a.pos, b.pos)
 
 

@@ -145,3 +145,61 @@ def test_post_argmax_picks_first_maximum(cuda_device, ggml_type, rows):
     tokens.fill_(-1)
     _run_post(ggml_type, w, x, px, y, rows, cols, p)
     assert int(tokens[1].item()) == -1 and int(pos.item()) == 1
+
+
+@pytest.mark.parametrize("max_ctx,pos", [(512, 0), (512, 17), (512, 511), (4096, 2500), (4096, 63), (4096, 64)])
+def test_split_attention_step_equals_separate_kernels(cuda_device, max_ctx, pos):
+    """The context-split fused attention step (per-chunk partials merged by the
+    last CTA) against qk_rope_kv + attention over the same cache."""
+    import numpy as np
+    import torch
+
+    from pyrite_b200 import _lib
+    lib = _lib.require()
+    nq, nkv, hd = 16, 4, 128
+    g = torch.Generator("cuda").manual_seed(pos)
+    qkv = torch.randn((nq + 2 * nkv) * hd, device="cuda", generator=g)
+    qn = torch.rand(hd, device="cuda", generator=g) + 0.5
+    kn = torch.rand(hd, device="cuda", generator=g) + 0.5
+    ang = np.arange(max_ctx)[:, None] * (1e6 ** (-2.0 * np.arange(hd // 2) / hd))[None, :]
+    rope = torch.from_numpy(np.ascontiguousarray(np.stack([np.cos(ang), np.sin(ang)], -1))).cuda()
+    kc = torch.randn(max_ctx, nkv * hd, device="cuda", generator=g)
+    vc = torch.randn(max_ctx, nkv * hd, device="cuda", generator=g)
+    kc2, vc2 = kc.clone(), vc.clone()
+    p = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    # separate kernels
+    q = torch.empty(nq * hd, device="cuda")
+    ref = torch.empty(nq * hd, device="cuda")
+    assert lib.pyrite_cuda_qk_rope_kv(qkv.data_ptr(), qn.data_ptr(), kn.data_ptr(), nq, nkv, hd, 1e-6, p.data_ptr(),
+                                      rope.data_ptr(), max_ctx, q.data_ptr(), kc2.data_ptr(), vc2.data_ptr(), s) == 0
+    assert lib.pyrite_cuda_attention(q.data_ptr(), kc2.data_ptr(), vc2.data_ptr(), p.data_ptr(), nq, nkv, hd,
+                                     max_ctx, ref.data_ptr(), s) == 0 or max_ctx * 4 > 48 * 1024
+    # fused, split
+    out = torch.empty(nq * hd, device="cuda")
+    per = int(lib.pyrite_cuda_workspace_size(0, nq * hd, 1))
+    ws = torch.zeros(per + 256, dtype=torch.uint8, device="cuda")
+    off = (-ws.data_ptr()) % 256
+    scratch = torch.zeros(int(lib.pyrite_cuda_attention_scratch_size(nq, max_ctx)), dtype=torch.uint8, device="cuda")
+    for _ in range(2):  # the tickets come back to zero
+        assert lib.pyrite_cuda_attention_step(qkv.data_ptr(), qn.data_ptr(), kn.data_ptr(), nq, nkv, hd, 1e-6,
+                                              p.data_ptr(), rope.data_ptr(), max_ctx, kc.data_ptr(), vc.data_ptr(),
+                                              out.data_ptr(), ws.data_ptr() + off, ws.numel() - off,
+                                              scratch.data_ptr(), scratch.numel(), s) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    assert int(scratch[: 4 * nq].view(torch.int32).abs().sum()) == 0
+    if max_ctx * 4 <= 48 * 1024:
+        assert torch.allclose(out, ref, rtol=1e-4, atol=1e-5)
+    else:  # beyond the one-CTA kernel's shared memory: an fp64 softmax in torch
+        qh = q.view(nq, hd).double()
+        k = kc2[: pos + 1].view(pos + 1, nkv, hd).double()
+        v = vc2[: pos + 1].view(pos + 1, nkv, hd).double()
+        grp = nq // nkv
+        want = []
+        for h in range(nq):
+            sc = (k[:, h // grp] @ qh[h]) / np.sqrt(hd)
+            w = torch.softmax(sc, 0)
+            want.append(w @ v[:, h // grp])
+        want = torch.cat(want).float()
+        assert torch.allclose(out, want, rtol=1e-4, atol=1e-5)
