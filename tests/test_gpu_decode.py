@@ -114,3 +114,8 @@ def _check_mixed(golden_name, cuda_device):
 def test_llama_q4_k_m_tiny_decode_matches_reference(cuda_device):
     """configs[2]'s architecture (llama, no QK norm, untied output) and Q4_K_M mix."""
     _check_mixed("llama_tiny.json", cuda_device)
+
+
+def test_c3_llama_8b_q4_k_m_two_layers_matches_reference(cuda_device):
+    """configs[2] at full width (hidden 4096, ffn 14336, vocab 128256), 2 layers."""
+    _check_mixed("c3_2l.json", cuda_device)

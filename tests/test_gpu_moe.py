@@ -95,12 +95,16 @@ def _moe_spec(d):
     return MoESpec(**{k: v for k, v in d["spec"].items() if k in names})
 
 
-def test_tiny_moe_decode_matches_reference(cuda_device):
+@pytest.mark.parametrize("golden", ["moe_tiny.json", "moe_c4_2l.json"])
+def test_moe_decode_matches_reference(cuda_device, golden):
+    """Greedy ids, routed experts of every layer of every pass and top logits;
+    moe_c4_2l is configs[3] at full width (hidden 2048, 128 experts top-8,
+    expert ffn 768, vocab 151936) with 2 layers."""
     import torch
 
     from pyrite_b200.kernels import cuda as K
     from pyrite_b200.moe import MoEDecoder
-    g = json.loads((GOLDEN / "moe_tiny.json").read_text())
+    g = json.loads((GOLDEN / golden).read_text())
     dec = MoEDecoder.synthetic(_moe_spec(g), device=cuda_device, max_ctx=128)
     prompt, want = g["prompt"], g["generated"]
     got = dec.generate(prompt, len(want))
