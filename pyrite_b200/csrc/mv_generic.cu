@@ -49,7 +49,23 @@ mv_generic_kernel(const uint8_t* __restrict__ w, size_t row_bytes, int rows, int
     T acc[NC];
 #pragma unroll
     for (int c = 0; c < NC; ++c) acc[c] = T(0);
-    if constexpr (BS == 1) {
+    if constexpr (TY == F32) {
+      if (((uintptr_t)row & 3) == 0) {  // whole-word loads (a router, a norm-sized matrix)
+        const float* rf = reinterpret_cast<const float*>(row);
+#pragma unroll 4
+        for (int col = lane; col < cols; col += 32) {
+          const T v = (T)rf[col];
+#pragma unroll
+          for (int c = 0; c < NC; ++c) acc[c] += v * x[c * ldx + col];
+        }
+      } else {
+        for (int col = lane; col < cols; col += 32) {
+          const T v = scalar_val<TY, T>(row + (size_t)col * BPB);
+#pragma unroll
+          for (int c = 0; c < NC; ++c) acc[c] += v * x[c * ldx + col];
+        }
+      }
+    } else if constexpr (BS == 1) {
       for (int col = lane; col < cols; col += 32) {
         const T v = scalar_val<TY, T>(row + (size_t)col * BPB);
 #pragma unroll

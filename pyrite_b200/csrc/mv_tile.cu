@@ -96,6 +96,12 @@ __global__ void __launch_bounds__(256) xprep_kernel(const float* __restrict__ x,
 
 namespace {
 
+// Q6_K rows of an odd number of super-blocks (a kernel instantiation of its own).
+constexpr int kQ6KRealign = 1014;
+}  // namespace
+template <> struct Geo<1014> { static constexpr int bs = 256, bpb = 210; };
+namespace {
+
 struct XView {  // one column of prepared x (global)
   const uint8_t* q0;
   const uint8_t* q1;
@@ -333,13 +339,22 @@ struct UnitQ80 {
 // lane's digits are shifted to its block's alignment (shift_digits) and split
 // at l = 16 where the scale changes, so the 9 aligned words of each field
 // feed dp4a directly.
+//
+// REALIGN: rows of an odd number of super-blocks (row_bytes = 2 mod 4)
+// alternate between the two 2-byte alignments; a block whose alignment is not
+// the one the lane's digits were shifted for has its words realigned by 16
+// bits as they are loaded (one word of look-ahead, or of look-behind with a
+// zero first word: digit positions outside the run are zero).
+template <bool REALIGN>
 struct UnitQ6K {
   static constexpr int UPB = 4, VALS = 64;
-  // [part][group g: l<16 -> words 0..4, l>=16 -> words 4..8] x 5 words, per plane
-  struct XU { uint32_t a[2][10], b[2][10]; float s[2], m[2][2]; };
+  // [part][group g: l<16 -> words 0..4, l>=16 -> words 4..8] x 5 words, per plane;
+  // mis: the block alignment (0 or 2) the digits are shifted for
+  struct XU { uint32_t a[2][10], b[2][10]; float s[2], m[2][2]; int mis; };
   __device__ static void load_x(const XView& x, int unit, XU& u, int wmod4) {
     const int blk = unit >> 2, j = unit & 3, h = j >> 1, tt = j & 1;
-    const int mis = (wmod4 + 210 * blk) & 3;  // 0 or 2
+    const int mis = (wmod4 + 210 * blk) & 3;  // 0 or 2 (in row 0)
+    u.mis = mis;
     const uint32_t m4g0 = mis ? 0x0000FFFFu : 0u, m4g1 = mis ? 0xFFFF0000u : 0xFFFFFFFFu;
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
@@ -365,11 +380,33 @@ struct UnitQ6K {
   }
   __device__ static float dot(uint32_t blk, int j, const XU& u, int) {
     const int h = j >> 1, tt = j & 1;
-    const uint32_t aql = (blk + 64 * h + 32 * tt) & ~3u, aqh = (blk + 128 + 32 * h) & ~3u;
+    uint32_t aql = (blk + 64 * h + 32 * tt) & ~3u, aqh = (blk + 128 + 32 * h) & ~3u;
+    uint32_t sh = 0, pq = 0, ph = 0;  // realignment: shift and the word before word k
+    if constexpr (REALIGN) {
+      const bool flip = (int)(blk & 3u) != u.mis;
+      sh = flip ? 16u : 0u;
+      if (flip && u.mis == 2) {  // weights 2 bytes before the digits' positions
+        aql -= 4;
+        aqh -= 4;
+      } else {
+        pq = lds32(aql);
+        ph = lds32(aqh);
+      }
+    }
     int acc[2][2][2] = {};  // [part][group][plane]
 #pragma unroll
     for (int k = 0; k < 9; ++k) {
-      const uint32_t ql = lds32(aql + 4 * k), s = lds32(aqh + 4 * k) >> (2 * tt);
+      uint32_t ql, s;
+      if constexpr (REALIGN) {
+        const uint32_t nq = lds32(aql + 4 * k + 4), nh = lds32(aqh + 4 * k + 4);
+        ql = __funnelshift_r(pq, nq, sh);
+        s = __funnelshift_r(ph, nh, sh) >> (2 * tt);
+        pq = nq;
+        ph = nh;
+      } else {
+        ql = lds32(aql + 4 * k);
+        s = lds32(aqh + 4 * k) >> (2 * tt);
+      }
       const uint32_t c0 = (ql & 0x0F0F0F0Fu) | ((s & 0x03030303u) << 4);
       const uint32_t c1 = ((ql >> 4) & 0x0F0F0F0Fu) | (s & 0x30303030u);
       if (k <= 4) {
@@ -448,7 +485,8 @@ template <int TY> struct UnitOf;
 template <> struct UnitOf<Q4_K> { using T = UnitK45<Q4_K>; };
 template <> struct UnitOf<Q5_K> { using T = UnitK45<Q5_K>; };
 template <> struct UnitOf<Q8_0> { using T = UnitQ80; };
-template <> struct UnitOf<Q6_K> { using T = UnitQ6K; };
+template <> struct UnitOf<Q6_K> { using T = UnitQ6K<false>; };
+template <> struct UnitOf<kQ6KRealign> { using T = UnitQ6K<true>; };
 template <> struct UnitOf<IQ4_XS> { using T = UnitIQ4XS; };
 
 constexpr int kThreads = 256, kWarps = 8, kMaxRowsPerStage = 64, kStages = 3;
@@ -534,7 +572,7 @@ struct TileArgs {
 };
 
 // CTAs per SM each format's register budget allows (launch bounds).
-template <int TY> constexpr int tile_min_blocks() { return TY == Q6_K ? 2 : 3; }
+template <int TY> constexpr int tile_min_blocks() { return (TY == Q6_K || TY == kQ6KRealign) ? 2 : 3; }
 
 template <int TY, int UL, int M>
 __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kernel(TileArgs a, int* status) {
@@ -761,8 +799,10 @@ bool lane_supported(int type_id, const uint8_t* w, size_t row_bytes, int cols) {
   const uintptr_t base = (uintptr_t)w;
   switch (type_id) {
     case Q4_K: case Q5_K: return (base & 15) == 0 && (row_bytes & 15) == 0;
-    // the shifted-digit decoders need each row to keep the word alignment
-    case Q8_0: case Q6_K: return (base & 1) == 0 && (row_bytes & 3) == 0;
+    // the shifted-digit decoders need 2-byte aligned blocks; Q8_0 rows keep the
+    // word alignment, Q6_K rows may alternate (a realigning instantiation)
+    case Q8_0: return (base & 1) == 0 && (row_bytes & 3) == 0;
+    case Q6_K: return (base & 1) == 0;
     case IQ4_XS: return (base & 7) == 0;
     default: return false;
   }
@@ -797,7 +837,9 @@ int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, in
     case Q4_K: return launch_tile_type<Q4_K>(ta, p.ul, p.smem, stream);
     case Q5_K: return launch_tile_type<Q5_K>(ta, p.ul, p.smem, stream);
     case Q8_0: return launch_tile_type<Q8_0>(ta, p.ul, p.smem, stream);
-    case Q6_K: return launch_tile_type<Q6_K>(ta, p.ul, p.smem, stream);
+    case Q6_K:
+      return (row_bytes & 3) ? launch_tile_type<kQ6KRealign>(ta, p.ul, p.smem, stream)
+                             : launch_tile_type<Q6_K>(ta, p.ul, p.smem, stream);
     case IQ4_XS: return launch_tile_type<IQ4_XS>(ta, p.ul, p.smem, stream);
     default: return 1;
   }
