@@ -247,9 +247,13 @@ int pyrite_cuda_argmax_step(const float *logits, size_t n, void *scratch, size_t
  * (-probability, expert id), their weights renormalised to sum 1 when
  * norm_topk_prob, then multiplied by scale: expert_ids[top_k] and
  * expert_weights[top_k] (fp32) in device memory.  n_experts <= 4096,
- * top_k <= 32. */
+ * top_k <= 32.  Experts sharded by id over shard_count GPUs: this GPU holds
+ * experts e % shard_count == shard_index at local index e / shard_count; the
+ * others get id -1 and weight 0 (skipped by the expert matvecs and the
+ * combine).  global_ids (may be NULL) receives the global ids. */
 int pyrite_cuda_moe_route(const float *router_logits, int n_experts, int top_k, int norm_topk_prob,
-                          double scale, int *expert_ids, float *expert_weights, void *stream);
+                          double scale, int shard_count, int shard_index, int *expert_ids,
+                          float *expert_weights, int *global_ids, void *stream);
 
 /* The batch-1 product over n_sel routed slices of a stacked expert tensor in
  * one launch: `stacked` holds n_experts matrices of rows x cols back to back
@@ -259,8 +263,9 @@ int pyrite_cuda_moe_route(const float *router_logits, int n_experts, int top_k, 
  * and its encoding at workspace + j * ws_stride (strides 0: one x for all, as
  * pyrite_cuda_prepare_x writes it) -- into y + j * y_stride.  Every decodable
  * type (the batch-1 kernel where it takes the format and alignment, else the
- * generic kernel on the fp32 x); an id outside [0, n_experts) reads expert 0
- * and sets status bit 1. */
+ * generic kernel on the fp32 x); id -1 skips the slice (an expert another GPU
+ * holds); any other id outside [0, n_experts) reads expert 0 and sets status
+ * bit 1. */
 int pyrite_cuda_matvec_experts(int type_id, const void *stacked, size_t stacked_len, size_t n_experts,
                                const int *expert_ids, size_t n_sel, const float *x, size_t x_stride,
                                const void *workspace, size_t workspace_len, size_t ws_stride,

@@ -25,13 +25,17 @@ namespace pyr {
 namespace {
 
 // One CTA (256 threads): n <= 4096 router logits, k <= 32.
+// Experts sharded by id over `shards` GPUs: this one (shard `index`) holds
+// experts e % shards == index at local slot e / shards; a selected expert it
+// does not hold gets id -1 and weight 0 (the expert matvecs skip it).
 __global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict__ logits, int n, int k, int norm,
-                                                        double scale, int* __restrict__ ids,
-                                                        float* __restrict__ weights) {
+                                                        double scale, int shards, int index, int* __restrict__ ids,
+                                                        float* __restrict__ weights, int* __restrict__ global_ids) {
   __shared__ double p[4096];
   __shared__ double dred[32];
   __shared__ int wi[32];
   __shared__ double chosen_p[32];
+  __shared__ int chosen_i[32];
   pdl_wait();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // softmax in fp64 (tensor_ops.py:513-521): exp(v - max) / sum
@@ -84,7 +88,7 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict_
           bi = wi[w];
         }
       chosen_p[r] = bp;
-      ids[r] = bi;
+      chosen_i[r] = bi;
       p[bi] = -1.0;
     }
     __syncthreads();
@@ -96,7 +100,11 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict_
       double w = chosen_p[r];
       if (norm && tot > 0.0) w = w / tot;
       if (scale != 1.0) w = w * scale;
-      weights[r] = (float)w;
+      const int e = chosen_i[r];
+      const bool mine = e % shards == index;
+      ids[r] = mine ? e / shards : -1;
+      weights[r] = mine ? (float)w : 0.0f;
+      if (global_ids) global_ids[r] = e;
     }
   }
   pdl_launch_dependents();
@@ -149,12 +157,15 @@ using namespace pyr;
 extern "C" {
 
 int pyrite_cuda_moe_route(const float* router_logits, int n_experts, int top_k, int norm_topk_prob, double scale,
-                          int* expert_ids, float* expert_weights, void* stream) {
+                          int shard_count, int shard_index, int* expert_ids, float* expert_weights, int* global_ids,
+                          void* stream) {
   if (!router_logits || !expert_ids || !expert_weights || n_experts <= 0 || n_experts > 4096 || top_k <= 0 ||
-      top_k > 32 || top_k > n_experts || !(scale > 0.0))
+      top_k > 32 || top_k > n_experts || !(scale > 0.0) || shard_count <= 0 || shard_index < 0 ||
+      shard_index >= shard_count)
     return PYRITE_E_SHAPE;
   return rc(launch_pdl(moe_route_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), router_logits,
-                       n_experts, top_k, norm_topk_prob ? 1 : 0, scale, expert_ids, expert_weights));
+                       n_experts, top_k, norm_topk_prob ? 1 : 0, scale, shard_count, shard_index, expert_ids,
+                       expert_weights, global_ids));
 }
 
 int pyrite_cuda_matvec_experts(int type_id, const void* stacked, size_t stacked_len, size_t n_experts,

@@ -32,6 +32,7 @@ mv_generic_kernel(const uint8_t* __restrict__ w, size_t row_bytes, int rows, int
     pdl_wait();  // the ids come from the preceding kernel
     const int j = blockIdx.y;
     int e = ex.ids[j];
+    if (e == -1) return;  // held by another GPU
     if (e < 0 || e >= ex.n_experts) {  // never read outside the stack
       if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(status, (int)kStatusBadExpert);
       e = 0;

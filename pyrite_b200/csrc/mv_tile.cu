@@ -638,6 +638,7 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   pdl_launch_dependents();
   if (a.experts) {  // written by the routing kernel this one waited for
     int eid = a.experts[sel];
+    if (eid == -1) return;  // selected, but held by another GPU: nothing issued yet
     if (eid < 0 || eid >= a.n_experts) {  // never read outside the stack
       if (tid == 0) atomicOr(status, (int)kStatusBadExpert);
       eid = 0;

@@ -174,6 +174,7 @@ class MixedDecoder:
         self.tokens, self.pos = z(max_ctx, dt=torch.int32), z(1, dt=torch.int32)
         self.argmax_scratch = z(int(L.pyrite_cuda_post_scratch_size()) + 256, dt=torch.uint8)
         self.ticket = z(1, dt=torch.int32)
+        self.expert_shards, self.expert_shard = 1, 0  # experts by id over GPUs (sharded subclass)
         self.attn_scratch = z(int(L.pyrite_cuda_attention_scratch_size(spec.num_attention_heads, max_ctx)),
                               dt=torch.uint8)
         # the experts each layer routed to in the latest step (rank order)
@@ -274,9 +275,9 @@ class MixedDecoder:
             k = s.num_experts_per_tok
             self._mv(ly.router, self.normed, self.ws_h, self.router_logits, 0, stream)
             _check(L.pyrite_cuda_moe_route(self.router_logits.data_ptr(), s.num_experts, k,
-                                           1 if s.norm_topk_prob else 0, 1.0, self.expert_ids.data_ptr(),
-                                           self.expert_w.data_ptr(), stream), "route")
-            self.route_log[li].copy_(self.expert_ids)
+                                           1 if s.norm_topk_prob else 0, 1.0, self.expert_shards, self.expert_shard,
+                                           self.expert_ids.data_ptr(), self.expert_w.data_ptr(),
+                                           self.route_log[li].data_ptr(), stream), "route")
             self._experts(ly.gate_exps, self.normed, 0, self.ws_h, 0, self.gate, stream)
             self._experts(ly.up_exps, self.normed, 0, self.ws_h, 0, self.up, stream)
             wa, wal = self._wsp(self.ws_act)

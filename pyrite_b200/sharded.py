@@ -1,0 +1,230 @@
+"""Tensor-parallel batch-1 decode across the GPUs of one box (NCCL over NVLink).
+
+One process per GPU (``torchrun``); rank g holds the shard of every tensor that
+:mod:`pyrite_b200.shard` assigns it and runs the same decode step as
+:class:`pyrite_b200.model.MixedDecoder` on its shard, with two collectives
+per layer, both inside the step's CUDA graph:
+
+* after the attention output projection (rank g multiplied its heads' columns):
+  ``allreduce`` of the partial residual update (hidden size floats);
+* after the feed-forward down projection (its rows of gate/up, its columns of
+  down; or, for MoE, the selected experts it owns): the same ``allreduce``;
+
+and one ``all_gather`` of the LM head's logits (rows sharded by vocabulary)
+before the greedy argmax, which every rank computes identically.  Norms, the
+embedding lookup and the router are replicated.  Sums across GPUs change the
+fp32 summation order only; greedy ids are checked against the reference's.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .kernels.cuda import _check
+from .model import _Layer, _Mat, MixedDecoder
+from .shard import even_range, head_shard, owned_experts, row_bytes, slice_cols, slice_rows
+from .synthetic import F32, DenseSpec, MoESpec, dense_tensors, moe_tensors
+
+
+class ShardedDecoder(MixedDecoder):
+    """``MixedDecoder`` split over ``world`` GPUs (this process: ``rank``)."""
+
+    def __init__(self, spec: DenseSpec | MoESpec, tensors: dict[str, tuple[tuple[int, ...], int, bytes]],
+                 rank: int, world: int, device: torch.device | str = "cuda", max_ctx: int = 512,
+                 replicate: bool = False, group=None):
+        self.spec = spec
+        self.moe = isinstance(spec, MoESpec)
+        self.dev = d = torch.device(device)
+        self.max_ctx = max_ctx
+        self.lib = L = _lib.require()
+        self.rank, self.world, self.group = rank, world, group
+        h, hd = spec.hidden_size, spec.head_dim
+        hs = head_shard(spec.num_attention_heads, spec.num_key_value_heads, world, rank)
+        self.heads = hs
+
+        def src(name: str) -> str:
+            if replicate and name.startswith("blk."):
+                parts = name.split(".")
+                parts[1] = str(int(parts[1]) % 2)
+                return ".".join(parts)
+            return name
+
+        def dev(b: bytes) -> torch.Tensor:
+            return torch.frombuffer(bytearray(b), dtype=torch.uint8).to(d)
+
+        def full(name: str) -> _Mat:
+            dims, t, payload = tensors[src(name)]
+            return _Mat(t, dev(payload), int(np.prod(dims[1:])), dims[0])
+
+        def rows(name: str, r0: int, r1: int) -> _Mat:
+            dims, t, payload = tensors[src(name)]
+            return _Mat(t, dev(slice_rows(payload, t, dims[0], r0, r1)), r1 - r0, dims[0])
+
+        def cols(name: str, c0: int, c1: int) -> _Mat:
+            dims, t, payload = tensors[src(name)]
+            return _Mat(t, dev(slice_cols(payload, t, dims[1], dims[0], c0, c1)), dims[1], c1 - c0)
+
+        def f32(name: str) -> torch.Tensor:
+            dims, t, payload = tensors[src(name)]
+            if t != F32:
+                raise ValueError(f"{name} must be F32")
+            return dev(payload).view(torch.float32)
+
+        def has(name: str) -> bool:
+            return src(name) in tensors
+
+        def cat(a: _Mat, b: _Mat) -> _Mat:
+            if a.ggml_type != b.ggml_type or a.cols != b.cols:
+                raise ValueError("concatenated matrices must share a GGML type and width")
+            return _Mat(a.ggml_type, torch.cat([a.data, b.data]), a.rows + b.rows, a.cols)
+
+        self.embd = full("token_embd.weight")
+        tied = spec.tied_embeddings or "output.weight" not in tensors
+        v0, v1 = even_range(spec.vocab_size, world, rank)
+        self.vocab_rows = (v0, v1)
+        self.lm_head = rows("token_embd.weight" if tied else "output.weight", v0, v1)
+        self.out_norm = f32("output_norm.weight")
+        q0, q1 = hs.q0 * hd, (hs.q0 + hs.nq) * hd
+        k0, k1 = hs.kv0 * hd, (hs.kv0 + hs.nkv) * hd
+        self.layers: list[_Layer] = []
+        for i in range(spec.num_hidden_layers):
+            p = f"blk.{i}."
+            ly = _Layer(attn_norm=f32(p + "attn_norm.weight"), ffn_norm=f32(p + "ffn_norm.weight"),
+                        q_norm=f32(p + "attn_q_norm.weight") if has(p + "attn_q_norm.weight") else None,
+                        k_norm=f32(p + "attn_k_norm.weight") if has(p + "attn_k_norm.weight") else None,
+                        qk=cat(rows(p + "attn_q.weight", q0, q1), rows(p + "attn_k.weight", k0, k1)),
+                        v=rows(p + "attn_v.weight", k0, k1), o=cols(p + "attn_output.weight", q0, q1))
+            if self.moe:
+                E = spec.num_experts
+                mine = owned_experts(E, world, rank)
+                ly.router = full(p + "ffn_gate_inp.weight")
+                for comp in ("gate", "up", "down"):
+                    dims, t, payload = tensors[src(p + f"ffn_{comp}_exps.weight")]
+                    per = dims[1] * row_bytes(t, dims[0])
+                    local = b"".join(payload[e * per:(e + 1) * per] for e in mine)
+                    setattr(ly, f"{comp}_exps", _Mat(t, dev(local), dims[1], dims[0]))
+            else:
+                f0, f1 = even_range(spec.intermediate_size, world, rank)
+                ly.gate_up = cat(rows(p + "ffn_gate.weight", f0, f1), rows(p + "ffn_up.weight", f0, f1))
+                ly.down = cols(p + "ffn_down.weight", f0, f1)
+            self.layers.append(ly)
+
+        z = lambda *shape, dt=torch.float32: torch.zeros(*shape, dtype=dt, device=d)  # noqa: E731
+        nq_l, nkv_l = hs.nq * hd, hs.nkv * hd
+        self.hidden, self.normed, self.part = z(h), z(h), z(h)
+        self.qkv, self.attn = z(nq_l + 2 * nkv_l), z(nq_l)
+        if self.moe:
+            ff, k = spec.moe_intermediate_size, spec.num_experts_per_tok
+            self.n_local_experts = len(owned_experts(spec.num_experts, world, rank))
+            self.router_logits = z(spec.num_experts)
+            self.expert_ids, self.expert_w = z(k, dt=torch.int32), z(k)
+            self.gate, self.up, self.act, self.down = z(k, ff), z(k, ff), z(k, ff), z(k, h)
+        else:
+            ff, k = spec.intermediate_size // world, 1
+            self.gu, self.act = z(2 * ff), z(ff)
+        self.ff = ff
+        self.logits_local = z(v1 - v0)
+        self.logits = z(spec.vocab_size)
+        self.kcache = z(spec.num_hidden_layers, max_ctx, nkv_l)
+        self.vcache = torch.zeros_like(self.kcache)
+        self.tokens, self.pos = z(max_ctx, dt=torch.int32), z(1, dt=torch.int32)
+        self.argmax_scratch = z(max(2048, int(L.pyrite_cuda_post_scratch_size())), dt=torch.uint8)
+        self.ticket = z(1, dt=torch.int32)
+        self.attn_scratch = z(int(L.pyrite_cuda_attention_scratch_size(hs.nq, max_ctx)), dt=torch.uint8)
+        self.expert_shards, self.expert_shard = world, rank
+        self.route_log = z(spec.num_hidden_layers, k, dt=torch.int32) if self.moe else None
+
+        def ws(n: int, copies: int = 1) -> tuple[torch.Tensor, int, int]:
+            per = int(L.pyrite_cuda_workspace_size(0, n, 1))
+            buf = torch.empty(per * copies + 256, dtype=torch.uint8, device=d)
+            return buf, (-buf.data_ptr()) % 256, per
+
+        self.ws_h, self.ws_q, self.ws_act = ws(h), ws(nq_l), ws(ff, k)
+        half = hd // 2
+        inv = spec.rope_theta ** (-2.0 * np.arange(half, dtype=np.float64) / hd)
+        ang = np.arange(max_ctx, dtype=np.float64)[:, None] * inv[None, :]
+        self.rope = torch.from_numpy(np.ascontiguousarray(np.stack([np.cos(ang), np.sin(ang)], axis=-1))).to(d)
+        self.graph = None
+        self.prompt_len = 0
+        # the communicator is set up (and warmed) before any graph capture
+        dist.all_reduce(self.part, group=self.group)
+        torch.cuda.synchronize(d)
+
+    @classmethod
+    def synthetic(cls, spec: DenseSpec | MoESpec, rank: int, world: int, device="cuda", max_ctx: int = 512,
+                  replicate: bool = False, group=None) -> "ShardedDecoder":
+        gen_spec = spec
+        if replicate:
+            from dataclasses import replace
+            gen_spec = replace(spec, num_hidden_layers=min(2, spec.num_hidden_layers))
+        gen = moe_tensors if isinstance(spec, MoESpec) else dense_tensors
+        tensors = {name: (dims, t, payload) for name, dims, t, payload in gen(gen_spec)}
+        return cls(spec, tensors, rank, world, device=device, max_ctx=max_ctx, replicate=replicate, group=group)
+
+    # ------------------------------------------------------------------ one step
+    def _allreduce_into_hidden(self) -> None:
+        dist.all_reduce(self.part, group=self.group)
+        self.hidden.add_(self.part)
+
+    def _step(self, stream: int) -> None:
+        s, L, hs = self.spec, self.lib, self.heads
+        h, ff, hd = s.hidden_size, self.ff, s.head_dim
+        eps = float(s.rms_norm_eps)
+        qk_rows = (hs.nq + hs.nkv) * hd
+        _check(L.pyrite_cuda_embed(self.embd.ggml_type, self.embd.data.data_ptr(), s.vocab_size, h,
+                                   self.tokens.data_ptr(), self.pos.data_ptr(), self.hidden.data_ptr(), stream), "embed")
+        for li, ly in enumerate(self.layers):
+            self._norm(self.hidden, ly.attn_norm, self.normed, self.ws_h, stream)
+            self._mv(ly.qk, self.normed, self.ws_h, self.qkv, 0, stream)
+            self._mv(ly.v, self.normed, self.ws_h, self.qkv[qk_rows:], 0, stream)
+            wq, wql = self._wsp(self.ws_q)
+            _check(L.pyrite_cuda_attention_step(
+                self.qkv.data_ptr(), ly.q_norm.data_ptr() if ly.q_norm is not None else None,
+                ly.k_norm.data_ptr() if ly.k_norm is not None else None, hs.nq, hs.nkv, hd, eps,
+                self.pos.data_ptr(), self.rope.data_ptr(), self.max_ctx, self.kcache[li].data_ptr(),
+                self.vcache[li].data_ptr(), self.attn.data_ptr(), wq, wql, self.attn_scratch.data_ptr(),
+                self.attn_scratch.numel(), stream), "attention_step")
+            self._mv(ly.o, self.attn, self.ws_q, self.part, 0, stream)
+            self._allreduce_into_hidden()
+            self._norm(self.hidden, ly.ffn_norm, self.normed, self.ws_h, stream)
+            if not self.moe:
+                self._mv(ly.gate_up, self.normed, self.ws_h, self.gu, 0, stream)
+                wf, wfl = self._wsp(self.ws_act)
+                _check(L.pyrite_cuda_silu_mul_encode(self.gu.data_ptr(), ff, self.act.data_ptr(), wf, wfl, stream),
+                       "silu")
+                self._mv(ly.down, self.act, self.ws_act, self.part, 0, stream)
+            else:
+                k = s.num_experts_per_tok
+                self._mv(ly.router, self.normed, self.ws_h, self.router_logits, 0, stream)
+                _check(L.pyrite_cuda_moe_route(self.router_logits.data_ptr(), s.num_experts, k,
+                                               1 if s.norm_topk_prob else 0, 1.0, self.world, self.rank,
+                                               self.expert_ids.data_ptr(), self.expert_w.data_ptr(),
+                                               self.route_log[li].data_ptr(), stream), "route")
+                self._local_experts(ly.gate_exps, self.normed, 0, self.ws_h, 0, self.gate, stream)
+                self._local_experts(ly.up_exps, self.normed, 0, self.ws_h, 0, self.up, stream)
+                wa, wal = self._wsp(self.ws_act)
+                _check(L.pyrite_cuda_moe_silu_mul_encode(self.gate.data_ptr(), self.up.data_ptr(), ff, k,
+                                                         self.act.data_ptr(), wa, wal, stream), "moe silu")
+                self._local_experts(ly.down_exps, self.act, ff, self.ws_act, self.ws_act[2], self.down, stream)
+                self.part.zero_()
+                _check(L.pyrite_cuda_moe_combine(self.down.data_ptr(), self.expert_w.data_ptr(), k, h,
+                                                 self.part.data_ptr(), stream), "combine")
+            self._allreduce_into_hidden()
+        self._norm(self.hidden, self.out_norm, self.normed, self.ws_h, stream)
+        self._mv(self.lm_head, self.normed, self.ws_h, self.logits_local, 0, stream)
+        dist.all_gather_into_tensor(self.logits, self.logits_local, group=self.group)
+        _check(L.pyrite_cuda_argmax_step(self.logits.data_ptr(), s.vocab_size, self.argmax_scratch.data_ptr(),
+                                         self.argmax_scratch.numel(), self.tokens.data_ptr(), self.pos.data_ptr(),
+                                         self.prompt_len, self.max_ctx, stream), "argmax")
+
+    def _local_experts(self, m: _Mat, x: torch.Tensor, x_stride: int, ws, ws_stride: int, y: torch.Tensor,
+                       stream: int) -> None:
+        wptr, wlen = self._wsp(ws)
+        k = self.spec.num_experts_per_tok
+        code = self.lib.pyrite_cuda_matvec_experts(m.ggml_type, m.data.data_ptr(), m.data.numel(),
+                                                   self.n_local_experts, self.expert_ids.data_ptr(), k, x.data_ptr(),
+                                                   x_stride, wptr, wlen, ws_stride, y.data_ptr(), y.shape[1], m.rows,
+                                                   m.cols, 0, stream)
+        _check(code, "expert matvec")

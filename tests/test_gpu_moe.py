@@ -40,13 +40,20 @@ def test_route_matches_reference_order_and_weights(cuda_device, n, k, norm):
         x = torch.from_numpy(logits).cuda()
         ids = torch.zeros(k, dtype=torch.int32, device="cuda")
         w = torch.zeros(k, device="cuda")
-        assert lib.pyrite_cuda_moe_route(x.data_ptr(), n, k, 1 if norm else 0, 1.0, ids.data_ptr(), w.data_ptr(),
-                                         torch.cuda.current_stream().cuda_stream) == 0
-        torch.cuda.synchronize()
-        assert K.status() == 0
         want_ids, want_w = O.moe_route(logits.astype(np.float64), k, norm)
-        assert ids.cpu().tolist() == want_ids
-        assert np.allclose(w.cpu().numpy(), np.asarray(want_w, dtype=np.float32), rtol=1e-6, atol=0)
+        for shards in (1, 3):
+            for index in range(shards):
+                gids = torch.zeros(k, dtype=torch.int32, device="cuda")
+                assert lib.pyrite_cuda_moe_route(x.data_ptr(), n, k, 1 if norm else 0, 1.0, shards, index,
+                                                 ids.data_ptr(), w.data_ptr(), gids.data_ptr(),
+                                                 torch.cuda.current_stream().cuda_stream) == 0
+                torch.cuda.synchronize()
+                assert K.status() == 0
+                assert gids.cpu().tolist() == want_ids
+                assert ids.cpu().tolist() == [e // shards if e % shards == index else -1 for e in want_ids]
+                wl = np.asarray([v if e % shards == index else 0.0 for e, v in zip(want_ids, want_w)],
+                                dtype=np.float32)
+                assert np.allclose(w.cpu().numpy(), wl, rtol=1e-6, atol=0)
 
 
 @pytest.mark.parametrize("ggml_type,cols", [(12, 2048), (14, 768), (14, 2048), (8, 1024), (23, 512), (2, 512)])
