@@ -318,10 +318,10 @@ def run_ours(args) -> None:
     del W, X, Y
     torch.cuda.empty_cache()
     models = None
-    if rank == 0 and not args.no_models:
+    if not args.no_models:  # every rank takes part (tensor parallel when world > 1)
         models = {}
         for which in ("c3", "c4"):
-            models[which] = model_leg(dev, which)
+            models[which] = model_leg(dev, which, world, rank, pg)
             torch.cuda.empty_cache()
 
     if rank == 0:
@@ -429,7 +429,7 @@ def batched_leg(dev, W, X, wl, stream, ncols_list=(8, 64)) -> dict:
 
 
 # ---------------------------------------------------------------- model legs
-def model_leg(dev, which: str) -> dict:
+def model_leg(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
     """Batch-1 decode throughput of a full-depth configs[2] (Llama-3-8B Q4_K_M)
     or configs[3] (Qwen3-30B-A3B Q4_K_M MoE) model: the prompt is processed one
     token at a time (as the reference does), then greedy decode; one CUDA graph
@@ -437,7 +437,10 @@ def model_leg(dev, which: str) -> dict:
     1 are generated from their seeds, every other layer holds its own HBM copy
     of layer (i % 2)'s bytes (generating 8-30 B seeded values on the host would
     take minutes; the bytes streamed per token are the same).  Parity for these
-    architectures is tested on 2-layer full-width models against the reference."""
+    architectures is tested on 2-layer full-width models against the reference.
+    With several GPUs the model is split tensor-parallel over them
+    (pyrite_b200.sharded: heads / rows / experts by id, NCCL allreduce after the
+    output and down projections); the time is the max over ranks."""
     import time as _t
 
     import torch
@@ -454,13 +457,20 @@ def model_leg(dev, which: str) -> dict:
         cfg = ("configs[3]: Qwen3-30B-A3B-shaped MoE, Q4_K_M mix, 48 layers, 128 experts top-8, prefill 256 "
                "seeded tokens (one per step), batch-1 decode of 128 tokens")
     t0 = _t.time()
-    dec = MixedDecoder.synthetic(spec, device=dev, max_ctx=ctx, replicate=True)
+    if world > 1:
+        from pyrite_b200.sharded import ShardedDecoder
+        dec = ShardedDecoder.synthetic(spec, rank, world, device=dev, max_ctx=ctx, replicate=True)
+    else:
+        dec = MixedDecoder.synthetic(spec, device=dev, max_ctx=ctx, replicate=True)
     built = _t.time() - t0
     prompt = prompt_ids(spec, n=prefill)
     dec.reset(prompt)
     dec.capture()
     dec.reset(prompt)
     stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize(dev)
+    if pg:
+        pg.barrier()
     e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     e0.record(stream)
     dec.run_steps(prefill - 1)
@@ -471,24 +481,35 @@ def model_leg(dev, which: str) -> dict:
     from pyrite_b200.kernels import cuda as K
     if K.status() != 0:
         raise SystemExit(f"device status word set during the {which} model leg")
-    ms_tok = e1.elapsed_time(e2) / new
+    times = torch.tensor([e1.elapsed_time(e2), e0.elapsed_time(e1)], device=dev)
     h = spec.hidden_size
     per_layer = [ly.qk.data.numel() + ly.v.data.numel() + ly.o.data.numel() for ly in dec.layers]
-    if dec.moe:
-        k, E = spec.num_experts_per_tok, spec.num_experts
-        per_layer = [a + ly.router.data.numel() + k * (ly.gate_exps.data.numel() + ly.up_exps.data.numel()
-                                                        + ly.down_exps.data.numel()) // E
+    if dec.moe:  # the selected experts' slices (each GPU holds E / world of them)
+        k = spec.num_experts_per_tok
+        held = spec.num_experts // world
+        per_layer = [a + ly.router.data.numel() // world
+                     + k * (ly.gate_exps.data.numel() + ly.up_exps.data.numel() + ly.down_exps.data.numel())
+                     // (held * world)
                      for a, ly in zip(per_layer, dec.layers)]
     else:
         per_layer = [a + (ly.gate_up.data.numel() if ly.gate_up is not None else
                           ly.gate.data.numel() + ly.up.data.numel()) + ly.down.data.numel()
                      for a, ly in zip(per_layer, dec.layers)]
-    active = sum(per_layer) + dec.lm_head.data.numel() + h * 4
+    mine = torch.tensor([float(sum(per_layer) + dec.lm_head.data.numel() + h * 4 // world)], device=dev,
+                        dtype=torch.float64)
+    if pg:
+        pg.all_reduce(times, op=pg.ReduceOp.MAX)
+        pg.all_reduce(mine)
+    active = float(mine.item())
+    ms_tok = float(times[0].item()) / new
+    pre_ms = float(times[1].item())
+    dec.graph = None  # graphs holding NCCL calls go before the process group does
     out = {"config": cfg, "decode_tok_s": round(1000.0 / ms_tok, 1), "ms_per_token": round(ms_tok, 4),
-           "prefill_tok_s": round((prefill - 1) * 1000.0 / e0.elapsed_time(e1), 1),
+           "prefill_tok_s": round((prefill - 1) * 1000.0 / pre_ms, 1),
+           "n_gpus": world, "parallelism": f"tensor parallel x{world}" if world > 1 else "one GPU",
            "active_weight_bytes_per_token": int(active),
            "weight_GBps": round(active / (ms_tok * 1e-3) / 1e9, 1),
-           "hbm_frac_of_measured": round(active / (ms_tok * 1e-3) / 1e9 / measured_peak()[0], 4),
+           "hbm_frac_of_measured": round(active / (ms_tok * 1e-3) / 1e9 / (measured_peak()[0] * world), 4),
            "weights": "layers 0-1 generated from seeds (N(0,0.02) quantized), deeper layers: own HBM copies of them",
            "host_build_seconds": round(built, 1)}
     del dec
