@@ -94,6 +94,25 @@ typedef struct pyrite_post_op {
   int *pos;             /* ARGMAX */
 } pyrite_post_op;
 
+/* The activation of a batch-1 matvec computed inside it (every CTA encodes
+ * its own copy in shared memory) instead of by a kernel of its own: */
+#define PYRITE_X_RMSNORM 1   /* x' = x * norm_weight / sqrt(mean(x^2) + eps), fp64 statistics */
+#define PYRITE_X_SILU_MUL 2  /* x = [gate (cols) | up (cols)]: x' = silu(gate) * up */
+
+/* y = W x' for the transformed activation x' above (executor.py:621-624 then
+ * the projection; or dense.py:491-494 then the down projection).  x_out
+ * receives x' in fp32 for later consumers.  Two forms, the same results up to
+ * fp32 rounding: the batch-1 kernel's CTAs each compute x' in their prologue
+ * (one launch), or the operation's own kernel writes x_out and `workspace`
+ * (as for pyrite_cuda_matvec_prepared) and the product follows.  Given x_out
+ * and a workspace, the library picks the faster form for the size; without
+ * them only the prologue form exists (formats with the batch-1 kernel, vectors
+ * 16-byte aligned).  flags: PYRITE_F_*. */
+int pyrite_cuda_matvec_transformed(int type_id, const void *weights, size_t weights_len, const float *x,
+                                   int x_op, const float *norm_weight, double eps, float *x_out,
+                                   void *workspace, size_t workspace_len, float *y, size_t rows,
+                                   size_t cols, unsigned flags, void *stream);
+
 /* Scratch bytes PYRITE_POST_ARGMAX needs on the current device. */
 size_t pyrite_cuda_post_scratch_size(void);
 

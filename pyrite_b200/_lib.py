@@ -26,6 +26,7 @@ class PostOp(ctypes.Structure):
 
 
 POST_NONE, POST_RMSNORM_ENCODE, POST_SILU_MUL_ENCODE, POST_ARGMAX = 0, 1, 2, 3
+X_RMSNORM, X_SILU_MUL = 1, 2  # pyrite_cuda_matvec_transformed
 
 # name -> (restype, argtypes); exactly the symbols of include/pyrite_b200.h
 SIGNATURES: dict[str, tuple] = {
@@ -39,6 +40,9 @@ SIGNATURES: dict[str, tuple] = {
     "pyrite_cuda_prepare_x": (ctypes.c_int, (_VP, ctypes.c_longlong, _SZ, _SZ, _VP, _SZ, _VP)),
     "pyrite_cuda_matvec_prepared": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _VP, _SZ, _VP, _SZ, _SZ,
                                                    ctypes.c_uint, _VP)),
+    "pyrite_cuda_matvec_transformed": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, ctypes.c_int, _VP,
+                                                      ctypes.c_double, _VP, _VP, _SZ, _VP, _SZ, _SZ, ctypes.c_uint,
+                                                      _VP)),
     "pyrite_cuda_post_scratch_size": (_SZ, ()),
     "pyrite_cuda_matvec_prepared_post": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _VP, _SZ, _VP, _SZ, _SZ,
                                                         ctypes.c_uint, ctypes.POINTER(PostOp), _VP)),

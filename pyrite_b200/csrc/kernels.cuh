@@ -98,9 +98,19 @@ struct ExpertArgs {
   int n_experts, n_sel;
   long long expert_bytes, ws_stride, y_stride;
 };
+// The activation computed in every CTA's prologue instead of a prepared
+// workspace: mode 1 RMSNorm of src with weight norm, mode 2 silu(src[:cols]) *
+// src[cols:]; CTA 0 also stores the fp32 activation to out (may be NULL).
+struct XPrologue {
+  int mode;
+  const float* src;
+  const float* norm;
+  double eps;
+  float* out;
+};
 int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const uint8_t* ws,
                    float* y, bool static_weights, cudaStream_t stream, bool accumulate = false,
-                   const PostArgs* post = nullptr, const ExpertArgs* ex = nullptr);
+                   const PostArgs* post = nullptr, const ExpertArgs* ex = nullptr, const XPrologue* xp = nullptr);
 // Largest grid launch_mv_lane uses (argmax partial slots needed).
 int lane_max_grid();
 

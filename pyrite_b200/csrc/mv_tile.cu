@@ -75,12 +75,8 @@ __global__ void __launch_bounds__(256) xprep_kernel(const float* __restrict__ x,
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float s = amax / 127.0f;
-    int d0 = 0, d1 = 0;
-    if (s > 0.0f) {
-      const float t = v / s;
-      d0 = max(-127, min(127, (int)rintf(t)));
-      d1 = max(-127, min(127, (int)rintf((t - (float)d0) * 254.0f)));
-    }
+    int d0, d1;
+    two_digits(v, digit_ratio(amax), d0, d1);
     float s16 = v;
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
@@ -102,7 +98,7 @@ constexpr int kQ6KRealign = 1014;
 template <> struct Geo<1014> { static constexpr int bs = 256, bpb = 210; };
 namespace {
 
-struct XView {  // one column of prepared x (global)
+struct XView {  // one column of prepared x (global, or this CTA's shared copy)
   const uint8_t* q0;
   const uint8_t* q1;
   const float* scale;
@@ -120,8 +116,8 @@ __device__ __forceinline__ XView xview(const uint8_t* ws, int cols) {
 struct Dig16 { uint4 a, b; };  // 16 digits of each plane
 __device__ __forceinline__ Dig16 dig16(const XView& x, int c) {
   Dig16 d;
-  d.a = __ldg(reinterpret_cast<const uint4*>(x.q0 + c));
-  d.b = __ldg(reinterpret_cast<const uint4*>(x.q1 + c));
+  d.a = *reinterpret_cast<const uint4*>(x.q0 + c);
+  d.b = *reinterpret_cast<const uint4*>(x.q1 + c);
   return d;
 }
 // 254 * dot(codes, x0) + dot(codes, x1) over 16 values, exact in int32
@@ -231,11 +227,11 @@ template <int TY> struct UnitK45 {
     const int ca = 256 * (unit >> 2) + 64 * (unit & 3), cb = ca + 32;
     dig32(x, ca, u.a);
     dig32(x, cb, u.b);
-    u.sa = __ldg(x.scale + (ca >> 5));
+    u.sa = *(x.scale + (ca >> 5));
     // Q4_K multiplies the high nibbles in place (16 * code): fold the 1/16 here
-    u.sb = __ldg(x.scale + (cb >> 5)) * (TY == Q4_K ? 0.0625f : 1.0f);
-    u.ma = __ldg(x.sum16 + (ca >> 4)) + __ldg(x.sum16 + (ca >> 4) + 1);
-    u.mb = __ldg(x.sum16 + (cb >> 4)) + __ldg(x.sum16 + (cb >> 4) + 1);
+    u.sb = *(x.scale + (cb >> 5)) * (TY == Q4_K ? 0.0625f : 1.0f);
+    u.ma = *(x.sum16 + (ca >> 4)) + *(x.sum16 + (ca >> 4) + 1);
+    u.mb = *(x.sum16 + (cb >> 4)) + *(x.sum16 + (cb >> 4) + 1);
   }
   __device__ static float dot(uint32_t blk, int p, const XU& u, int) {
     const uint4 hdr = lds128(blk);
@@ -309,7 +305,7 @@ struct UnitQ80 {
     shift_digits(w, mis, u.a);
     words8(lo, hi, true, w);
     shift_digits(w, mis, u.b);
-    u.s = __ldg(x.scale + unit);
+    u.s = *(x.scale + unit);
   }
   __device__ static float dot(uint32_t blk, int, const XU& u, int) {
     const uint32_t base = (blk + 2) & ~3u;
@@ -373,9 +369,9 @@ struct UnitQ6K {
 #pragma unroll
         for (int k = 5; k < 9; ++k) dst[k + 1] = sw[k];
       }
-      u.s[p] = __ldg(x.scale + (c >> 5));
-      u.m[p][0] = __ldg(x.sum16 + (c >> 4));
-      u.m[p][1] = __ldg(x.sum16 + (c >> 4) + 1);
+      u.s[p] = *(x.scale + (c >> 5));
+      u.m[p][0] = *(x.sum16 + (c >> 4));
+      u.m[p][1] = *(x.sum16 + (c >> 4) + 1);
     }
   }
   __device__ static float dot(uint32_t blk, int j, const XU& u, int) {
@@ -454,7 +450,7 @@ struct UnitIQ4XS {
       u.b[2 * k] = __byte_perm(w4(lo.b, k), w4(hi.b, k), 0x5140);
       u.b[2 * k + 1] = __byte_perm(w4(lo.b, k), w4(hi.b, k), 0x7362);
     }
-    u.s = __ldg(x.scale + unit);
+    u.s = *(x.scale + unit);
   }
   __device__ static float dot(uint32_t blk, int j, const XU& u, int) {
     const uint2 hdr = lds64(blk);  // d | scales_h | scales_l[4]
@@ -569,6 +565,16 @@ struct TileArgs {
   const int* experts;
   int n_experts, n_sel;
   long long expert_bytes, ws_stride, y_stride;
+  // x prologue (xmode != 0): every CTA encodes its own copy of x into shared
+  // memory from fp32 input instead of reading a prepared workspace --
+  // 1: x = xsrc * xnorm / rms(xsrc) (fp64 statistics), 2: x = silu(xsrc[0:cols])
+  // * xsrc[cols:2 cols]; CTA 0 also writes the fp32 x to xout when non-null
+  int xmode;
+  const float* xsrc;
+  const float* xnorm;
+  double xeps;
+  float* xout;
+  int xenc_off;  // byte offset of the shared copy in the dynamic shared memory
 };
 
 // CTAs per SM each format's register budget allows (launch bounds).
@@ -597,18 +603,6 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   const uint8_t* wb = a.w;  // this CTA's matrix (an expert's: set once its id is readable)
   const uint32_t ring = smem_addr(smem);
   const size_t stage_stride = (size_t)rows_per_stage * a.row_bytes;
-
-  // this lane's units (inactive ones point at block 0 and are masked out, so
-  // every lane runs the same instructions -- the K-quant decode shuffles)
-  int uoff[UL], uj[UL];
-  float uon[UL];
-#pragma unroll
-  for (int k = 0; k < UL; ++k) {
-    const int u = ls + k * lps;
-    uon[k] = u < units ? 1.f : 0.f;
-    uoff[k] = u < units ? (u / U::UPB) * BPB : 0;
-    uj[k] = u < units ? u % U::UPB : 0;
-  }
 
   auto stage_rows = [&](int st) { return min(rows_per_stage, a.rows - st * rows_per_stage); };
   // the CTA's k-th stage -> ring slot k % S, one bulk copy of its contiguous bytes
@@ -650,8 +644,29 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   if (!early && tid == 0)
     for (int k = 0; k < min(my, S - 1); ++k) issue(k);
 
+  const uint8_t* xws = a.ws + (size_t)sel * (size_t)a.ws_stride;
+  if (a.xmode) {  // this CTA's own encoding of x (the input was written by the preceding kernel)
+    __shared__ double xshm[32];
+    uint8_t* enc = smem + a.xenc_off;
+    float* xo = blockIdx.x == 0 ? a.xout : nullptr;
+    if (a.xmode == 1) cta_rmsnorm_encode(a.xsrc, a.xnorm, a.cols, a.xeps, xo, enc, xshm);
+    else cta_silu_mul_encode(a.xsrc, a.cols, xo, enc);
+    __syncthreads();
+    xws = enc;
+  }
+  // this lane's units (inactive ones point at block 0 and are masked out, so
+  // every lane runs the same instructions -- the K-quant decode shuffles)
+  int uoff[UL], uj[UL];
+  float uon[UL];
+#pragma unroll
+  for (int k = 0; k < UL; ++k) {
+    const int u = ls + k * lps;
+    uon[k] = u < units ? 1.f : 0.f;
+    uoff[k] = u < units ? (u / U::UPB) * BPB : 0;
+    uj[k] = u < units ? u % U::UPB : 0;
+  }
   typename U::XU xu[UL];  // this lane's x, for the whole kernel
-  const XView xv = xview(a.ws + (size_t)sel * (size_t)a.ws_stride, a.cols);
+  const XView xv = xview(xws, a.cols);
 #pragma unroll
   for (int k = 0; k < UL; ++k) U::load_x(xv, ls + k * lps < units ? ls + k * lps : 0, xu[k], wmod4);
 
@@ -714,9 +729,9 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   if (a.post.op != kPostNone) run_post(a.post, a.y, a.rows, best_v, best_i);
 }
 
-struct TilePlan { int rs_log2, m, stage_bytes, ul; size_t smem; };
+struct TilePlan { int rs_log2, m, stage_bytes, ul; size_t smem; int xenc_off; };
 
-TilePlan plan_tile(size_t row_bytes, int rows, int cols, int vals) {
+TilePlan plan_tile(size_t row_bytes, int rows, int cols, int vals, size_t xenc_bytes) {
   TilePlan p{};
   const int units = cols / vals;
   int pow2 = 32;
@@ -737,6 +752,10 @@ TilePlan plan_tile(size_t row_bytes, int rows, int cols, int vals) {
   const size_t sb = ((size_t)rs * p.m * row_bytes + 16 + 32 + 127) & ~(size_t)127;
   p.stage_bytes = (int)sb;
   p.smem = (size_t)kStages * sb + 2 * kWarps * p.m * sizeof(float) + (size_t)kStages * 8;
+  if (xenc_bytes) {
+    p.xenc_off = (int)((p.smem + 255) & ~(size_t)255);
+    p.smem = (size_t)p.xenc_off + xenc_bytes;
+  }
   return p;
 }
 
@@ -748,7 +767,7 @@ int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
   static int sms[64] = {};
   static bool smem_set[64] = {};
   if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-  constexpr int kMaxSmem = 110 * 1024;
+  constexpr int kMaxSmem = 150 * 1024;
   if (!smem_set[dev]) {
     if (cudaFuncSetAttribute(mv_tile_kernel<TY, UL, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
         cudaSuccess)
@@ -820,11 +839,14 @@ int launch_xprep(const float* x, long long ldx, int cols, int ncols, uint8_t* ws
 
 int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const uint8_t* ws,
                    float* y, bool static_weights, cudaStream_t stream, bool accumulate, const PostArgs* post,
-                   const ExpertArgs* ex) {
+                   const ExpertArgs* ex, const XPrologue* xp) {
   const int vals = (type_id == Q6_K || type_id == Q4_K || type_id == Q5_K) ? 64 : 32;
-  const TilePlan p = plan_tile(row_bytes, rows, cols, vals);
+  const size_t xenc = xp ? ((lane_workspace_bytes(cols) + 255) & ~(size_t)255) : 0;
+  const TilePlan p = plan_tile(row_bytes, rows, cols, vals, xenc);
   TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs_log2, p.m, p.stage_bytes, static_weights ? 1 : 0,
-              accumulate ? 1 : 0, post ? *post : PostArgs{}, nullptr, 0, 0, 0, 0, 0};
+              accumulate ? 1 : 0, post ? *post : PostArgs{}, nullptr, 0, 0, 0, 0, 0,
+              xp ? xp->mode : 0, xp ? xp->src : nullptr, xp ? xp->norm : nullptr, xp ? xp->eps : 0.0,
+              xp ? xp->out : nullptr, p.xenc_off};
   if (ex) {
     ta.experts = ex->ids;
     ta.n_experts = ex->n_experts;

@@ -8,19 +8,27 @@
 
 namespace pyr {
 
+// The two int8 digits of v in a 32-value block of largest magnitude amax:
+// t = v * r with r = 127 / amax (0 for an all-zero block), d0 = rint(t),
+// d1 = rint((t - d0) * 254), so v ~ (d0 + d1 / 254) * amax / 127.  No clamp is
+// needed: |t| rounds to at most 127 and |t - d0| <= 1/2.
+__device__ __forceinline__ float digit_ratio(float amax) { return amax > 0.0f ? 127.0f / amax : 0.0f; }
+__device__ __forceinline__ void two_digits(float v, float r, int& d0, int& d1) {
+  const float t = v * r;
+  d0 = __float2int_rn(t);
+  d1 = __float2int_rn((t - (float)d0) * 254.0f);
+}
+
 // Encode 32 values (lane l holds value l of block b) into the prepared-x
-// layout of mv_tile.cu: digits x0, x1, scale s/254, and the two 16-value sums.
+// layout of mv_tile.cu: digits x0, x1, scale s/254 (s = amax / 127), and the
+// two 16-value sums.
 __device__ __forceinline__ void encode_block(float v, int lane, int b, int cols, uint8_t* ws) {
   float amax = fabsf(v);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   const float s = amax / 127.0f;
-  int d0 = 0, d1 = 0;
-  if (s > 0.0f) {
-    const float t = v / s;
-    d0 = max(-127, min(127, (int)rintf(t)));
-    d1 = max(-127, min(127, (int)rintf((t - (float)d0) * 254.0f)));
-  }
+  int d0, d1;
+  two_digits(v, digit_ratio(amax), d0, d1);
   float s16 = v;
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
@@ -78,8 +86,147 @@ __device__ __forceinline__ void warps_silu_mul_encode(const float* gu, int f, fl
     const float g = __ldcg(gu + i), u = __ldcg(gu + f + i);
     const float sg = g > -60.0f ? g / (1.0f + expf(-g)) : 0.0f;
     const float v = sg * u;
-    act[i] = v;
+    if (act) act[i] = v;
     encode_block(v, lane, b, f, ws);
+  }
+}
+
+// ---- the same encodings for a matvec CTA's prologue -------------------------
+// Every CTA of a matvec that computes its own x' encodes the whole vector, so
+// the work is laid out for latency: thread t takes the 16-value groups
+// g = t, t + blockDim.x, ... as four float4 loads; a 32-value block is the
+// group pair (2b, 2b + 1), held by adjacent lanes.  Per value the arithmetic is
+// encode_block's, and the 16-value sums add in the order of its shuffle tree
+// (offsets 8, 4, 2, 1), so the bytes equal those of the kernels above for the
+// same input values.
+
+// Encode group g (values v): both lanes of a pair call this together (the
+// amax exchange is a shuffle), `on` equal for the pair.
+__device__ __forceinline__ void encode_group(const float (&v)[16], int g, int cols, bool on, uint8_t* enc,
+                                             float* out) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  const float s = amax / 127.0f, r = digit_ratio(amax);
+  uint32_t p0[4], p1[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    p0[q] = 0u;
+    p1[q] = 0u;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int d0, d1;
+      two_digits(v[4 * q + j], r, d0, d1);
+      p0[q] |= ((uint32_t)d0 & 0xffu) << (8 * j);
+      p1[q] |= ((uint32_t)d1 & 0xffu) << (8 * j);
+    }
+  }
+  float a8[8], a4[4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a8[i] = v[i] + v[i + 8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) a4[i] = a8[i] + a8[i + 4];
+  const float s16 = (a4[0] + a4[2]) + (a4[1] + a4[3]);
+  if (!on) return;
+  *reinterpret_cast<uint4*>(enc + 16 * g) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
+  *reinterpret_cast<uint4*>(enc + cols + 16 * g) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+  float* scale = reinterpret_cast<float*>(enc + 2 * cols);
+  if ((g & 1) == 0) scale[g >> 1] = s / 254.0f;
+  scale[cols / 32 + g] = s16;
+  if (out) {
+    float4* o = reinterpret_cast<float4*>(out + 16 * g);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  }
+}
+
+__device__ __forceinline__ void load16(const float* p, float (&v)[16]) {  // through L2: p may be fresh
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 t = __ldcg(q + i);
+    v[4 * i] = t.x;
+    v[4 * i + 1] = t.y;
+    v[4 * i + 2] = t.z;
+    v[4 * i + 3] = t.w;
+  }
+}
+
+// block_rmsnorm_encode for a CTA prologue (x, w 16-byte aligned, n % 32 == 0).
+// Each thread's first group of x and w stays in registers, so for n up to
+// 16 * blockDim.x the statistics and the encoding cost one round trip to L2.
+__device__ __forceinline__ void cta_rmsnorm_encode(const float* x, const float* w, int n, double eps, float* out,
+                                                   uint8_t* enc, double* shm) {
+  const int G = n / 16, nt = blockDim.x, tid = threadIdx.x;
+  float4 x0[4], w0[4];
+  double ss = 0.0;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    x0[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    w0[q] = x0[q];
+  }
+  if (tid < G) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      x0[q] = __ldcg(reinterpret_cast<const float4*>(x + 16 * tid) + q);
+      w0[q] = __ldg(reinterpret_cast<const float4*>(w + 16 * tid) + q);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    ss += (double)x0[q].x * x0[q].x + (double)x0[q].y * x0[q].y + (double)x0[q].z * x0[q].z +
+          (double)x0[q].w * x0[q].w;
+  for (int g = tid + nt; g < G; g += nt) {
+    float v[16];
+    load16(x + 16 * g, v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) ss += (double)v[i] * (double)v[i];
+  }
+  const double total = block_sum(ss, shm);
+  const double inv = 1.0 / sqrt(total / (double)(n > 0 ? n : 1) + eps);
+  for (int g0 = 0; g0 < G; g0 += nt) {  // same trip count in every thread
+    const int g = g0 + tid;
+    const bool on = g < G;
+    float v[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float4 xv = x0[q], wv = w0[q];
+      if (g0 > 0 && on) {
+        xv = __ldcg(reinterpret_cast<const float4*>(x + 16 * g) + q);
+        wv = __ldg(reinterpret_cast<const float4*>(w + 16 * g) + q);
+      }
+      v[4 * q] = (float)((double)xv.x * inv * (double)wv.x);
+      v[4 * q + 1] = (float)((double)xv.y * inv * (double)wv.y);
+      v[4 * q + 2] = (float)((double)xv.z * inv * (double)wv.z);
+      v[4 * q + 3] = (float)((double)xv.w * inv * (double)wv.w);
+    }
+    encode_group(v, g, n, on, enc, out);
+  }
+}
+
+// warps_silu_mul_encode for a CTA prologue (gu 16-byte aligned, f % 32 == 0).
+__device__ __forceinline__ void cta_silu_mul_encode(const float* gu, int f, float* out, uint8_t* enc) {
+  const int G = f / 16, nt = blockDim.x;
+  for (int g0 = 0; g0 < G; g0 += nt) {
+    const int g = g0 + threadIdx.x;
+    const bool on = g < G;
+    float v[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float4 gv = make_float4(0.f, 0.f, 0.f, 0.f), uv = gv;
+      if (on) {
+        gv = __ldcg(reinterpret_cast<const float4*>(gu + 16 * g) + q);
+        uv = __ldcg(reinterpret_cast<const float4*>(gu + f + 16 * g) + q);
+      }
+      const float ga[4] = {gv.x, gv.y, gv.z, gv.w}, ua[4] = {uv.x, uv.y, uv.z, uv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float sg = ga[j] > -60.0f ? ga[j] / (1.0f + expf(-ga[j])) : 0.0f;
+        v[4 * q + j] = sg * ua[j];
+      }
+    }
+    encode_group(v, g, f, on, enc, out);
   }
 }
 

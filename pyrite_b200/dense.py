@@ -19,13 +19,17 @@ B200 layout choices:
     sequence of launches, captured once in a CUDA graph and replayed for the
     whole prompt (processed one token at a time, as the reference does) and
     every generated token, with no host synchronisation in between.
-  * Fused step (default): q/k norm, RoPE, KV append, attention and the
-    encoding of its output run as one kernel, and the greedy argmax runs in
-    the last CTA of the LM-head matvec (a post op).  The RMSNorms and SwiGLU
-    stay kernels of their own: run as post ops in the last CTA of their
-    producer they cost more than a launch (measured on B200: 256 threads
-    serialise work a 1024-thread kernel does at once).  ``fused=False`` keeps
-    one launch per operation (same results).
+  * Fused step (default): the RMSNorm before a projection and the SwiGLU
+    before the down projection go through ``pyrite_cuda_matvec_transformed``,
+    which computes them in the projection's own prologue (every CTA encodes
+    its copy of the activation in shared memory) where that is faster than a
+    kernel of their own (norms over 4096 values and more); q/k norm, RoPE, KV
+    append, attention and the encoding of its output run as one kernel; the
+    greedy argmax runs in the last CTA of the LM-head matvec (a post op).
+    (The norms as post ops in the last CTA of their producer were measured
+    slower than their own kernels: one CTA serialises the work.)
+    ``fused=False`` keeps one launch per operation (same results up to fp32
+    rounding).
 """
 from __future__ import annotations
 
@@ -182,6 +186,16 @@ class DenseDecoder:
                                                          ctypes.byref(post), stream)
         _check(code, "matvec+post")
 
+    def _matvec_x(self, w: torch.Tensor, x: torch.Tensor, x_op: int, norm: torch.Tensor | None, ws: str,
+                  x_out: torch.Tensor, y: torch.Tensor, rows: int, cols: int, flags: int, stream: int) -> None:
+        """y (+)= W x' with x' = RMSNorm(x) or SiLU(gate) * up computed inside the matvec."""
+        wptr, wlen = self._ws(ws)
+        code = self.lib.pyrite_cuda_matvec_transformed(
+            self.wtype, w.data_ptr(), w.numel(), x.data_ptr(), x_op, norm.data_ptr() if norm is not None else None,
+            float(self.spec.rms_norm_eps), x_out.data_ptr(), wptr, wlen, y.data_ptr(), rows, cols,
+            flags | STATIC_WEIGHTS, stream)
+        _check(code, "matvec+x")
+
     def _step_fused(self, stream: int) -> None:
         s, L = self.spec, self.lib
         h, f = s.hidden_size, s.intermediate_size
@@ -189,29 +203,24 @@ class DenseDecoder:
         nl = len(self.layers)
         _check(L.pyrite_cuda_embed(self.wtype, self.embd.data_ptr(), s.vocab_size, h, self.tokens.data_ptr(),
                                    self.pos.data_ptr(), self.hidden.data_ptr(), stream), "embed")
-        wh, whl = self._ws("h")
-        _check(L.pyrite_cuda_rmsnorm_encode(self.hidden.data_ptr(), self.layers[0].attn_norm.data_ptr(), h, eps,
-                                            self.normed.data_ptr(), wh, whl, stream), "rmsnorm")
         for li, ly in enumerate(self.layers):
-            self._matvec(ly.qkv, self.normed, "h", self.qkv, s.q_dim + 2 * s.kv_dim, h, 0, stream)
+            self._matvec_x(ly.qkv, self.hidden, _lib.X_RMSNORM, ly.attn_norm, "h", self.normed, self.qkv,
+                           s.q_dim + 2 * s.kv_dim, h, 0, stream)
             wq, wql = self._ws("q")
             _check(L.pyrite_cuda_attention_step(
                 self.qkv.data_ptr(), ly.q_norm.data_ptr() if ly.q_norm is not None else None,
                 ly.k_norm.data_ptr() if ly.k_norm is not None else None, s.num_attention_heads,
                 s.num_key_value_heads, s.head_dim, eps, self.pos.data_ptr(), self.rope.data_ptr(), self.max_ctx,
-                self.kcache[li].data_ptr(), self.vcache[li].data_ptr(), self.attn.data_ptr(), wq, wql, self.attn_scratch.data_ptr(),
-                self.attn_scratch.numel(), stream),
-                "attention_step")
+                self.kcache[li].data_ptr(), self.vcache[li].data_ptr(), self.attn.data_ptr(), wq, wql,
+                self.attn_scratch.data_ptr(), self.attn_scratch.numel(), stream), "attention_step")
             self._matvec(ly.o, self.attn, "q", self.hidden, h, s.q_dim, ACCUMULATE, stream)
-            _check(L.pyrite_cuda_rmsnorm_encode(self.hidden.data_ptr(), ly.ffn_norm.data_ptr(), h, eps,
-                                                self.normed.data_ptr(), wh, whl, stream), "rmsnorm")
-            self._matvec(ly.gate_up, self.normed, "h", self.gu, 2 * f, h, 0, stream)
-            wf, wfl = self._ws("f")
-            _check(L.pyrite_cuda_silu_mul_encode(self.gu.data_ptr(), f, self.act.data_ptr(), wf, wfl, stream), "silu")
-            nxt = self.layers[li + 1].attn_norm if li + 1 < nl else self.out_norm
-            self._matvec(ly.down, self.act, "f", self.hidden, h, f, ACCUMULATE, stream)
-            _check(L.pyrite_cuda_rmsnorm_encode(self.hidden.data_ptr(), nxt.data_ptr(), h, eps,
-                                                self.normed.data_ptr(), wh, whl, stream), "rmsnorm")
+            self._matvec_x(ly.gate_up, self.hidden, _lib.X_RMSNORM, ly.ffn_norm, "h", self.normed, self.gu,
+                           2 * f, h, 0, stream)
+            self._matvec_x(ly.down, self.gu, _lib.X_SILU_MUL, None, "f", self.act, self.hidden, h, f, ACCUMULATE,
+                           stream)
+        wh, whl = self._ws("h")
+        _check(L.pyrite_cuda_rmsnorm_encode(self.hidden.data_ptr(), self.out_norm.data_ptr(), h, eps,
+                                            self.normed.data_ptr(), wh, whl, stream), "rmsnorm")
         self._matvec_post(self.lm_head, self.normed, "h", self.logits, s.vocab_size, h, 0,
                           self._post(_lib.POST_ARGMAX, 3 * nl), stream)
 

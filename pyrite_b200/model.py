@@ -224,6 +224,16 @@ class MixedDecoder:
                                                              flags | STATIC_WEIGHTS, ctypes.byref(post), stream)
         _check(code, "matvec")
 
+    def _mvx(self, m: _Mat, x: torch.Tensor, x_op: int, norm: torch.Tensor | None, x_out: torch.Tensor, ws,
+             y: torch.Tensor, flags: int, stream: int) -> None:
+        """y (+)= W x' with x' = RMSNorm(x) or SiLU(gate) * up computed inside the matvec."""
+        wptr, wlen = self._wsp(ws)
+        code = self.lib.pyrite_cuda_matvec_transformed(
+            m.ggml_type, m.data.data_ptr(), m.data.numel(), x.data_ptr(), x_op,
+            norm.data_ptr() if norm is not None else None, float(self.spec.rms_norm_eps), x_out.data_ptr(), wptr,
+            wlen, y.data_ptr(), m.rows, m.cols, flags | STATIC_WEIGHTS, stream)
+        _check(code, "matvec+x")
+
     def _experts(self, m: _Mat, x: torch.Tensor, x_stride: int, ws, ws_stride: int, y: torch.Tensor,
                  stream: int) -> None:
         wptr, wlen = self._wsp(ws)
@@ -247,9 +257,9 @@ class MixedDecoder:
         _check(L.pyrite_cuda_embed(self.embd.ggml_type, self.embd.data.data_ptr(), s.vocab_size, h,
                                    self.tokens.data_ptr(), self.pos.data_ptr(), self.hidden.data_ptr(), stream), "embed")
         for li, ly in enumerate(self.layers):
-            self._norm(self.hidden, ly.attn_norm, self.normed, self.ws_h, stream)
-            self._mv(ly.qk, self.normed, self.ws_h, self.qkv, 0, stream)
-            self._mv(ly.v, self.normed, self.ws_h, self.qkv[qk_rows:], 0, stream)
+            self._mvx(ly.qk, self.hidden, _lib.X_RMSNORM, ly.attn_norm, self.normed, self.ws_h, self.qkv, 0, stream)
+            self._mvx(ly.v, self.hidden, _lib.X_RMSNORM, ly.attn_norm, self.normed, self.ws_h, self.qkv[qk_rows:], 0,
+                      stream)
             wq, wql = self._wsp(self.ws_q)
             _check(L.pyrite_cuda_attention_step(
                 self.qkv.data_ptr(), ly.q_norm.data_ptr() if ly.q_norm is not None else None,
@@ -259,18 +269,17 @@ class MixedDecoder:
                 self.attn_scratch.numel(), stream),
                 "attention_step")
             self._mv(ly.o, self.attn, self.ws_q, self.hidden, ACCUMULATE, stream)
-            self._norm(self.hidden, ly.ffn_norm, self.normed, self.ws_h, stream)
-            if not self.moe:  # SwiGLU feed-forward
+            if not self.moe:  # SwiGLU feed-forward, norm and SiLU in the projections' prologues
+                X = _lib.X_RMSNORM
                 if ly.gate_up is not None:
-                    self._mv(ly.gate_up, self.normed, self.ws_h, self.gu, 0, stream)
+                    self._mvx(ly.gate_up, self.hidden, X, ly.ffn_norm, self.normed, self.ws_h, self.gu, 0, stream)
                 else:
-                    self._mv(ly.gate, self.normed, self.ws_h, self.gu[:ff], 0, stream)
-                    self._mv(ly.up, self.normed, self.ws_h, self.gu[ff:], 0, stream)
-                wf, wfl = self._wsp(self.ws_act)
-                _check(L.pyrite_cuda_silu_mul_encode(self.gu.data_ptr(), ff, self.act.data_ptr(), wf, wfl, stream),
-                       "silu")
-                self._mv(ly.down, self.act, self.ws_act, self.hidden, ACCUMULATE, stream)
+                    self._mvx(ly.gate, self.hidden, X, ly.ffn_norm, self.normed, self.ws_h, self.gu[:ff], 0, stream)
+                    self._mvx(ly.up, self.hidden, X, ly.ffn_norm, self.normed, self.ws_h, self.gu[ff:], 0, stream)
+                self._mvx(ly.down, self.gu, _lib.X_SILU_MUL, None, self.act, self.ws_act, self.hidden, ACCUMULATE,
+                          stream)
                 continue
+            self._norm(self.hidden, ly.ffn_norm, self.normed, self.ws_h, stream)
             # routed feed-forward
             k = s.num_experts_per_tok
             self._mv(ly.router, self.normed, self.ws_h, self.router_logits, 0, stream)

@@ -176,9 +176,9 @@ class ShardedDecoder(MixedDecoder):
         _check(L.pyrite_cuda_embed(self.embd.ggml_type, self.embd.data.data_ptr(), s.vocab_size, h,
                                    self.tokens.data_ptr(), self.pos.data_ptr(), self.hidden.data_ptr(), stream), "embed")
         for li, ly in enumerate(self.layers):
-            self._norm(self.hidden, ly.attn_norm, self.normed, self.ws_h, stream)
-            self._mv(ly.qk, self.normed, self.ws_h, self.qkv, 0, stream)
-            self._mv(ly.v, self.normed, self.ws_h, self.qkv[qk_rows:], 0, stream)
+            self._mvx(ly.qk, self.hidden, _lib.X_RMSNORM, ly.attn_norm, self.normed, self.ws_h, self.qkv, 0, stream)
+            self._mvx(ly.v, self.hidden, _lib.X_RMSNORM, ly.attn_norm, self.normed, self.ws_h, self.qkv[qk_rows:], 0,
+                      stream)
             wq, wql = self._wsp(self.ws_q)
             _check(L.pyrite_cuda_attention_step(
                 self.qkv.data_ptr(), ly.q_norm.data_ptr() if ly.q_norm is not None else None,
@@ -188,14 +188,12 @@ class ShardedDecoder(MixedDecoder):
                 self.attn_scratch.numel(), stream), "attention_step")
             self._mv(ly.o, self.attn, self.ws_q, self.part, 0, stream)
             self._allreduce_into_hidden()
-            self._norm(self.hidden, ly.ffn_norm, self.normed, self.ws_h, stream)
             if not self.moe:
-                self._mv(ly.gate_up, self.normed, self.ws_h, self.gu, 0, stream)
-                wf, wfl = self._wsp(self.ws_act)
-                _check(L.pyrite_cuda_silu_mul_encode(self.gu.data_ptr(), ff, self.act.data_ptr(), wf, wfl, stream),
-                       "silu")
-                self._mv(ly.down, self.act, self.ws_act, self.part, 0, stream)
+                self._mvx(ly.gate_up, self.hidden, _lib.X_RMSNORM, ly.ffn_norm, self.normed, self.ws_h, self.gu, 0,
+                          stream)
+                self._mvx(ly.down, self.gu, _lib.X_SILU_MUL, None, self.act, self.ws_act, self.part, 0, stream)
             else:
+                self._norm(self.hidden, ly.ffn_norm, self.normed, self.ws_h, stream)
                 k = s.num_experts_per_tok
                 self._mv(ly.router, self.normed, self.ws_h, self.router_logits, 0, stream)
                 _check(L.pyrite_cuda_moe_route(self.router_logits.data_ptr(), s.num_experts, k,

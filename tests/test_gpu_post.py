@@ -203,3 +203,112 @@ def test_split_attention_step_equals_separate_kernels(cuda_device, max_ctx, pos)
             want.append(w @ v[:, h // grp])
         want = torch.cat(want).float()
         assert torch.allclose(out, want, rtol=1e-4, atol=1e-5)
+
+
+def _transformed(lib, ggml_type, w, x, x_op, norm, x_out, ws_ptr, ws_len, y, rows, cols, flags=0):
+    import torch
+
+    code = lib.pyrite_cuda_matvec_transformed(ggml_type, w.data_ptr(), w.numel(), x.data_ptr(), x_op,
+                                              norm.data_ptr() if norm is not None else None, 1e-6,
+                                              x_out.data_ptr() if x_out is not None else None, ws_ptr, ws_len,
+                                              y.data_ptr(), rows, cols, flags,
+                                              torch.cuda.current_stream().cuda_stream)
+    assert code == 0, code
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("ggml_type", [8, 12, 13, 14, 23, 2])
+@pytest.mark.parametrize("rows,cols", [(1024, 2048), (7, 4096), (3000, 14336), (64, 1024)])
+@pytest.mark.parametrize("given_ws", [True, False])
+def test_matvec_rmsnorm_prologue_equals_separate_kernels(cuda_device, ggml_type, rows, cols, given_ws):
+    """RMSNorm computed with the matvec (pyrite_cuda_matvec_transformed; in its
+    prologue when no workspace is given, else in the form the library picks)
+    against pyrite_cuda_rmsnorm_encode + pyrite_cuda_matvec_prepared: the same
+    fp64 statistics up to summation order, so the same product within 1e-5 of
+    sum |w x|; accumulate adds to y."""
+    if ggml_type == 2 and not given_ws:
+        pytest.skip("formats without the batch-1 kernel need the workspace")
+    import torch
+
+    from pyrite_b200 import _lib
+    from pyrite_b200.kernels import cuda as K
+    lib = _lib.require()
+    w, x, _ = _setup(ggml_type, rows, cols, rows + cols)
+    x = x * 3.0
+    norm_w = torch.rand(cols, device="cuda") + 0.5
+    s = torch.cuda.current_stream().cuda_stream
+    ref_x = torch.empty(cols, device="cuda")
+    ref_buf, ref_ptr, ref_len, _, _ = _ws(cols)
+    assert lib.pyrite_cuda_rmsnorm_encode(x.data_ptr(), norm_w.data_ptr(), cols, 1e-6, ref_x.data_ptr(), ref_ptr,
+                                          ref_len, s) == 0
+    ref_y = torch.empty(rows, device="cuda")
+    assert lib.pyrite_cuda_matvec_prepared(ggml_type, w.data_ptr(), w.numel(), ref_x.data_ptr(), ref_ptr, ref_len,
+                                           ref_y.data_ptr(), rows, cols, 0, s) == 0
+    dense = K.dequantize_rows(ggml_type, w, rows, cols).double().abs()
+    bound = (dense @ ref_x.double().abs()).float() * 1e-5 + 1e-6
+    x_out = torch.full((cols,), float("nan"), device="cuda")
+    y = torch.full((rows,), float("nan"), device="cuda")
+    buf, ptr, ln, _, _ = _ws(cols)
+    if not given_ws:
+        ptr, ln = None, 0
+    _transformed(lib, ggml_type, w, x, _lib.X_RMSNORM, norm_w, x_out, ptr, ln, y, rows, cols)
+    assert K.status() == 0
+    assert torch.allclose(x_out, ref_x, rtol=1e-6, atol=0)
+    assert bool(((y - ref_y).abs() <= bound).all())
+    base = torch.randn(rows, device="cuda")
+    y2 = base.clone()
+    _transformed(lib, ggml_type, w, x, _lib.X_RMSNORM, norm_w, x_out if given_ws else None, ptr, ln, y2, rows,
+                 cols, 2)  # PYRITE_F_ACCUMULATE
+    assert bool(((y2 - (base + ref_y)).abs() <= bound + 1e-6 * base.abs()).all())
+
+
+@pytest.mark.parametrize("ggml_type", [8, 12, 14, 2])
+@pytest.mark.parametrize("rows,f", [(4096, 14336), (5, 1024)])
+@pytest.mark.parametrize("given_ws", [True, False])
+def test_matvec_silu_prologue_equals_separate_kernels(cuda_device, ggml_type, rows, f, given_ws):
+    """SiLU(gate) * up computed with the down projection (in its prologue when
+    no workspace is given): elementwise, so the encoded activation and the
+    product are identical to pyrite_cuda_silu_mul_encode +
+    pyrite_cuda_matvec_prepared."""
+    if ggml_type == 2 and not given_ws:
+        pytest.skip("formats without the batch-1 kernel need the workspace")
+    import torch
+
+    from pyrite_b200 import _lib
+    lib = _lib.require()
+    w, _, _ = _setup(ggml_type, rows, f, rows ^ f)
+    gu = torch.randn(2 * f, device="cuda", generator=torch.Generator("cuda").manual_seed(f)) * 4
+    s = torch.cuda.current_stream().cuda_stream
+    ref_act = torch.empty(f, device="cuda")
+    ref_buf, ref_ptr, ref_len, _, _ = _ws(f)
+    assert lib.pyrite_cuda_silu_mul_encode(gu.data_ptr(), f, ref_act.data_ptr(), ref_ptr, ref_len, s) == 0
+    ref_y = torch.empty(rows, device="cuda")
+    assert lib.pyrite_cuda_matvec_prepared(ggml_type, w.data_ptr(), w.numel(), ref_act.data_ptr(), ref_ptr, ref_len,
+                                           ref_y.data_ptr(), rows, f, 0, s) == 0
+    act = torch.empty(f, device="cuda")
+    y = torch.empty(rows, device="cuda")
+    buf, ptr, ln, _, _ = _ws(f)
+    if not given_ws:
+        ptr, ln = None, 0
+    _transformed(lib, ggml_type, w, gu, _lib.X_SILU_MUL, None, act, ptr, ln, y, rows, f)
+    assert torch.equal(act, ref_act)
+    assert torch.equal(y, ref_y)
+
+
+def test_matvec_transformed_rejects_bad_arguments(cuda_device):
+    import torch
+
+    from pyrite_b200 import _lib
+    lib = _lib.require()
+    w, x, _ = _setup(8, 64, 256, 1)
+    y = torch.empty(64, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    # unknown operation, RMSNorm without a weight, a format without the batch-1
+    # kernel given no workspace
+    assert lib.pyrite_cuda_matvec_transformed(8, w.data_ptr(), w.numel(), x.data_ptr(), 3, None, 1e-6, None, None, 0,
+                                              y.data_ptr(), 64, 256, 0, s) == -3
+    assert lib.pyrite_cuda_matvec_transformed(8, w.data_ptr(), w.numel(), x.data_ptr(), 1, None, 1e-6, None, None, 0,
+                                              y.data_ptr(), 64, 256, 0, s) == -3
+    w2, _, _ = _setup(2, 64, 256, 1)
+    assert lib.pyrite_cuda_matvec_transformed(2, w2.data_ptr(), w2.numel(), x.data_ptr(), 2, None, 1e-6, None, None,
+                                              0, y.data_ptr(), 64, 256, 0, s) == -3
