@@ -256,17 +256,15 @@ template <int TY> struct UnitK45 {
     }
     const int ia = dot32<false>(lo, u.a), ib = dot32<TY == Q4_K>(hi, u.b);
     // (scale, min) pairs 2p and 2p+1 (native.c:52-60): for j < 4 bytes j, j+4;
-    // for j >= 4 the low 4 bits in byte j+4 and the top 2 in bytes j-4 / j
-    const int k8 = 16 * (p & 1);
-    const uint32_t y = hdr.y >> k8, z = hdr.z >> k8, w = hdr.w >> k8;
-    uint32_t sca, mna, scb, mnb;
-    if (p < 2) {
-      sca = y & 63;        mna = z & 63;
-      scb = (y >> 8) & 63; mnb = (z >> 8) & 63;
-    } else {
-      sca = (w & 15) | ((y >> 2) & 0x30);        mna = ((w >> 4) & 15) | ((z >> 2) & 0x30);
-      scb = ((w >> 8) & 15) | ((y >> 10) & 0x30); mnb = ((w >> 12) & 15) | ((z >> 10) & 0x30);
-    }
+    // for j >= 4 the low 4 bits in byte j+4 and the top 2 in bytes j-4 / j.
+    // All eight of each, four per word, without branches (the four lanes of
+    // a super-block take different p); a byte permute picks the lane's pair.
+    const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu, mn_lo = hdr.z & 0x3F3F3F3Fu;
+    const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+    const uint32_t mn_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
+    const uint32_t sel = (uint32_t)(34 * p + 16);  // bytes 2p, 2p + 1 of (lo, hi)
+    const uint32_t scp = __byte_perm(sc_lo, sc_hi, sel), mnp = __byte_perm(mn_lo, mn_hi, sel);
+    const uint32_t sca = scp & 0xffu, scb = (scp >> 8) & 0xffu, mna = mnp & 0xffu, mnb = (mnp >> 8) & 0xffu;
     const float d = half_f(hdr.x & 0xffff), dmin = half_f(hdr.x >> 16);
     return d * ((float)sca * u.sa * (float)ia + (float)scb * u.sb * (float)ib) -
            dmin * ((float)mna * u.ma + (float)mnb * u.mb);
@@ -458,19 +456,22 @@ struct UnitIQ4XS {
     const uint32_t qw[4] = {q01.x, q01.y, q23.x, q23.y};
     // the book as int8: -127 -104 -83 -65 -49 -35 -22 -10 | 1 13 25 38 53 69 89 113
     const uint32_t T0 = 0xBFAD9881u, T1 = 0xF6EADDCFu, T2 = 0x26190D01u, T3 = 0x71594535u;
-    int a = 0, b = 0;
+    int a = 0, b = 0, a1 = 0, b1 = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const uint32_t n = (qw[k] >> (16 * half)) & 0xffffu;
-        const uint32_t sel = n & 0x7777u;
-        const uint32_t v = __byte_perm(__byte_perm(T0, T1, sel), __byte_perm(T2, T3, sel),
-                                       0x3210u | ((n & 0x8888u) >> 1));
-        a = __dp4a((int)v, (int)u.a[2 * k + half], a);
-        b = __dp4a((int)v, (int)u.b[2 * k + half], b);
-      }
+      // the selectors of all 8 nibbles at once (prmt reads the low 16 bits):
+      // bits 0-2 index a half of the book, bit 3 picks the half
+      const uint32_t sel = qw[k] & 0x77777777u, pick = ((qw[k] >> 1) & 0x44444444u) | 0x32103210u;
+      const uint32_t v0 = __byte_perm(__byte_perm(T0, T1, sel), __byte_perm(T2, T3, sel), pick);
+      const uint32_t sel1 = sel >> 16, pick1 = pick >> 16;
+      const uint32_t v1 = __byte_perm(__byte_perm(T0, T1, sel1), __byte_perm(T2, T3, sel1), pick1);
+      a = __dp4a((int)v0, (int)u.a[2 * k], a);
+      b = __dp4a((int)v0, (int)u.b[2 * k], b);
+      a1 = __dp4a((int)v1, (int)u.a[2 * k + 1], a1);
+      b1 = __dp4a((int)v1, (int)u.b[2 * k + 1], b1);
     }
+    a += a1;
+    b += b1;
     const uint32_t sh = hdr.x >> 16;
     const int ls = ((hdr.y >> (4 * j)) & 15) | (int)(((sh >> (2 * j)) & 3u) << 4);
     return half_f(hdr.x & 0xffff) * (float)(ls - 32) * u.s * (float)(a * 254 + b);
