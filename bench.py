@@ -488,8 +488,8 @@ def model_leg(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
         k = spec.num_experts_per_tok
         held = spec.num_experts // world
         per_layer = [a + ly.router.data.numel() // world
-                     + k * (ly.gate_exps.data.numel() + ly.up_exps.data.numel() + ly.down_exps.data.numel())
-                     // (held * world)
+                     + k * sum(m.data.numel() for m in (ly.gate_exps, ly.up_exps, ly.gate_up_exps, ly.down_exps)
+                               if m is not None) // (held * world)
                      for a, ly in zip(per_layer, dec.layers)]
     else:
         per_layer = [a + (ly.gate_up.data.numel() if ly.gate_up is not None else

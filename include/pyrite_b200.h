@@ -113,6 +113,15 @@ int pyrite_cuda_matvec_transformed(int type_id, const void *weights, size_t weig
                                    void *workspace, size_t workspace_len, float *y, size_t rows,
                                    size_t cols, unsigned flags, void *stream);
 
+/* The form pyrite_cuda_matvec_transformed takes for these arguments given a
+ * workspace: 1 = prologue (the workspace is left untouched), 0 = the
+ * operation's own kernel first (afterwards the workspace and x_out hold x',
+ * so further matrices on the same x' can use pyrite_cuda_matvec_prepared),
+ * or a PYRITE_E_* code.  Host only; nothing is launched. */
+int pyrite_cuda_matvec_transformed_form(int type_id, const void *weights, size_t weights_len, const float *x,
+                                        int x_op, const float *norm_weight, const float *x_out, size_t rows,
+                                        size_t cols);
+
 /* Scratch bytes PYRITE_POST_ARGMAX needs on the current device. */
 size_t pyrite_cuda_post_scratch_size(void);
 
@@ -290,6 +299,18 @@ int pyrite_cuda_matvec_experts(int type_id, const void *stacked, size_t stacked_
                                const void *workspace, size_t workspace_len, size_t ws_stride,
                                float *y, size_t y_stride, size_t rows, size_t cols, unsigned flags,
                                void *stream);
+
+/* pyrite_cuda_matvec_experts over n_groups stacks of the same type and shape
+ * stored back to back (e.g. ffn_gate_exps then ffn_up_exps: stacked_len =
+ * n_groups * n_experts * rows * row_bytes), all in one launch: selection
+ * j < n_groups * n_ids multiplies expert expert_ids[j % n_ids] of stack
+ * j / n_ids by activation j % n_ids into y + j * y_stride.  n_groups <= 8,
+ * n_groups * n_ids <= 64. */
+int pyrite_cuda_matvec_expert_groups(int type_id, const void *stacked, size_t stacked_len, size_t n_experts,
+                                     size_t n_groups, const int *expert_ids, size_t n_ids, const float *x,
+                                     size_t x_stride, const void *workspace, size_t workspace_len,
+                                     size_t ws_stride, float *y, size_t y_stride, size_t rows, size_t cols,
+                                     unsigned flags, void *stream);
 
 /* act_j = silu(gate_j) * up_j for the n_sel experts (gate, up, act: n_sel x ff),
  * each encoded at workspace + j * pyrite_cuda_workspace_size(0, ff, 1). */

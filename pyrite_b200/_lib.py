@@ -43,6 +43,8 @@ SIGNATURES: dict[str, tuple] = {
     "pyrite_cuda_matvec_transformed": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, ctypes.c_int, _VP,
                                                       ctypes.c_double, _VP, _VP, _SZ, _VP, _SZ, _SZ, ctypes.c_uint,
                                                       _VP)),
+    "pyrite_cuda_matvec_transformed_form": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, ctypes.c_int, _VP, _VP, _SZ,
+                                                           _SZ)),
     "pyrite_cuda_post_scratch_size": (_SZ, ()),
     "pyrite_cuda_matvec_prepared_post": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _VP, _VP, _SZ, _VP, _SZ, _SZ,
                                                         ctypes.c_uint, ctypes.POINTER(PostOp), _VP)),
@@ -61,6 +63,8 @@ SIGNATURES: dict[str, tuple] = {
                                              ctypes.c_int, ctypes.c_int, _VP, _VP, _VP, _VP)),
     "pyrite_cuda_matvec_experts": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _SZ, _VP, _SZ, _VP, _SZ, _VP, _SZ, _SZ,
                                                   _VP, _SZ, _SZ, _SZ, ctypes.c_uint, _VP)),
+    "pyrite_cuda_matvec_expert_groups": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _SZ, _SZ, _VP, _SZ, _VP, _SZ, _VP,
+                                                        _SZ, _SZ, _VP, _SZ, _SZ, _SZ, ctypes.c_uint, _VP)),
     "pyrite_cuda_moe_silu_mul_encode": (ctypes.c_int, (_VP, _VP, _SZ, _SZ, _VP, _VP, _SZ, _VP)),
     "pyrite_cuda_moe_combine": (ctypes.c_int, (_VP, _VP, _SZ, _SZ, _VP, _VP)),
     "pyrite_cuda_silu_mul_encode": (ctypes.c_int, (_VP, _SZ, _VP, _VP, _SZ, _VP)),

@@ -235,23 +235,22 @@ int pyrite_cuda_matvec_prepared(int type_id, const void* weights, size_t weights
   return rc > 0 ? PYRITE_E_CUDA : rc;
 }
 
-int pyrite_cuda_matvec_transformed(int type_id, const void* weights, size_t weights_len, const float* x, int x_op,
-                                   const float* norm_weight, double eps, float* x_out, void* workspace,
-                                   size_t workspace_len, float* y, size_t rows, size_t cols, unsigned flags,
-                                   void* stream) {
+// Validation and the choice of form shared by pyrite_cuda_matvec_transformed
+// and pyrite_cuda_matvec_transformed_form: 1 = prologue, 0 = the operation's
+// own kernel then the product, < 0 = error code.
+static int transformed_plan(int type_id, const void* weights, size_t weights_len, const float* x, int x_op,
+                            const float* norm_weight, const float* x_out, bool have_ws, size_t rows, size_t cols,
+                            size_t* row_bytes) {
   size_t rb = 0;
   int rc = geometry(type_id, rows, cols, &rb, nullptr);
   if (rc) return rc;
-  if (!weights || !x || !y || weights_len != rb * rows || cols % 32) return PYRITE_E_BUFFER;
+  if (!weights || !x || weights_len != rb * rows || cols % 32) return PYRITE_E_BUFFER;
   if (x_op != PYRITE_X_RMSNORM && x_op != PYRITE_X_SILU_MUL) return PYRITE_E_BUFFER;
   if (x_op == PYRITE_X_RMSNORM && !norm_weight) return PYRITE_E_BUFFER;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const uint8_t* w = static_cast<const uint8_t*>(weights);
-  const bool acc = (flags & PYRITE_F_ACCUMULATE) != 0;
+  *row_bytes = rb;
   // the prologue reads and writes the vectors as float4
   const bool vec16 = (((uintptr_t)x | (uintptr_t)norm_weight | (uintptr_t)x_out) & 15) == 0;
-  const bool lane = vec16 && lane_supported(type_id, w, rb, (int)cols);
-  const bool have_ws = x_out && workspace && workspace_len >= ws_col_bytes((int)cols) && !((uintptr_t)workspace & 255);
+  const bool lane = vec16 && lane_supported(type_id, static_cast<const uint8_t*>(weights), rb, (int)cols);
   // Every CTA of the prologue form encodes the whole vector after the
   // preceding kernel finished, one L2 round trip under the weight stream of
   // the whole grid.  Measured on B200: that beats a kernel of its own for an
@@ -259,17 +258,39 @@ int pyrite_cuda_matvec_transformed(int type_id, const void* weights, size_t weig
   // gate/up); shorter norms and SiLU * up (more work per value, ffn-wide
   // vectors) are faster as their own kernel, which is used when the caller
   // gives a workspace.
-  const bool prologue = lane && (!have_ws || (x_op == PYRITE_X_RMSNORM && cols >= 4096));
-  if (prologue) {
+  if (lane && (!have_ws || (x_op == PYRITE_X_RMSNORM && cols >= 4096))) return 1;
+  return have_ws ? 0 : PYRITE_E_BUFFER;
+}
+
+int pyrite_cuda_matvec_transformed_form(int type_id, const void* weights, size_t weights_len, const float* x,
+                                        int x_op, const float* norm_weight, const float* x_out, size_t rows,
+                                        size_t cols) {
+  size_t rb = 0;
+  return transformed_plan(type_id, weights, weights_len, x, x_op, norm_weight, x_out, x_out != nullptr, rows, cols,
+                          &rb);
+}
+
+int pyrite_cuda_matvec_transformed(int type_id, const void* weights, size_t weights_len, const float* x, int x_op,
+                                   const float* norm_weight, double eps, float* x_out, void* workspace,
+                                   size_t workspace_len, float* y, size_t rows, size_t cols, unsigned flags,
+                                   void* stream) {
+  if (!y) return PYRITE_E_BUFFER;
+  const bool have_ws = x_out && workspace && workspace_len >= ws_col_bytes((int)cols) && !((uintptr_t)workspace & 255);
+  size_t rb = 0;
+  int rc = transformed_plan(type_id, weights, weights_len, x, x_op, norm_weight, x_out, have_ws, rows, cols, &rb);
+  if (rc < 0) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* w = static_cast<const uint8_t*>(weights);
+  const bool acc = (flags & PYRITE_F_ACCUMULATE) != 0;
+  if (rc == 1) {
     XPrologue xp{x_op == PYRITE_X_RMSNORM ? 1 : 2, x, norm_weight, eps, x_out};
     rc = launch_mv_lane(type_id, w, rb, (int)rows, (int)cols, nullptr, y, (flags & PYRITE_F_STATIC_WEIGHTS) != 0, s,
                         acc, nullptr, nullptr, &xp);
     return rc > 0 ? PYRITE_E_CUDA : rc;
   }
-  // formats without the batch-1 kernel (or vectors not 16-byte aligned): the
-  // operation's own kernel into the workspace and x_out (required here), then
-  // the product
-  if (!have_ws) return PYRITE_E_BUFFER;
+  // formats without the batch-1 kernel (or vectors not 16-byte aligned), or
+  // sizes where that is faster: the operation's own kernel into the workspace
+  // and x_out, then the product
   rc = x_op == PYRITE_X_RMSNORM
            ? pyrite_cuda_rmsnorm_encode(x, norm_weight, cols, eps, x_out, workspace, workspace_len, stream)
            : pyrite_cuda_silu_mul_encode(x, cols, x_out, workspace, workspace_len, stream);

@@ -93,10 +93,15 @@ int launch_xprep(const float* x, long long ldx, int cols, int ncols, uint8_t* ws
 // expert_bytes apart; ids[0..n_sel) (device memory, read after the preceding
 // kernel) pick the ones to multiply, each by its own prepared x (ws_stride
 // bytes apart, 0: one shared x) into y + j * y_stride.
+// Selection j (of n_sel) multiplies expert ids[j % n_ids] of group j / n_ids:
+// the stack holds n_sel / n_ids groups of n_experts experts each (one group
+// per matrix, e.g. gate and up), so one launch covers every group.  x and the
+// workspace advance per id (j % n_ids), y per selection.
 struct ExpertArgs {
   const int* ids;
   int n_experts, n_sel;
   long long expert_bytes, ws_stride, y_stride;
+  int n_ids = 0;  // 0: n_sel (one group)
 };
 // The activation computed in every CTA's prologue instead of a prepared
 // workspace: mode 1 RMSNorm of src with weight norm, mode 2 silu(src[:cols]) *

@@ -172,23 +172,34 @@ int pyrite_cuda_matvec_experts(int type_id, const void* stacked, size_t stacked_
                                const int* expert_ids, size_t n_sel, const float* x, size_t x_stride,
                                const void* workspace, size_t workspace_len, size_t ws_stride, float* y,
                                size_t y_stride, size_t rows, size_t cols, unsigned flags, void* stream) {
+  return pyrite_cuda_matvec_expert_groups(type_id, stacked, stacked_len, n_experts, 1, expert_ids, n_sel, x, x_stride,
+                                          workspace, workspace_len, ws_stride, y, y_stride, rows, cols, flags, stream);
+}
+
+int pyrite_cuda_matvec_expert_groups(int type_id, const void* stacked, size_t stacked_len, size_t n_experts,
+                                     size_t n_groups, const int* expert_ids, size_t n_ids, const float* x,
+                                     size_t x_stride, const void* workspace, size_t workspace_len, size_t ws_stride,
+                                     float* y, size_t y_stride, size_t rows, size_t cols, unsigned flags,
+                                     void* stream) {
+  if (n_groups == 0 || n_groups > 8) return PYRITE_E_BUFFER;
+  const size_t n_sel = n_ids * n_groups;
   const TypeGeo* t = find_type(type_id);
   if (!t) return PYRITE_E_TYPE;
   if (rows == 0 || cols == 0 || cols % (size_t)t->bs || rows > 0x7fffffffu || cols > 0x7fffffffu)
     return PYRITE_E_SHAPE;
   const size_t rb = cols / t->bs * t->bpb;
   const size_t expert_bytes = rb * rows;
-  if (!stacked || !expert_ids || !x || !y || !workspace || n_experts == 0 || n_experts > 0x7fffffffu || n_sel == 0 ||
-      n_sel > 64 || stacked_len != expert_bytes * n_experts)
+  if (!stacked || !expert_ids || !x || !y || !workspace || n_experts == 0 || n_experts > 0x7fffffffu || n_ids == 0 ||
+      n_sel > 64 || stacked_len != expert_bytes * n_experts * n_groups)
     return PYRITE_E_BUFFER;
   if (y_stride < rows) return PYRITE_E_BUFFER;
   const size_t per = pyrite_cuda_workspace_size(0, cols, 1);
   if (((uintptr_t)workspace & 255) || (ws_stride && (ws_stride < per || ws_stride % 256)) ||
-      workspace_len < (ws_stride ? ws_stride * (n_sel - 1) + per : per))
+      workspace_len < (ws_stride ? ws_stride * (n_ids - 1) + per : per))
     return PYRITE_E_BUFFER;
   const uint8_t* w = static_cast<const uint8_t*>(stacked);
   ExpertArgs ex{expert_ids, (int)n_experts, (int)n_sel, (long long)expert_bytes, (long long)ws_stride,
-                (long long)y_stride};
+                (long long)y_stride, (int)n_ids};
   const bool acc = (flags & PYRITE_F_ACCUMULATE) != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int r;

@@ -16,9 +16,9 @@ namespace pyr {
 
 // Routed experts (ex.ids != nullptr): blockIdx.y = j picks stacked matrix
 // ids[j] (expert_bytes apart), x + j * x_stride and y + j * y_stride.
-struct GenericExperts {
+struct GenericExperts {  // as ExpertArgs: slice j = expert ids[j % n_ids] of group j / n_ids
   const int* ids = nullptr;
-  int n_experts = 0;
+  int n_experts = 0, n_ids = 1;
   long long expert_bytes = 0, x_stride = 0, y_stride = 0;
 };
 
@@ -30,15 +30,16 @@ mv_generic_kernel(const uint8_t* __restrict__ w, size_t row_bytes, int rows, int
   constexpr int BS = Geo<TY>::bs, BPB = Geo<TY>::bpb;
   if (ex.ids) {
     pdl_wait();  // the ids come from the preceding kernel
-    const int j = blockIdx.y;
-    int e = ex.ids[j];
+    const int j = blockIdx.y, idn = j % ex.n_ids;
+    int e = ex.ids[idn];
     if (e == -1) return;  // held by another GPU
     if (e < 0 || e >= ex.n_experts) {  // never read outside the stack
       if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(status, (int)kStatusBadExpert);
       e = 0;
     }
+    e += (j / ex.n_ids) * ex.n_experts;
     w += (size_t)e * (size_t)ex.expert_bytes;
-    x += (size_t)j * (size_t)ex.x_stride;
+    x += (size_t)idn * (size_t)ex.x_stride;
     y += (size_t)j * (size_t)ex.y_stride;
   }
   const int lane = threadIdx.x & 31;
@@ -145,6 +146,7 @@ int launch_mv_generic(int type_id, const MatvecArgs<T>& a, cudaStream_t stream, 
   if (experts) {
     ex.ids = experts->ids;
     ex.n_experts = experts->n_experts;
+    ex.n_ids = experts->n_ids > 0 ? experts->n_ids : experts->n_sel;
     ex.expert_bytes = experts->expert_bytes;
     ex.x_stride = x_stride;
     ex.y_stride = experts->y_stride;

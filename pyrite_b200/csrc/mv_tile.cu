@@ -559,12 +559,13 @@ struct TileArgs {
   int static_weights;
   int accumulate;   // y += W x (a residual stream) instead of y = W x
   PostArgs post;    // operation run on the whole y by the last CTA to finish
-  // routed experts (experts != nullptr): w is a stack of n_experts matrices
-  // expert_bytes apart; the CTAs form n_sel equal groups, group j multiplies
-  // matrix experts[j] (read on the device) by the j-th prepared x (ws +
-  // j * ws_stride) into y + j * y_stride.
+  // routed experts (experts != nullptr): w is a stack of matrices
+  // expert_bytes apart, n_sel / n_ids groups of n_experts; the CTAs form n_sel
+  // equal groups, group j multiplies matrix experts[j % n_ids] of stack group
+  // j / n_ids (the id read on the device) by prepared x number j % n_ids (ws +
+  // (j % n_ids) * ws_stride) into y + j * y_stride.
   const int* experts;
-  int n_experts, n_sel;
+  int n_experts, n_sel, n_ids;
   long long expert_bytes, ws_stride, y_stride;
   // x prologue (xmode != 0): every CTA encodes its own copy of x into shared
   // memory from fp32 input instead of reading a prepared workspace --
@@ -632,12 +633,14 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   pdl_wait();
   pdl_launch_dependents();
   if (a.experts) {  // written by the routing kernel this one waited for
-    int eid = a.experts[sel];
+    const int idn = sel % a.n_ids;
+    int eid = a.experts[idn];
     if (eid == -1) return;  // selected, but held by another GPU: nothing issued yet
     if (eid < 0 || eid >= a.n_experts) {  // never read outside the stack
       if (tid == 0) atomicOr(status, (int)kStatusBadExpert);
       eid = 0;
     }
+    eid += (sel / a.n_ids) * a.n_experts;
     wb = a.w + (size_t)eid * (size_t)a.expert_bytes;
   }
   const int wmod4 = (int)((uintptr_t)wb & 3);
@@ -645,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   if (!early && tid == 0)
     for (int k = 0; k < min(my, S - 1); ++k) issue(k);
 
-  const uint8_t* xws = a.ws + (size_t)sel * (size_t)a.ws_stride;
+  const uint8_t* xws = a.ws + (size_t)(a.experts ? sel % a.n_ids : 0) * (size_t)a.ws_stride;
   if (a.xmode) {  // this CTA's own encoding of x (the input was written by the preceding kernel)
     __shared__ double xshm[32];
     uint8_t* enc = smem + a.xenc_off;
@@ -845,13 +848,14 @@ int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, in
   const size_t xenc = xp ? ((lane_workspace_bytes(cols) + 255) & ~(size_t)255) : 0;
   const TilePlan p = plan_tile(row_bytes, rows, cols, vals, xenc);
   TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs_log2, p.m, p.stage_bytes, static_weights ? 1 : 0,
-              accumulate ? 1 : 0, post ? *post : PostArgs{}, nullptr, 0, 0, 0, 0, 0,
+              accumulate ? 1 : 0, post ? *post : PostArgs{}, nullptr, 0, 0, 0, 0, 0, 0,
               xp ? xp->mode : 0, xp ? xp->src : nullptr, xp ? xp->norm : nullptr, xp ? xp->eps : 0.0,
               xp ? xp->out : nullptr, p.xenc_off};
   if (ex) {
     ta.experts = ex->ids;
     ta.n_experts = ex->n_experts;
     ta.n_sel = ex->n_sel;
+    ta.n_ids = ex->n_ids > 0 ? ex->n_ids : ex->n_sel;
     ta.expert_bytes = ex->expert_bytes;
     ta.ws_stride = ex->ws_stride;
     ta.y_stride = ex->y_stride;

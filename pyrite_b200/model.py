@@ -59,6 +59,7 @@ class _Layer:
     gate_exps: _Mat | None = None  # stacked: rows = moe ff, E matrices
     up_exps: _Mat | None = None
     down_exps: _Mat | None = None
+    gate_up_exps: _Mat | None = None  # [gate stack | up stack] when both share a type (one launch for both)
 
 
 class MixedDecoder:
@@ -153,6 +154,8 @@ class MixedDecoder:
                 ly.down = mat(p + "ffn_down.weight")
             self.layers.append(ly)
         host.clear()
+        self.n_stack_experts = spec.num_experts if self.moe else 0
+        self._pair_expert_stacks()
 
         # activations and state
         q_dim, kv_dim = spec.q_dim, spec.kv_dim
@@ -163,7 +166,9 @@ class MixedDecoder:
             ff, E, k = spec.moe_intermediate_size, spec.num_experts, spec.num_experts_per_tok
             self.router_logits = z(E)
             self.expert_ids, self.expert_w = z(k, dt=torch.int32), z(k)
-            self.gate, self.up, self.act, self.down = z(k, ff), z(k, ff), z(k, ff), z(k, h)
+            self.gate_up_out = z(2 * k, ff)  # [gate_j | up_j] of the selected experts
+            self.gate, self.up = self.gate_up_out[:k], self.gate_up_out[k:]
+            self.act, self.down = z(k, ff), z(k, h)
         else:
             ff, k = spec.intermediate_size, 1
             self.gu, self.act = z(2 * ff), z(ff)
@@ -234,14 +239,54 @@ class MixedDecoder:
             wlen, y.data_ptr(), m.rows, m.cols, flags | STATIC_WEIGHTS, stream)
         _check(code, "matvec+x")
 
+    def _x_in_workspace(self, m: _Mat, x: torch.Tensor, x_op: int, norm: torch.Tensor | None,
+                        x_out: torch.Tensor) -> bool:
+        """Whether ``_mvx(m, x, ...)`` runs the operation's own kernel first, so
+        that its workspace and ``x_out`` hold x' for further matrices."""
+        form = self.lib.pyrite_cuda_matvec_transformed_form(
+            m.ggml_type, m.data.data_ptr(), m.data.numel(), x.data_ptr(), x_op,
+            norm.data_ptr() if norm is not None else None, x_out.data_ptr(), m.rows, m.cols)
+        _check(min(form, 0), "matvec+x form")
+        return form == 0
+
+    def _mvx2(self, a: _Mat, b: _Mat, x: torch.Tensor, norm: torch.Tensor, ws, ya: torch.Tensor,
+              yb: torch.Tensor, stream: int) -> None:
+        """ya = A RMSNorm(x), yb = B RMSNorm(x): the norm runs once when the
+        library computes it in a kernel of its own, else in both prologues."""
+        X = _lib.X_RMSNORM
+        self._mvx(a, x, X, norm, self.normed, ws, ya, 0, stream)
+        if self._x_in_workspace(a, x, X, norm, self.normed):
+            self._mv(b, self.normed, ws, yb, 0, stream)
+        else:
+            self._mvx(b, x, X, norm, self.normed, ws, yb, 0, stream)
+
+    def _pair_expert_stacks(self) -> None:
+        """Store ffn_gate_exps and ffn_up_exps back to back when they share a
+        type and shape, so one launch multiplies both for every selected expert."""
+        for ly in self.layers:
+            g, u = ly.gate_exps, ly.up_exps
+            if g is None or u is None or g.ggml_type != u.ggml_type or (g.rows, g.cols) != (u.rows, u.cols):
+                continue
+            ly.gate_up_exps = _Mat(g.ggml_type, torch.cat([g.data, u.data]), g.rows, g.cols)
+            ly.gate_exps = ly.up_exps = None
+
     def _experts(self, m: _Mat, x: torch.Tensor, x_stride: int, ws, ws_stride: int, y: torch.Tensor,
-                 stream: int) -> None:
+                 stream: int, groups: int = 1) -> None:
+        """y[j] = stack (j // k) expert ids[j % k] times activation j % k, for
+        j < groups * k, in one launch."""
         wptr, wlen = self._wsp(ws)
-        E, k = self.spec.num_experts, self.spec.num_experts_per_tok
-        code = self.lib.pyrite_cuda_matvec_experts(m.ggml_type, m.data.data_ptr(), m.data.numel(), E,
-                                                   self.expert_ids.data_ptr(), k, x.data_ptr(), x_stride, wptr, wlen,
-                                                   ws_stride, y.data_ptr(), y.shape[1], m.rows, m.cols, 0, stream)
+        k = self.spec.num_experts_per_tok
+        code = self.lib.pyrite_cuda_matvec_expert_groups(
+            m.ggml_type, m.data.data_ptr(), m.data.numel(), self.n_stack_experts, groups, self.expert_ids.data_ptr(),
+            k, x.data_ptr(), x_stride, wptr, wlen, ws_stride, y.data_ptr(), y.shape[-1], m.rows, m.cols, 0, stream)
         _check(code, "expert matvec")
+
+    def _gate_up_experts(self, ly: _Layer, stream: int) -> None:
+        if ly.gate_up_exps is not None:
+            self._experts(ly.gate_up_exps, self.normed, 0, self.ws_h, 0, self.gate_up_out, stream, groups=2)
+        else:
+            self._experts(ly.gate_exps, self.normed, 0, self.ws_h, 0, self.gate, stream)
+            self._experts(ly.up_exps, self.normed, 0, self.ws_h, 0, self.up, stream)
 
     def _norm(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, ws, stream: int) -> None:
         wptr, wlen = self._wsp(ws)
@@ -257,9 +302,7 @@ class MixedDecoder:
         _check(L.pyrite_cuda_embed(self.embd.ggml_type, self.embd.data.data_ptr(), s.vocab_size, h,
                                    self.tokens.data_ptr(), self.pos.data_ptr(), self.hidden.data_ptr(), stream), "embed")
         for li, ly in enumerate(self.layers):
-            self._mvx(ly.qk, self.hidden, _lib.X_RMSNORM, ly.attn_norm, self.normed, self.ws_h, self.qkv, 0, stream)
-            self._mvx(ly.v, self.hidden, _lib.X_RMSNORM, ly.attn_norm, self.normed, self.ws_h, self.qkv[qk_rows:], 0,
-                      stream)
+            self._mvx2(ly.qk, ly.v, self.hidden, ly.attn_norm, self.ws_h, self.qkv, self.qkv[qk_rows:], stream)
             wq, wql = self._wsp(self.ws_q)
             _check(L.pyrite_cuda_attention_step(
                 self.qkv.data_ptr(), ly.q_norm.data_ptr() if ly.q_norm is not None else None,
@@ -270,12 +313,11 @@ class MixedDecoder:
                 "attention_step")
             self._mv(ly.o, self.attn, self.ws_q, self.hidden, ACCUMULATE, stream)
             if not self.moe:  # SwiGLU feed-forward, norm and SiLU in the projections' prologues
-                X = _lib.X_RMSNORM
                 if ly.gate_up is not None:
-                    self._mvx(ly.gate_up, self.hidden, X, ly.ffn_norm, self.normed, self.ws_h, self.gu, 0, stream)
+                    self._mvx(ly.gate_up, self.hidden, _lib.X_RMSNORM, ly.ffn_norm, self.normed, self.ws_h, self.gu, 0,
+                              stream)
                 else:
-                    self._mvx(ly.gate, self.hidden, X, ly.ffn_norm, self.normed, self.ws_h, self.gu[:ff], 0, stream)
-                    self._mvx(ly.up, self.hidden, X, ly.ffn_norm, self.normed, self.ws_h, self.gu[ff:], 0, stream)
+                    self._mvx2(ly.gate, ly.up, self.hidden, ly.ffn_norm, self.ws_h, self.gu[:ff], self.gu[ff:], stream)
                 self._mvx(ly.down, self.gu, _lib.X_SILU_MUL, None, self.act, self.ws_act, self.hidden, ACCUMULATE,
                           stream)
                 continue
@@ -287,8 +329,7 @@ class MixedDecoder:
                                            1 if s.norm_topk_prob else 0, 1.0, self.expert_shards, self.expert_shard,
                                            self.expert_ids.data_ptr(), self.expert_w.data_ptr(),
                                            self.route_log[li].data_ptr(), stream), "route")
-            self._experts(ly.gate_exps, self.normed, 0, self.ws_h, 0, self.gate, stream)
-            self._experts(ly.up_exps, self.normed, 0, self.ws_h, 0, self.up, stream)
+            self._gate_up_experts(ly, stream)
             wa, wal = self._wsp(self.ws_act)
             _check(L.pyrite_cuda_moe_silu_mul_encode(self.gate.data_ptr(), self.up.data_ptr(), ff, k,
                                                      self.act.data_ptr(), wa, wal, stream), "moe silu")

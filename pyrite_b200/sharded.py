@@ -110,6 +110,8 @@ class ShardedDecoder(MixedDecoder):
                 ly.gate_up = cat(rows(p + "ffn_gate.weight", f0, f1), rows(p + "ffn_up.weight", f0, f1))
                 ly.down = cols(p + "ffn_down.weight", f0, f1)
             self.layers.append(ly)
+        self.n_stack_experts = len(owned_experts(spec.num_experts, world, rank)) if self.moe else 0
+        self._pair_expert_stacks()
 
         z = lambda *shape, dt=torch.float32: torch.zeros(*shape, dtype=dt, device=d)  # noqa: E731
         nq_l, nkv_l = hs.nq * hd, hs.nkv * hd
@@ -120,7 +122,9 @@ class ShardedDecoder(MixedDecoder):
             self.n_local_experts = len(owned_experts(spec.num_experts, world, rank))
             self.router_logits = z(spec.num_experts)
             self.expert_ids, self.expert_w = z(k, dt=torch.int32), z(k)
-            self.gate, self.up, self.act, self.down = z(k, ff), z(k, ff), z(k, ff), z(k, h)
+            self.gate_up_out = z(2 * k, ff)
+            self.gate, self.up = self.gate_up_out[:k], self.gate_up_out[k:]
+            self.act, self.down = z(k, ff), z(k, h)
         else:
             ff, k = spec.intermediate_size // world, 1
             self.gu, self.act = z(2 * ff), z(ff)
@@ -176,9 +180,7 @@ class ShardedDecoder(MixedDecoder):
         _check(L.pyrite_cuda_embed(self.embd.ggml_type, self.embd.data.data_ptr(), s.vocab_size, h,
                                    self.tokens.data_ptr(), self.pos.data_ptr(), self.hidden.data_ptr(), stream), "embed")
         for li, ly in enumerate(self.layers):
-            self._mvx(ly.qk, self.hidden, _lib.X_RMSNORM, ly.attn_norm, self.normed, self.ws_h, self.qkv, 0, stream)
-            self._mvx(ly.v, self.hidden, _lib.X_RMSNORM, ly.attn_norm, self.normed, self.ws_h, self.qkv[qk_rows:], 0,
-                      stream)
+            self._mvx2(ly.qk, ly.v, self.hidden, ly.attn_norm, self.ws_h, self.qkv, self.qkv[qk_rows:], stream)
             wq, wql = self._wsp(self.ws_q)
             _check(L.pyrite_cuda_attention_step(
                 self.qkv.data_ptr(), ly.q_norm.data_ptr() if ly.q_norm is not None else None,
@@ -200,12 +202,11 @@ class ShardedDecoder(MixedDecoder):
                                                1 if s.norm_topk_prob else 0, 1.0, self.world, self.rank,
                                                self.expert_ids.data_ptr(), self.expert_w.data_ptr(),
                                                self.route_log[li].data_ptr(), stream), "route")
-                self._local_experts(ly.gate_exps, self.normed, 0, self.ws_h, 0, self.gate, stream)
-                self._local_experts(ly.up_exps, self.normed, 0, self.ws_h, 0, self.up, stream)
+                self._gate_up_experts(ly, stream)
                 wa, wal = self._wsp(self.ws_act)
                 _check(L.pyrite_cuda_moe_silu_mul_encode(self.gate.data_ptr(), self.up.data_ptr(), ff, k,
                                                          self.act.data_ptr(), wa, wal, stream), "moe silu")
-                self._local_experts(ly.down_exps, self.act, ff, self.ws_act, self.ws_act[2], self.down, stream)
+                self._experts(ly.down_exps, self.act, ff, self.ws_act, self.ws_act[2], self.down, stream)
                 self.part.zero_()
                 _check(L.pyrite_cuda_moe_combine(self.down.data_ptr(), self.expert_w.data_ptr(), k, h,
                                                  self.part.data_ptr(), stream), "combine")
@@ -216,13 +217,3 @@ class ShardedDecoder(MixedDecoder):
         _check(L.pyrite_cuda_argmax_step(self.logits.data_ptr(), s.vocab_size, self.argmax_scratch.data_ptr(),
                                          self.argmax_scratch.numel(), self.tokens.data_ptr(), self.pos.data_ptr(),
                                          self.prompt_len, self.max_ctx, stream), "argmax")
-
-    def _local_experts(self, m: _Mat, x: torch.Tensor, x_stride: int, ws, ws_stride: int, y: torch.Tensor,
-                       stream: int) -> None:
-        wptr, wlen = self._wsp(ws)
-        k = self.spec.num_experts_per_tok
-        code = self.lib.pyrite_cuda_matvec_experts(m.ggml_type, m.data.data_ptr(), m.data.numel(),
-                                                   self.n_local_experts, self.expert_ids.data_ptr(), k, x.data_ptr(),
-                                                   x_stride, wptr, wlen, ws_stride, y.data_ptr(), y.shape[1], m.rows,
-                                                   m.cols, 0, stream)
-        _check(code, "expert matvec")

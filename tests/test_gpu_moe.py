@@ -96,6 +96,49 @@ def test_expert_matvec_matches_each_slice(cuda_device, ggml_type, cols):
             assert np.all(got[j, rows:] == -7.0)  # nothing written past the slice's rows
 
 
+
+@pytest.mark.parametrize("ggml_type,cols", [(12, 2048), (14, 768), (8, 1024), (2, 512)])
+@pytest.mark.parametrize("groups", [2, 3])
+def test_expert_groups_equal_one_call_per_stack(cuda_device, ggml_type, cols, groups):
+    """pyrite_cuda_matvec_expert_groups over `groups` stacks stored back to back
+    (gate | up) gives, bit for bit, what one pyrite_cuda_matvec_experts call
+    per stack gives; ids of -1 (experts held elsewhere) leave their rows of
+    every group untouched."""
+    import torch
+
+    from pyrite_b200 import _lib
+    from pyrite_b200.kernels import cuda as K
+    lib = _lib.require()
+    rows, n_experts, sel = 64, 6, [5, -1, 0, 5]
+    k = len(sel)
+    payload = random_payload(ggml_type, rows * n_experts * groups, cols, seed=7 * cols + groups)
+    w = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
+    ids = torch.tensor(sel, dtype=torch.int32, device="cuda")
+    x = torch.from_numpy(np.random.default_rng(groups).normal(0, 1, cols).astype(np.float32)).cuda()
+    per = int(lib.pyrite_cuda_workspace_size(0, cols, 1))
+    ws = torch.empty(per + 256, dtype=torch.uint8, device="cuda")
+    off = (-ws.data_ptr()) % 256
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.pyrite_cuda_prepare_x(x.data_ptr(), cols, cols, 1, ws.data_ptr() + off, ws.numel() - off, s) == 0
+    y = torch.full((groups * k, rows), -3.0, device="cuda")
+    assert lib.pyrite_cuda_matvec_expert_groups(ggml_type, w.data_ptr(), w.numel(), n_experts, groups,
+                                                ids.data_ptr(), k, x.data_ptr(), 0, ws.data_ptr() + off,
+                                                ws.numel() - off, 0, y.data_ptr(), rows, rows, cols, 0, s) == 0
+    one = w.numel() // groups
+    for g in range(groups):
+        yg = torch.full((k, rows), -3.0, device="cuda")
+        assert lib.pyrite_cuda_matvec_experts(ggml_type, w.data_ptr() + g * one, one, n_experts, ids.data_ptr(), k,
+                                              x.data_ptr(), 0, ws.data_ptr() + off, ws.numel() - off, 0,
+                                              yg.data_ptr(), rows, rows, cols, 0, s) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(y[g * k:(g + 1) * k], yg)
+        assert bool((yg[1] == -3.0).all())
+    assert K.status() == 0
+    # a stack length that is not groups * n_experts matrices is refused
+    assert lib.pyrite_cuda_matvec_expert_groups(ggml_type, w.data_ptr(), w.numel() - one, n_experts, groups,
+                                                ids.data_ptr(), k, x.data_ptr(), 0, ws.data_ptr() + off,
+                                                ws.numel() - off, 0, y.data_ptr(), rows, rows, cols, 0, s) == -3
+
 def _moe_spec(d):
     from pyrite_b200.synthetic import MoESpec
     names = {f.name for f in fields(MoESpec)}
