@@ -283,6 +283,18 @@ int pyrite_cuda_moe_route(const float *router_logits, int n_experts, int top_k, 
                           double scale, int shard_count, int shard_index, int *expert_ids,
                           float *expert_weights, int *global_ids, void *stream);
 
+/* The router product (an F32 matrix of n_experts rows x hidden, type id 0, as
+ * the reference stores it) and pyrite_cuda_moe_route in one launch:
+ * router_logits receives the logits (accumulated in fp64 like the reference's
+ * products, rounded to fp32 once), then the last CTA to finish routes.  `ticket`: one zeroed unsigned in
+ * device memory, left at zero (one per concurrent call).  Other router types:
+ * PYRITE_E_TYPE (use pyrite_cuda_matvec + pyrite_cuda_moe_route). */
+int pyrite_cuda_moe_router_route(int router_type, const void *router, size_t router_len, size_t hidden,
+                                 const float *x, float *router_logits, int n_experts, int top_k,
+                                 int norm_topk_prob, double scale, int shard_count, int shard_index,
+                                 int *expert_ids, float *expert_weights, int *global_ids, unsigned *ticket,
+                                 void *stream);
+
 /* The batch-1 product over n_sel routed slices of a stacked expert tensor in
  * one launch: `stacked` holds n_experts matrices of rows x cols back to back
  * (expert e at e * rows * row_bytes, qwen3_moe.py:364-398); expert_ids

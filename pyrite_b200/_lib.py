@@ -61,6 +61,9 @@ SIGNATURES: dict[str, tuple] = {
                                                   _VP, _SZ, _VP)),
     "pyrite_cuda_moe_route": (ctypes.c_int, (_VP, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_double,
                                              ctypes.c_int, ctypes.c_int, _VP, _VP, _VP, _VP)),
+    "pyrite_cuda_moe_router_route": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _SZ, _VP, _VP, ctypes.c_int, ctypes.c_int,
+                                                    ctypes.c_int, ctypes.c_double, ctypes.c_int, ctypes.c_int, _VP,
+                                                    _VP, _VP, _VP, _VP)),
     "pyrite_cuda_matvec_experts": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _SZ, _VP, _SZ, _VP, _SZ, _VP, _SZ, _SZ,
                                                   _VP, _SZ, _SZ, _SZ, ctypes.c_uint, _VP)),
     "pyrite_cuda_matvec_expert_groups": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _SZ, _SZ, _VP, _SZ, _VP, _SZ, _VP,

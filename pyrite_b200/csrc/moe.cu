@@ -24,23 +24,35 @@
 namespace pyr {
 namespace {
 
-// One CTA (256 threads): n <= 4096 router logits, k <= 32.
+struct RouteArgs {
+  int n, k, norm;
+  double scale;
+  int shards, index;
+  int* ids;
+  float* weights;
+  int* global_ids;
+};
+
+// The routing of one token by one CTA (256 threads): n <= 4096 router logits
+// (read through L2: other CTAs may just have written them), k <= 32.
 // Experts sharded by id over `shards` GPUs: this one (shard `index`) holds
 // experts e % shards == index at local slot e / shards; a selected expert it
 // does not hold gets id -1 and weight 0 (the expert matvecs skip it).
-__global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict__ logits, int n, int k, int norm,
-                                                        double scale, int shards, int index, int* __restrict__ ids,
-                                                        float* __restrict__ weights, int* __restrict__ global_ids) {
+__device__ void route_block(const float* __restrict__ logits, const RouteArgs& a) {
   __shared__ double p[4096];
   __shared__ double dred[32];
   __shared__ int wi[32];
   __shared__ double chosen_p[32];
   __shared__ int chosen_i[32];
-  pdl_wait();
+  const int n = a.n, k = a.k, norm = a.norm, shards = a.shards, index = a.index;
+  const double scale = a.scale;
+  int* const ids = a.ids;
+  float* const weights = a.weights;
+  int* const global_ids = a.global_ids;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // softmax in fp64 (tensor_ops.py:513-521): exp(v - max) / sum
   double m = -DBL_MAX;
-  for (int e = tid; e < n; e += blockDim.x) m = fmax(m, (double)logits[e]);
+  for (int e = tid; e < n; e += blockDim.x) m = fmax(m, (double)__ldcg(logits + e));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0) dred[warp] = m;
@@ -50,7 +62,7 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict_
   __syncthreads();
   double s = 0.0;
   for (int e = tid; e < n; e += blockDim.x) {
-    const double x = exp((double)logits[e] - m);
+    const double x = exp((double)__ldcg(logits + e) - m);
     p[e] = x;
     s += x;
   }
@@ -106,6 +118,54 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict_
       weights[r] = mine ? (float)w : 0.0f;
       if (global_ids) global_ids[r] = e;
     }
+  }
+}
+
+__global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict__ logits, RouteArgs a) {
+  pdl_wait();
+  route_block(logits, a);
+  pdl_launch_dependents();
+}
+
+// The F32 router matvec and the routing in one launch.  CTA r computes logit
+// r: every thread a strided share of the row in fp64 (the reference's native
+// products accumulate in fp64), one fixed-order block sum, rounded to fp32
+// once -- one round trip to memory per CTA instead of a warp walking the row.
+// The last CTA to finish (a ticket, no CTA waits) routes.  W: E rows of h F32
+// values; float4 loads when W and x are 16-byte aligned and h % 4 == 0.
+__global__ void __launch_bounds__(256) moe_router_route_kernel(const float* __restrict__ W, int h,
+                                                               const float* __restrict__ x,
+                                                               float* __restrict__ logits, unsigned* ticket,
+                                                               RouteArgs a) {
+  __shared__ double dshm[32];
+  __shared__ int last;
+  pdl_wait();
+  const int r = blockIdx.x, tid = threadIdx.x;
+  const float* rf = W + (size_t)r * (size_t)h;
+  double acc = 0.0;
+  if ((((uintptr_t)rf | (uintptr_t)x) & 15) == 0 && (h & 3) == 0) {
+    for (int c = 4 * tid; c < h; c += 4 * (int)blockDim.x) {
+      const float4 w4 = __ldg(reinterpret_cast<const float4*>(rf + c));
+      const float4 x4 = __ldcg(reinterpret_cast<const float4*>(x + c));
+      acc += (double)w4.x * (double)x4.x;
+      acc += (double)w4.y * (double)x4.y;
+      acc += (double)w4.z * (double)x4.z;
+      acc += (double)w4.w * (double)x4.w;
+    }
+  } else {
+    for (int c = tid; c < h; c += blockDim.x) acc += (double)__ldg(rf + c) * (double)__ldcg(x + c);
+  }
+  const double total = block_sum(acc, dshm);
+  if (tid == 0) {
+    logits[r] = (float)total;
+    __threadfence();
+    last = atomicAdd(ticket, 1u) == gridDim.x - 1 ? 1 : 0;
+  }
+  __syncthreads();
+  if (last) {
+    __threadfence();
+    route_block(logits, a);
+    if (tid == 0) *ticket = 0u;
   }
   pdl_launch_dependents();
 }
@@ -163,9 +223,25 @@ int pyrite_cuda_moe_route(const float* router_logits, int n_experts, int top_k, 
       top_k > 32 || top_k > n_experts || !(scale > 0.0) || shard_count <= 0 || shard_index < 0 ||
       shard_index >= shard_count)
     return PYRITE_E_SHAPE;
-  return rc(launch_pdl(moe_route_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), router_logits,
-                       n_experts, top_k, norm_topk_prob ? 1 : 0, scale, shard_count, shard_index, expert_ids,
-                       expert_weights, global_ids));
+  RouteArgs a{n_experts, top_k, norm_topk_prob ? 1 : 0, scale, shard_count, shard_index, expert_ids, expert_weights,
+              global_ids};
+  return rc(launch_pdl(moe_route_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), router_logits, a));
+}
+
+int pyrite_cuda_moe_router_route(int router_type, const void* router, size_t router_len, size_t hidden,
+                                 const float* x, float* router_logits, int n_experts, int top_k, int norm_topk_prob,
+                                 double scale, int shard_count, int shard_index, int* expert_ids,
+                                 float* expert_weights, int* global_ids, unsigned* ticket, void* stream) {
+  if (router_type != 0) return PYRITE_E_TYPE;  // F32 routers (the reference keeps them unquantized)
+  if (!router || !x || !router_logits || !ticket || !expert_ids || !expert_weights || n_experts <= 0 ||
+      n_experts > 4096 || top_k <= 0 || top_k > 32 || top_k > n_experts || !(scale > 0.0) || shard_count <= 0 ||
+      shard_index < 0 || shard_index >= shard_count || hidden == 0 || hidden > 0x7fffffffu)
+    return PYRITE_E_SHAPE;
+  if (router_len != (size_t)n_experts * hidden * 4 || ((uintptr_t)router & 3)) return PYRITE_E_BUFFER;
+  RouteArgs a{n_experts, top_k, norm_topk_prob ? 1 : 0, scale, shard_count, shard_index, expert_ids, expert_weights,
+              global_ids};
+  return rc(launch_pdl(moe_router_route_kernel, dim3(n_experts), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       static_cast<const float*>(router), (int)hidden, x, router_logits, ticket, a));
 }
 
 int pyrite_cuda_matvec_experts(int type_id, const void* stacked, size_t stacked_len, size_t n_experts,

@@ -165,6 +165,7 @@ class MixedDecoder:
         if self.moe:
             ff, E, k = spec.moe_intermediate_size, spec.num_experts, spec.num_experts_per_tok
             self.router_logits = z(E)
+            self.route_ticket = z(1, dt=torch.int32)
             self.expert_ids, self.expert_w = z(k, dt=torch.int32), z(k)
             self.gate_up_out = z(2 * k, ff)  # [gate_j | up_j] of the selected experts
             self.gate, self.up = self.gate_up_out[:k], self.gate_up_out[k:]
@@ -281,6 +282,22 @@ class MixedDecoder:
             k, x.data_ptr(), x_stride, wptr, wlen, ws_stride, y.data_ptr(), y.shape[-1], m.rows, m.cols, 0, stream)
         _check(code, "expert matvec")
 
+    def _route(self, ly: _Layer, li: int, stream: int) -> None:
+        """Router logits and top-k routing (one launch for an F32 router)."""
+        s, L = self.spec, self.lib
+        k, norm = s.num_experts_per_tok, 1 if s.norm_topk_prob else 0
+        if ly.router.ggml_type == F32:
+            _check(L.pyrite_cuda_moe_router_route(
+                F32, ly.router.data.data_ptr(), ly.router.data.numel(), ly.router.cols, self.normed.data_ptr(),
+                self.router_logits.data_ptr(), s.num_experts, k, norm, 1.0, self.expert_shards, self.expert_shard,
+                self.expert_ids.data_ptr(), self.expert_w.data_ptr(), self.route_log[li].data_ptr(),
+                self.route_ticket.data_ptr(), stream), "router+route")
+            return
+        self._mv(ly.router, self.normed, self.ws_h, self.router_logits, 0, stream)
+        _check(L.pyrite_cuda_moe_route(self.router_logits.data_ptr(), s.num_experts, k, norm, 1.0, self.expert_shards,
+                                       self.expert_shard, self.expert_ids.data_ptr(), self.expert_w.data_ptr(),
+                                       self.route_log[li].data_ptr(), stream), "route")
+
     def _gate_up_experts(self, ly: _Layer, stream: int) -> None:
         if ly.gate_up_exps is not None:
             self._experts(ly.gate_up_exps, self.normed, 0, self.ws_h, 0, self.gate_up_out, stream, groups=2)
@@ -324,11 +341,7 @@ class MixedDecoder:
             self._norm(self.hidden, ly.ffn_norm, self.normed, self.ws_h, stream)
             # routed feed-forward
             k = s.num_experts_per_tok
-            self._mv(ly.router, self.normed, self.ws_h, self.router_logits, 0, stream)
-            _check(L.pyrite_cuda_moe_route(self.router_logits.data_ptr(), s.num_experts, k,
-                                           1 if s.norm_topk_prob else 0, 1.0, self.expert_shards, self.expert_shard,
-                                           self.expert_ids.data_ptr(), self.expert_w.data_ptr(),
-                                           self.route_log[li].data_ptr(), stream), "route")
+            self._route(ly, li, stream)
             self._gate_up_experts(ly, stream)
             wa, wal = self._wsp(self.ws_act)
             _check(L.pyrite_cuda_moe_silu_mul_encode(self.gate.data_ptr(), self.up.data_ptr(), ff, k,

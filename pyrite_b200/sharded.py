@@ -121,6 +121,7 @@ class ShardedDecoder(MixedDecoder):
             ff, k = spec.moe_intermediate_size, spec.num_experts_per_tok
             self.n_local_experts = len(owned_experts(spec.num_experts, world, rank))
             self.router_logits = z(spec.num_experts)
+            self.route_ticket = z(1, dt=torch.int32)
             self.expert_ids, self.expert_w = z(k, dt=torch.int32), z(k)
             self.gate_up_out = z(2 * k, ff)
             self.gate, self.up = self.gate_up_out[:k], self.gate_up_out[k:]
@@ -197,11 +198,7 @@ class ShardedDecoder(MixedDecoder):
             else:
                 self._norm(self.hidden, ly.ffn_norm, self.normed, self.ws_h, stream)
                 k = s.num_experts_per_tok
-                self._mv(ly.router, self.normed, self.ws_h, self.router_logits, 0, stream)
-                _check(L.pyrite_cuda_moe_route(self.router_logits.data_ptr(), s.num_experts, k,
-                                               1 if s.norm_topk_prob else 0, 1.0, self.world, self.rank,
-                                               self.expert_ids.data_ptr(), self.expert_w.data_ptr(),
-                                               self.route_log[li].data_ptr(), stream), "route")
+                self._route(ly, li, stream)
                 self._gate_up_experts(ly, stream)
                 wa, wal = self._wsp(self.ws_act)
                 _check(L.pyrite_cuda_moe_silu_mul_encode(self.gate.data_ptr(), self.up.data_ptr(), ff, k,

@@ -139,6 +139,44 @@ def test_expert_groups_equal_one_call_per_stack(cuda_device, ggml_type, cols, gr
                                                 ids.data_ptr(), k, x.data_ptr(), 0, ws.data_ptr() + off,
                                                 ws.numel() - off, 0, y.data_ptr(), rows, rows, cols, 0, s) == -3
 
+
+@pytest.mark.parametrize("E,h,k,shards,index", [(128, 2048, 8, 1, 0), (16, 256, 4, 2, 1), (60, 1024, 6, 4, 3)])
+def test_router_route_equals_matvec_then_route(cuda_device, E, h, k, shards, index):
+    """pyrite_cuda_moe_router_route (one launch): logits within fp32 rounding
+    of the fp64 product, and the ids, weights and global ids that
+    pyrite_cuda_moe_route gives for those logits; the ticket is left at zero."""
+    import torch
+
+    from pyrite_b200 import _lib
+    lib = _lib.require()
+    g = torch.Generator("cuda").manual_seed(E * h + k)
+    router = torch.randn(E, h, device="cuda", generator=g) * 0.02
+    s = torch.cuda.current_stream().cuda_stream
+    ticket = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for rep in range(3):
+        x = torch.randn(h, device="cuda", generator=g)
+        got_l = torch.empty(E, device="cuda")
+        got = [torch.full((k,), -5, dtype=torch.int32, device="cuda"), torch.zeros(k, device="cuda"),
+               torch.zeros(k, dtype=torch.int32, device="cuda")]
+        assert lib.pyrite_cuda_moe_router_route(0, router.data_ptr(), router.numel() * 4, h, x.data_ptr(),
+                                                got_l.data_ptr(), E, k, 1, 1.0, shards, index, got[0].data_ptr(),
+                                                got[1].data_ptr(), got[2].data_ptr(), ticket.data_ptr(), s) == 0
+        exact = (router.double() @ x.double()).float()
+        assert torch.allclose(got_l, exact, rtol=2e-7, atol=1e-9)
+        want_l = got_l.clone()
+        want = [torch.full((k,), -5, dtype=torch.int32, device="cuda"), torch.zeros(k, device="cuda"),
+                torch.zeros(k, dtype=torch.int32, device="cuda")]
+        assert lib.pyrite_cuda_moe_route(want_l.data_ptr(), E, k, 1, 1.0, shards, index, want[0].data_ptr(),
+                                         want[1].data_ptr(), want[2].data_ptr(), s) == 0
+        torch.cuda.synchronize()
+        for a, b in zip(got, want):
+            assert torch.equal(a, b)
+        assert int(ticket.item()) == 0
+    # quantized routers are not taken
+    assert lib.pyrite_cuda_moe_router_route(8, router.data_ptr(), router.numel(), h, x.data_ptr(), got_l.data_ptr(),
+                                            E, k, 1, 1.0, 1, 0, got[0].data_ptr(), got[1].data_ptr(), None,
+                                            ticket.data_ptr(), s) == -1
+
 def _moe_spec(d):
     from pyrite_b200.synthetic import MoESpec
     names = {f.name for f in fields(MoESpec)}
