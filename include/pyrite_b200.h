@@ -295,6 +295,19 @@ int pyrite_cuda_moe_router_route(int router_type, const void *router, size_t rou
                                  int *expert_ids, float *expert_weights, int *global_ids, unsigned *ticket,
                                  void *stream);
 
+/* As pyrite_cuda_moe_router_route with x the residual stream: the launch
+ * also computes x' = RMSNorm(x) * norm_weight (fp64 statistics, as
+ * pyrite_cuda_rmsnorm_encode), routes on W x', and writes x' to `normed` and
+ * its encoding to `workspace` (as pyrite_cuda_rmsnorm_encode does) for the
+ * expert products.  hidden % 32 == 0; router, x, norm_weight, normed 16-byte
+ * aligned, workspace 256-byte aligned. */
+int pyrite_cuda_moe_norm_router_route(int router_type, const void *router, size_t router_len, size_t hidden,
+                                      const float *x, const float *norm_weight, double eps, float *normed,
+                                      void *workspace, size_t workspace_len, float *router_logits,
+                                      int n_experts, int top_k, int norm_topk_prob, double scale,
+                                      int shard_count, int shard_index, int *expert_ids,
+                                      float *expert_weights, int *global_ids, unsigned *ticket, void *stream);
+
 /* The batch-1 product over n_sel routed slices of a stacked expert tensor in
  * one launch: `stacked` holds n_experts matrices of rows x cols back to back
  * (expert e at e * rows * row_bytes, qwen3_moe.py:364-398); expert_ids
@@ -332,6 +345,7 @@ int pyrite_cuda_moe_silu_mul_encode(const float *gate, const float *up, size_t f
 /* hidden[i] += sum_j expert_weights[j] * expert_out[j * h + i], j ascending. */
 int pyrite_cuda_moe_combine(const float *expert_out, const float *expert_weights, size_t n_sel, size_t h,
                             float *hidden, void *stream);
+
 
 /* Static description of a return code. */
 const char *pyrite_error_string(int code);

@@ -133,17 +133,40 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict_
 // once -- one round trip to memory per CTA instead of a warp walking the row.
 // The last CTA to finish (a ticket, no CTA waits) routes.  W: E rows of h F32
 // values; float4 loads when W and x are 16-byte aligned and h % 4 == 0.
+struct RouterNorm {  // x is the residual: RMSNorm it first (nw != nullptr)
+  const float* nw;
+  double eps;
+  float* out;    // the normalised x (fp32), written by CTA 0
+  uint8_t* ws;   // and its encoding for the expert products
+};
+
 __global__ void __launch_bounds__(256) moe_router_route_kernel(const float* __restrict__ W, int h,
                                                                const float* __restrict__ x,
                                                                float* __restrict__ logits, unsigned* ticket,
-                                                               RouteArgs a) {
+                                                               RouteArgs a, RouterNorm nm) {
   __shared__ double dshm[32];
   __shared__ int last;
   pdl_wait();
   const int r = blockIdx.x, tid = threadIdx.x;
   const float* rf = W + (size_t)r * (size_t)h;
   double acc = 0.0;
-  if ((((uintptr_t)rf | (uintptr_t)x) & 15) == 0 && (h & 3) == 0) {
+  if (nm.nw) {  // every CTA computes the same statistics; the row takes the normalised values
+    float4 x0[4];
+    const double inv = cta_rms_inv(x, h, nm.eps, dshm, x0);
+    for (int g = tid; g < h / 16; g += blockDim.x) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 xv = g == tid ? x0[q] : __ldcg(reinterpret_cast<const float4*>(x + 16 * g) + q);
+        const float4 wv = __ldg(reinterpret_cast<const float4*>(nm.nw + 16 * g) + q);
+        const float4 rv = __ldg(reinterpret_cast<const float4*>(rf + 16 * g) + q);
+        acc += (double)rv.x * (double)(float)((double)xv.x * inv * (double)wv.x);
+        acc += (double)rv.y * (double)(float)((double)xv.y * inv * (double)wv.y);
+        acc += (double)rv.z * (double)(float)((double)xv.z * inv * (double)wv.z);
+        acc += (double)rv.w * (double)(float)((double)xv.w * inv * (double)wv.w);
+      }
+    }
+    if (r == 0) cta_rmsnorm_encode(x, nm.nw, h, nm.eps, nm.out, nm.ws, dshm);
+  } else if ((((uintptr_t)rf | (uintptr_t)x) & 15) == 0 && (h & 3) == 0) {
     for (int c = 4 * tid; c < h; c += 4 * (int)blockDim.x) {
       const float4 w4 = __ldg(reinterpret_cast<const float4*>(rf + c));
       const float4 x4 = __ldcg(reinterpret_cast<const float4*>(x + c));
@@ -232,16 +255,34 @@ int pyrite_cuda_moe_router_route(int router_type, const void* router, size_t rou
                                  const float* x, float* router_logits, int n_experts, int top_k, int norm_topk_prob,
                                  double scale, int shard_count, int shard_index, int* expert_ids,
                                  float* expert_weights, int* global_ids, unsigned* ticket, void* stream) {
+  return pyrite_cuda_moe_norm_router_route(router_type, router, router_len, hidden, x, nullptr, 0.0, nullptr, nullptr,
+                                           0, router_logits, n_experts, top_k, norm_topk_prob, scale, shard_count,
+                                           shard_index, expert_ids, expert_weights, global_ids, ticket, stream);
+}
+
+int pyrite_cuda_moe_norm_router_route(int router_type, const void* router, size_t router_len, size_t hidden,
+                                      const float* x, const float* norm_weight, double eps, float* normed,
+                                      void* workspace, size_t workspace_len, float* router_logits, int n_experts,
+                                      int top_k, int norm_topk_prob, double scale, int shard_count, int shard_index,
+                                      int* expert_ids, float* expert_weights, int* global_ids, unsigned* ticket,
+                                      void* stream) {
   if (router_type != 0) return PYRITE_E_TYPE;  // F32 routers (the reference keeps them unquantized)
   if (!router || !x || !router_logits || !ticket || !expert_ids || !expert_weights || n_experts <= 0 ||
       n_experts > 4096 || top_k <= 0 || top_k > 32 || top_k > n_experts || !(scale > 0.0) || shard_count <= 0 ||
       shard_index < 0 || shard_index >= shard_count || hidden == 0 || hidden > 0x7fffffffu)
     return PYRITE_E_SHAPE;
   if (router_len != (size_t)n_experts * hidden * 4 || ((uintptr_t)router & 3)) return PYRITE_E_BUFFER;
+  RouterNorm nm{norm_weight, eps, normed, static_cast<uint8_t*>(workspace)};
+  if (norm_weight) {  // the norm prologue reads whole float4 groups; the encoding needs the workspace
+    if (!normed || !workspace || hidden % 32 || ((uintptr_t)router & 15) ||
+        (((uintptr_t)x | (uintptr_t)norm_weight | (uintptr_t)normed) & 15) || ((uintptr_t)workspace & 255) ||
+        workspace_len < pyrite_cuda_workspace_size(0, hidden, 1))
+      return PYRITE_E_BUFFER;
+  }
   RouteArgs a{n_experts, top_k, norm_topk_prob ? 1 : 0, scale, shard_count, shard_index, expert_ids, expert_weights,
               global_ids};
   return rc(launch_pdl(moe_router_route_kernel, dim3(n_experts), dim3(256), 0, static_cast<cudaStream_t>(stream),
-                       static_cast<const float*>(router), (int)hidden, x, router_logits, ticket, a));
+                       static_cast<const float*>(router), (int)hidden, x, router_logits, ticket, a, nm));
 }
 
 int pyrite_cuda_matvec_experts(int type_id, const void* stacked, size_t stacked_len, size_t n_experts,

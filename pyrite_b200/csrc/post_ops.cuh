@@ -156,22 +156,17 @@ __device__ __forceinline__ void load16(const float* p, float (&v)[16]) {  // thr
 // block_rmsnorm_encode for a CTA prologue (x, w 16-byte aligned, n % 32 == 0).
 // Each thread's first group of x and w stays in registers, so for n up to
 // 16 * blockDim.x the statistics and the encoding cost one round trip to L2.
-__device__ __forceinline__ void cta_rmsnorm_encode(const float* x, const float* w, int n, double eps, float* out,
-                                                   uint8_t* enc, double* shm) {
+// 1 / sqrt(mean(x^2) + eps) of n values (x 16-byte aligned, n % 16 == 0) for
+// the whole CTA, in a fixed order (every CTA that calls it gets the same
+// bits); x0 returns the thread's first 16-value group (zeros past the end).
+__device__ __forceinline__ double cta_rms_inv(const float* x, int n, double eps, double* shm, float4 (&x0)[4]) {
   const int G = n / 16, nt = blockDim.x, tid = threadIdx.x;
-  float4 x0[4], w0[4];
   double ss = 0.0;
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    x0[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-    w0[q] = x0[q];
-  }
+  for (int q = 0; q < 4; ++q) x0[q] = make_float4(0.f, 0.f, 0.f, 0.f);
   if (tid < G) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      x0[q] = __ldcg(reinterpret_cast<const float4*>(x + 16 * tid) + q);
-      w0[q] = __ldg(reinterpret_cast<const float4*>(w + 16 * tid) + q);
-    }
+    for (int q = 0; q < 4; ++q) x0[q] = __ldcg(reinterpret_cast<const float4*>(x + 16 * tid) + q);
   }
 #pragma unroll
   for (int q = 0; q < 4; ++q)
@@ -184,7 +179,20 @@ __device__ __forceinline__ void cta_rmsnorm_encode(const float* x, const float* 
     for (int i = 0; i < 16; ++i) ss += (double)v[i] * (double)v[i];
   }
   const double total = block_sum(ss, shm);
-  const double inv = 1.0 / sqrt(total / (double)(n > 0 ? n : 1) + eps);
+  return 1.0 / sqrt(total / (double)(n > 0 ? n : 1) + eps);
+}
+
+__device__ __forceinline__ void cta_rmsnorm_encode(const float* x, const float* w, int n, double eps, float* out,
+                                                   uint8_t* enc, double* shm) {
+  const int G = n / 16, nt = blockDim.x, tid = threadIdx.x;
+  float4 x0[4], w0[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) w0[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (tid < G) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) w0[q] = __ldg(reinterpret_cast<const float4*>(w + 16 * tid) + q);
+  }
+  const double inv = cta_rms_inv(x, n, eps, shm, x0);
   for (int g0 = 0; g0 < G; g0 += nt) {  // same trip count in every thread
     const int g = g0 + tid;
     const bool on = g < G;

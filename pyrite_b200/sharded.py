@@ -196,17 +196,14 @@ class ShardedDecoder(MixedDecoder):
                           stream)
                 self._mvx(ly.down, self.gu, _lib.X_SILU_MUL, None, self.act, self.ws_act, self.part, 0, stream)
             else:
-                self._norm(self.hidden, ly.ffn_norm, self.normed, self.ws_h, stream)
                 k = s.num_experts_per_tok
                 self._route(ly, li, stream)
                 self._gate_up_experts(ly, stream)
                 wa, wal = self._wsp(self.ws_act)
                 _check(L.pyrite_cuda_moe_silu_mul_encode(self.gate.data_ptr(), self.up.data_ptr(), ff, k,
                                                          self.act.data_ptr(), wa, wal, stream), "moe silu")
-                self._experts(ly.down_exps, self.act, ff, self.ws_act, self.ws_act[2], self.down, stream)
                 self.part.zero_()
-                _check(L.pyrite_cuda_moe_combine(self.down.data_ptr(), self.expert_w.data_ptr(), k, h,
-                                                 self.part.data_ptr(), stream), "combine")
+                self._down_combine(ly, self.part, stream)
             self._allreduce_into_hidden()
         self._norm(self.hidden, self.out_norm, self.normed, self.ws_h, stream)
         self._mv(self.lm_head, self.normed, self.ws_h, self.logits_local, 0, stream)

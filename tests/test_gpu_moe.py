@@ -177,6 +177,56 @@ def test_router_route_equals_matvec_then_route(cuda_device, E, h, k, shards, ind
                                             E, k, 1, 1.0, 1, 0, got[0].data_ptr(), got[1].data_ptr(), None,
                                             ticket.data_ptr(), s) == -1
 
+
+@pytest.mark.parametrize("E,h,k", [(128, 2048, 8), (16, 256, 4)])
+def test_norm_router_route_equals_norm_then_router_route(cuda_device, E, h, k):
+    """pyrite_cuda_moe_norm_router_route (RMSNorm in the routing launch) writes
+    the same normed vector, encoding, logits and routing as
+    pyrite_cuda_rmsnorm_encode followed by pyrite_cuda_moe_router_route."""
+    import torch
+
+    from pyrite_b200 import _lib
+    lib = _lib.require()
+    g = torch.Generator("cuda").manual_seed(h + k)
+    router = torch.randn(E, h, device="cuda", generator=g) * 0.02
+    nw = torch.rand(h, device="cuda", generator=g) + 0.5
+    x = torch.randn(h, device="cuda", generator=g) * 3
+    s = torch.cuda.current_stream().cuda_stream
+    per = int(lib.pyrite_cuda_workspace_size(0, h, 1))
+
+    def ws():
+        b = torch.zeros(per + 256, dtype=torch.uint8, device="cuda")
+        off = (-b.data_ptr()) % 256
+        return b, b.data_ptr() + off, b.numel() - off, off
+
+    def outs():
+        return (torch.empty(E, device="cuda"), torch.full((k,), -5, dtype=torch.int32, device="cuda"),
+                torch.zeros(k, device="cuda"), torch.zeros(k, dtype=torch.int32, device="cuda"))
+
+    ticket = torch.zeros(1, dtype=torch.int32, device="cuda")
+    nb, nptr, nlen, noff = ws()
+    normed = torch.empty(h, device="cuda")
+    got = outs()
+    assert lib.pyrite_cuda_moe_norm_router_route(0, router.data_ptr(), router.numel() * 4, h, x.data_ptr(),
+                                                 nw.data_ptr(), 1e-6, normed.data_ptr(), nptr, nlen,
+                                                 got[0].data_ptr(), E, k, 1, 1.0, 1, 0, got[1].data_ptr(),
+                                                 got[2].data_ptr(), got[3].data_ptr(), ticket.data_ptr(), s) == 0
+    rb, rptr, rlen, roff = ws()
+    ref_n = torch.empty(h, device="cuda")
+    assert lib.pyrite_cuda_rmsnorm_encode(x.data_ptr(), nw.data_ptr(), h, 1e-6, ref_n.data_ptr(), rptr, rlen, s) == 0
+    want = outs()
+    assert lib.pyrite_cuda_moe_router_route(0, router.data_ptr(), router.numel() * 4, h, ref_n.data_ptr(),
+                                            want[0].data_ptr(), E, k, 1, 1.0, 1, 0, want[1].data_ptr(),
+                                            want[2].data_ptr(), want[3].data_ptr(), ticket.data_ptr(), s) == 0
+    torch.cuda.synchronize()
+    # the same fp64 statistics up to summation order: equal to within an ulp
+    assert torch.allclose(normed, ref_n, rtol=2e-7, atol=0)
+    assert np.mean((nb[noff:noff + per] == rb[roff:roff + per]).cpu().numpy()) > 0.999
+    assert torch.allclose(got[0], want[0], rtol=1e-6, atol=1e-7)
+    for a, b in zip(got[1:], want[1:]):
+        assert torch.equal(a, b)
+    assert int(ticket.item()) == 0
+
 def _moe_spec(d):
     from pyrite_b200.synthetic import MoESpec
     names = {f.name for f in fields(MoESpec)}
