@@ -320,7 +320,7 @@ def run_ours(args) -> None:
     models = None
     if not args.no_models:  # every rank takes part (tensor parallel when world > 1)
         models = {}
-        for which in ("c3", "c4"):
+        for which in ("c3", "c4", "c5"):
             models[which] = model_leg(dev, which, world, rank, pg)
             torch.cuda.empty_cache()
 
@@ -430,8 +430,9 @@ def batched_leg(dev, W, X, wl, stream, ncols_list=(8, 64)) -> dict:
 
 # ---------------------------------------------------------------- model legs
 def model_leg(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
-    """Batch-1 decode throughput of a full-depth configs[2] (Llama-3-8B Q4_K_M)
-    or configs[3] (Qwen3-30B-A3B Q4_K_M MoE) model: the prompt is processed one
+    """Batch-1 decode throughput of a full-depth configs[2] (Llama-3-8B Q4_K_M),
+    configs[3] (Qwen3-30B-A3B Q4_K_M MoE) or configs[4] (Qwen3-235B-A22B
+    Q4_K_M MoE, ~142 GB) model: the prompt is processed one
     token at a time (as the reference does), then greedy decode; one CUDA graph
     per step, CUDA events around the decode steps.  Layer weights: layers 0 and
     1 are generated from their seeds, every other layer holds its own HBM copy
@@ -452,10 +453,15 @@ def model_leg(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
         spec, prefill, new, ctx = DenseSpec.c3(), 512, 128, 4096
         cfg = ("configs[2]: Llama-3-8B-shaped, Q4_K_M mix, 32 layers, prefill 512 seeded tokens (one per step), "
                "batch-1 decode of 128 tokens, KV ctx 4096")
-    else:
+    elif which == "c4":
         spec, prefill, new, ctx = MoESpec.c4(), 256, 128, 1024
         cfg = ("configs[3]: Qwen3-30B-A3B-shaped MoE, Q4_K_M mix, 48 layers, 128 experts top-8, prefill 256 "
                "seeded tokens (one per step), batch-1 decode of 128 tokens")
+    else:
+        spec, prefill, new, ctx = MoESpec.c5(), 1024, 256, 8192
+        cfg = ("configs[4]: Qwen3-235B-A22B-shaped MoE, Q4_K_M mix (~142 GB), 94 layers, 64 q / 4 kv heads, "
+               "128 experts top-8, expert ffn 1536, prefill 1024 seeded tokens (one per step), batch-1 decode of "
+               "256 tokens, KV ctx 8192")
     t0 = _t.time()
     if world > 1:
         from pyrite_b200.sharded import ShardedDecoder

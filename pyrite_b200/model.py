@@ -78,16 +78,17 @@ class MixedDecoder:
         self.max_ctx = max_ctx
         self.lib = L = _lib.require()
         h = spec.hidden_size
-        host: dict[str, torch.Tensor] = {}
+        first: dict[str, torch.Tensor] = {}  # replicate: the uploaded layer-0/1 tensors
 
         def raw(name: str) -> torch.Tensor:
             if replicate and name.startswith("blk."):
                 parts = name.split(".")
                 parts[1] = str(int(parts[1]) % 2)
                 src = ".".join(parts)
-                if src not in host:
-                    host[src] = torch.frombuffer(bytearray(tensors[src][2]), dtype=torch.uint8)
-                return host[src].to(d)  # a device copy of its own per layer
+                if src not in first:  # first use: upload; later layers: a device copy of their own
+                    first[src] = torch.frombuffer(bytearray(tensors[src][2]), dtype=torch.uint8).to(d)
+                    return first[src]
+                return first[src].clone()
             return torch.frombuffer(bytearray(tensors[name][2]), dtype=torch.uint8).to(d)
 
         def meta(name: str) -> tuple[tuple[int, ...], int]:
@@ -153,7 +154,7 @@ class MixedDecoder:
                     ly.gate, ly.up = g, u
                 ly.down = mat(p + "ffn_down.weight")
             self.layers.append(ly)
-        host.clear()
+        first.clear()
         self.n_stack_experts = spec.num_experts if self.moe else 0
         self._pair_expert_stacks()
 

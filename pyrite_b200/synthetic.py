@@ -69,6 +69,26 @@ def _weights(name: str, count: int, seed: int) -> np.ndarray:
     return rng.normal(0.0, 0.02, count).astype(np.float32)
 
 
+def _weights_chunked(name: str, count: int, seed: int, chunk: int = 1 << 22) -> np.ndarray:
+    """Seeded N(0, 0.02) float32 weights drawn in independently seeded chunks
+    on all host cores (the ~10^10-value checkpoints of configs[4]): chunk i of
+    tensor `name` comes from default_rng([crc32(name), seed, i])."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+
+    out = np.empty(count, dtype=np.float32)
+    key = zlib.crc32(name.encode())
+
+    def fill(i: int) -> None:
+        part = out[i * chunk:(i + 1) * chunk]
+        np.random.default_rng([key, seed & 0xFFFFFFFF, i]).standard_normal(part.shape[0], dtype=np.float32, out=part)
+        part *= np.float32(0.02)
+
+    with ThreadPoolExecutor(max(1, os.cpu_count() or 1)) as ex:
+        list(ex.map(fill, range((count + chunk - 1) // chunk)))
+    return out
+
+
 def metadata(spec: DenseSpec) -> dict[str, object]:
     """GGUF metadata keys the reference reads (``dense.py:113-186``)."""
     a = spec.architecture
@@ -161,6 +181,7 @@ class MoESpec:
     context_length: int = 40960
     seed: int = 20240607
     qk_norm: bool = True
+    chunked_weights: bool = False  # weights from _weights_chunked (configs[4] sizes)
 
     @property
     def q_dim(self) -> int:
@@ -174,6 +195,12 @@ class MoESpec:
     def c4(cls) -> "MoESpec":
         """Qwen3-30B-A3B-shaped, Q4_K_M mix."""
         return cls()
+
+    @classmethod
+    def c5(cls) -> "MoESpec":
+        """Qwen3-235B-A22B-shaped, Q4_K_M mix (~142 GB)."""
+        return cls(hidden_size=4096, num_hidden_layers=94, num_attention_heads=64, num_key_value_heads=4,
+                   intermediate_size=12288, moe_intermediate_size=1536, chunked_weights=True)
 
     @classmethod
     def tiny(cls) -> "MoESpec":
@@ -230,10 +257,12 @@ def moe_tensors(spec: MoESpec) -> Iterator[tuple[str, tuple[int, ...], int, byte
     ones = lambda n: np.ones(n, dtype=np.float32).tobytes()  # noqa: E731
     h, q, kv, ff, E = spec.hidden_size, spec.q_dim, spec.kv_dim, spec.moe_intermediate_size, spec.num_experts
 
+    gen = _weights_chunked if spec.chunked_weights else _weights
+
     def mat(name: str, dims: tuple[int, ...]) -> tuple[str, tuple[int, ...], int, bytes]:
         t = moe_tensor_type(spec, name)
         count = int(np.prod(dims))
-        w = _weights(name, count, spec.seed)
+        w = gen(name, count, spec.seed)
         return name, dims, t, (w.tobytes() if t == F32 else quantize(t, w))
 
     yield mat("token_embd.weight", (h, spec.vocab_size))

@@ -9,6 +9,7 @@ and the experts routed at every layer of every pass:
 
     python tests/golden/make_moe_golden.py --spec tiny --out moe_tiny.json
     python tests/golden/make_moe_golden.py --spec c4 --layers 2 --out moe_c4_2l.json
+    python tests/golden/make_moe_golden.py --spec c5 --layers 2 --out moe_c5_2l.json
 
 Needs the reference tree (``PYRITE_REF_ROOT``, default /root/reference); the
 committed JSON is what the tests read.
@@ -31,7 +32,7 @@ REF = Path(os.environ.get("PYRITE_REF_ROOT", "/root/reference"))
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--spec", choices=("tiny", "c4"), default="tiny")
+    ap.add_argument("--spec", choices=("tiny", "c4", "c5"), default="tiny")
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--vocab", type=int, default=None)
     ap.add_argument("--prompt", type=int, default=8)
@@ -41,7 +42,7 @@ def main() -> None:
 
     from pyrite_b200.synthetic import MoESpec, moe_metadata, moe_tensors, prompt_ids
 
-    spec = MoESpec.tiny() if args.spec == "tiny" else MoESpec.c4()
+    spec = {"tiny": MoESpec.tiny, "c4": MoESpec.c4, "c5": MoESpec.c5}[args.spec]()
     if args.layers is not None:
         spec = replace(spec, num_hidden_layers=args.layers)
     if args.vocab is not None:

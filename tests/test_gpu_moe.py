@@ -233,11 +233,13 @@ def _moe_spec(d):
     return MoESpec(**{k: v for k, v in d["spec"].items() if k in names})
 
 
-@pytest.mark.parametrize("golden", ["moe_tiny.json", "moe_c4_2l.json"])
+@pytest.mark.parametrize("golden", ["moe_tiny.json", "moe_c4_2l.json", "moe_c5_2l.json"])
 def test_moe_decode_matches_reference(cuda_device, golden):
     """Greedy ids, routed experts of every layer of every pass and top logits;
     moe_c4_2l is configs[3] at full width (hidden 2048, 128 experts top-8,
-    expert ffn 768, vocab 151936) with 2 layers."""
+    expert ffn 768, vocab 151936) with 2 layers, moe_c5_2l configs[4] at full
+    width (hidden 4096, 64 q / 4 kv heads, 128 experts top-8, expert ffn 1536)
+    with 2 layers."""
     import torch
 
     from pyrite_b200.kernels import cuda as K
