@@ -103,7 +103,10 @@ class ShardedDecoder(MixedDecoder):
                 for comp in ("gate", "up", "down"):
                     dims, t, payload = tensors[src(p + f"ffn_{comp}_exps.weight")]
                     per = dims[1] * row_bytes(t, dims[0])
-                    local = b"".join(payload[e * per:(e + 1) * per] for e in mine)
+                    if len(payload) == len(mine) * per:  # drawn for this GPU only (chunked specs)
+                        local = payload
+                    else:
+                        local = b"".join(payload[e * per:(e + 1) * per] for e in mine)
                     setattr(ly, f"{comp}_exps", _Mat(t, dev(local), dims[1], dims[0]))
             else:
                 f0, f1 = even_range(spec.intermediate_size, world, rank)
@@ -164,8 +167,12 @@ class ShardedDecoder(MixedDecoder):
         if replicate:
             from dataclasses import replace
             gen_spec = replace(spec, num_hidden_layers=min(2, spec.num_hidden_layers))
-        gen = moe_tensors if isinstance(spec, MoESpec) else dense_tensors
-        tensors = {name: (dims, t, payload) for name, dims, t, payload in gen(gen_spec)}
+        if isinstance(spec, MoESpec):  # chunked specs draw only this GPU's experts
+            subset = owned_experts(spec.num_experts, world, rank) if spec.chunked_weights else None
+            items = moe_tensors(gen_spec, experts=subset)
+        else:
+            items = dense_tensors(gen_spec)
+        tensors = {name: (dims, t, payload) for name, dims, t, payload in items}
         return cls(spec, tensors, rank, world, device=device, max_ctx=max_ctx, replicate=replicate, group=group)
 
     # ------------------------------------------------------------------ one step

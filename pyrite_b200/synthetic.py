@@ -89,6 +89,35 @@ def _weights_chunked(name: str, count: int, seed: int, chunk: int = 1 << 22) -> 
     return out
 
 
+def _weights_chunked_ranges(name: str, count: int, seed: int, ranges: list[tuple[int, int]],
+                            chunk: int = 1 << 22) -> np.ndarray:
+    """Values [a, b) for each (a, b) of ``ranges``, concatenated, of
+    ``_weights_chunked(name, count, seed)``, drawing only the chunks they
+    touch (one GPU's experts of a configs[4] stack)."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+
+    key = zlib.crc32(name.encode())
+    need = sorted({i for a, b in ranges for i in range(a // chunk, (b - 1) // chunk + 1)})
+
+    def draw(i: int) -> np.ndarray:
+        n = min(chunk, count - i * chunk)
+        part = np.random.default_rng([key, seed & 0xFFFFFFFF, i]).standard_normal(n, dtype=np.float32)
+        part *= np.float32(0.02)
+        return part
+
+    with ThreadPoolExecutor(max(1, os.cpu_count() or 1)) as ex:
+        chunks = dict(zip(need, ex.map(draw, need)))
+    out = np.empty(sum(b - a for a, b in ranges), dtype=np.float32)
+    o = 0
+    for a, b in ranges:
+        for i in range(a // chunk, (b - 1) // chunk + 1):
+            lo, hi = max(a, i * chunk), min(b, (i + 1) * chunk)
+            out[o:o + hi - lo] = chunks[i][lo - i * chunk:hi - i * chunk]
+            o += hi - lo
+    return out
+
+
 def metadata(spec: DenseSpec) -> dict[str, object]:
     """GGUF metadata keys the reference reads (``dense.py:113-186``)."""
     a = spec.architecture
@@ -251,18 +280,28 @@ def moe_metadata(spec: MoESpec) -> dict[str, object]:
     }
 
 
-def moe_tensors(spec: MoESpec) -> Iterator[tuple[str, tuple[int, ...], int, bytes]]:
+def moe_tensors(spec: MoESpec, experts: list[int] | None = None) -> Iterator[tuple[str, tuple[int, ...], int, bytes]]:
     """(name, GGML dims, GGML type, payload) of every tensor of the checkpoint.
-    A stacked expert tensor ``(cols, rows, E)`` is E matrices back to back."""
+    A stacked expert tensor ``(cols, rows, E)`` is E matrices back to back.
+    ``experts`` (chunked-weight specs only): the stacked tensors' payloads hold
+    just those experts, in that order (the bytes of the full tensor's slices),
+    and only their values are drawn."""
     ones = lambda n: np.ones(n, dtype=np.float32).tobytes()  # noqa: E731
     h, q, kv, ff, E = spec.hidden_size, spec.q_dim, spec.kv_dim, spec.moe_intermediate_size, spec.num_experts
 
     gen = _weights_chunked if spec.chunked_weights else _weights
 
+    if experts is not None and not spec.chunked_weights:
+        raise ValueError("expert subsets need a chunked-weight spec")
+
     def mat(name: str, dims: tuple[int, ...]) -> tuple[str, tuple[int, ...], int, bytes]:
         t = moe_tensor_type(spec, name)
         count = int(np.prod(dims))
-        w = gen(name, count, spec.seed)
+        if experts is not None and len(dims) == 3:  # one GPU's experts of a stack
+            per = dims[0] * dims[1]
+            w = _weights_chunked_ranges(name, count, spec.seed, [(e * per, (e + 1) * per) for e in experts])
+        else:
+            w = gen(name, count, spec.seed)
         return name, dims, t, (w.tobytes() if t == F32 else quantize(t, w))
 
     yield mat("token_embd.weight", (h, spec.vocab_size))

@@ -81,3 +81,23 @@ def test_two_rank_gloo_column_shards_and_allreduce():
         assert p.exitcode == 0
     for _, err, lm_ok in results:
         assert err < 1e-9 and lm_ok
+
+
+def test_chunked_expert_subset_equals_slices_of_full_stack():
+    """A GPU drawing only its experts of a chunked-weight checkpoint gets the
+    very bytes of those experts' slices of the full stacked tensors."""
+    from dataclasses import replace
+
+    from pyrite_b200.synthetic import MoESpec, moe_tensors
+    spec = replace(MoESpec.c5(), num_hidden_layers=1, hidden_size=256, moe_intermediate_size=256, num_experts=8,
+                   vocab_size=512, num_attention_heads=4, num_key_value_heads=2)
+    full = {n: (d, p) for n, d, _, p in moe_tensors(spec)}
+    mine = owned_experts(8, 4, 3)
+    for n, d, _, p in moe_tensors(spec, experts=mine):
+        fd, fp = full[n]
+        assert d == fd
+        if len(d) == 3:
+            per = len(fp) // 8
+            assert p == b"".join(fp[e * per:(e + 1) * per] for e in mine)
+        else:
+            assert p == fp
