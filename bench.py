@@ -510,6 +510,9 @@ def model_leg(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
     ms_tok = float(times[0].item()) / new
     pre_ms = float(times[1].item())
     dec.graph = None  # graphs holding NCCL calls go before the process group does
+    if pg:  # the NVLink sum's peer mappings, after every rank's last step
+        pg.barrier()
+        dec.close()
     out = {"config": cfg, "decode_tok_s": round(1000.0 / ms_tok, 1), "ms_per_token": round(ms_tok, 4),
            "prefill_tok_s": round((prefill - 1) * 1000.0 / pre_ms, 1),
            "n_gpus": world, "parallelism": f"tensor parallel x{world}" if world > 1 else "one GPU",

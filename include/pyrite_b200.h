@@ -347,6 +347,27 @@ int pyrite_cuda_moe_combine(const float *expert_out, const float *expert_weights
                             float *hidden, void *stream);
 
 
+/* ---- the decode step's sum across GPUs (tensor parallel) --------------------
+ * The partial residual updates of the ranks (n floats each, after the output
+ * and down projections) summed on every rank over NVLink peer memory, one
+ * kernel per call; replaces the reference-free NCCL allreduce of the
+ * sharded step (the reference runs on one host process).  Set-up, once per
+ * rank: pyrite_cuda_ipc_buffer_create(pyrite_cuda_allreduce_buffer_size(n))
+ * (zeroed), exchange the 64-byte handles, pyrite_cuda_ipc_buffer_open every
+ * peer's, put the world device pointers (this rank's own at index rank) in a
+ * device array `peer_buffers`, zero a device counter `epoch`, and let all
+ * ranks pass a host barrier.  Every rank then makes the same calls in the
+ * same order; inout += sum over ranks (rank order, identical bits on every
+ * rank) of part.  A wait longer than 5 s sets status bit 0 (see
+ * pyrite_cuda_status) and returns. */
+size_t pyrite_cuda_allreduce_buffer_size(size_t n);
+int pyrite_cuda_ipc_buffer_create(size_t bytes, void **dev_ptr, void *handle_out);
+int pyrite_cuda_ipc_buffer_open(const void *handle, void **dev_ptr);
+int pyrite_cuda_ipc_buffer_close(void *dev_ptr, int owned);
+int pyrite_cuda_allreduce_sum(const float *part, float *inout, size_t n,
+                              const unsigned long long *peer_buffers, int world, int rank,
+                              unsigned *epoch, void *stream);
+
 /* Static description of a return code. */
 const char *pyrite_error_string(int code);
 

@@ -21,7 +21,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OBJ = PKG / "_native" / "obj"
 LIB = PKG / "_native" / "libpyrite_b200.so"
-SOURCES = ["capi.cu", "mv_generic.cu", "mv_tile.cu", "mm_tc.cu", "noalloc.cu", "decode.cu", "moe.cu", "quantize.cpp"]
+SOURCES = ["capi.cu", "mv_generic.cu", "mv_tile.cu", "mm_tc.cu", "noalloc.cu", "decode.cu", "moe.cu", "allreduce.cu", "quantize.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # host code: no FMA contraction, so the quantizers round exactly like the
 # Python encoders they restate

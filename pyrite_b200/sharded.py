@@ -1,4 +1,4 @@
-"""Tensor-parallel batch-1 decode across the GPUs of one box (NCCL over NVLink).
+"""Tensor-parallel batch-1 decode across the GPUs of one box (NVLink).
 
 One process per GPU (``torchrun``); rank g holds the shard of every tensor that
 :mod:`pyrite_b200.shard` assigns it and runs the same decode step as
@@ -10,12 +10,17 @@ per layer, both inside the step's CUDA graph:
 * after the feed-forward down projection (its rows of gate/up, its columns of
   down; or, for MoE, the selected experts it owns): the same ``allreduce``;
 
-and one ``all_gather`` of the LM head's logits (rows sharded by vocabulary)
+each one kernel (``pyrite_cuda_allreduce_sum``: every rank publishes its
+partial in a buffer the others map by CUDA IPC, raises a flag in every peer's
+buffer and sums all partials over NVLink in rank order; ``p2p=False`` uses
+NCCL instead), and one NCCL ``all_gather`` of the LM head's logits (rows sharded by vocabulary)
 before the greedy argmax, which every rank computes identically.  Norms, the
 embedding lookup and the router are replicated.  Sums across GPUs change the
 fp32 summation order only; greedy ids are checked against the reference's.
 """
 from __future__ import annotations
+
+import ctypes
 
 import numpy as np
 import torch
@@ -33,7 +38,7 @@ class ShardedDecoder(MixedDecoder):
 
     def __init__(self, spec: DenseSpec | MoESpec, tensors: dict[str, tuple[tuple[int, ...], int, bytes]],
                  rank: int, world: int, device: torch.device | str = "cuda", max_ctx: int = 512,
-                 replicate: bool = False, group=None):
+                 replicate: bool = False, group=None, p2p: bool = True):
         self.spec = spec
         self.moe = isinstance(spec, MoESpec)
         self.dev = d = torch.device(device)
@@ -159,6 +164,52 @@ class ShardedDecoder(MixedDecoder):
         # the communicator is set up (and warmed) before any graph capture
         dist.all_reduce(self.part, group=self.group)
         torch.cuda.synchronize(d)
+        self._ipc_owned: int | None = None
+        self._ipc_opened: list[int] = []
+        self.peer_buffers = None
+        if p2p and world > 1:
+            self._setup_p2p()
+
+    def _setup_p2p(self) -> None:
+        """The one-shot NVLink sum (pyrite_cuda_allreduce_sum): a zeroed buffer
+        per rank shared by CUDA IPC handles, the device array of every rank's
+        buffer address and this rank's call counter."""
+        L, d, h = self.lib, self.dev, self.spec.hidden_size
+        ptr, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
+        _check(L.pyrite_cuda_ipc_buffer_create(L.pyrite_cuda_allreduce_buffer_size(h), ctypes.byref(ptr), handle),
+               "ipc buffer")
+        self._ipc_owned = ptr.value
+        handles: list[bytes | None] = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=self.group)
+        ptrs = []
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(ptr.value)
+                continue
+            p = ctypes.c_void_p()
+            _check(L.pyrite_cuda_ipc_buffer_open(hb, ctypes.byref(p)), "ipc open")
+            self._ipc_opened.append(p.value)
+            ptrs.append(p.value)
+        self.peer_buffers = torch.tensor(ptrs, dtype=torch.int64, device=d)
+        self.ar_epoch = torch.zeros(1, dtype=torch.int32, device=d)
+        torch.cuda.synchronize(d)
+        dist.barrier(group=self.group)  # every buffer is zeroed before any flag is raised
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after every rank's
+        last step: call it on all ranks after a barrier)."""
+        torch.cuda.synchronize(self.dev)
+        for p in self._ipc_opened:
+            self.lib.pyrite_cuda_ipc_buffer_close(p, 0)
+        self._ipc_opened = []
+        if self._ipc_owned is not None:
+            self.lib.pyrite_cuda_ipc_buffer_close(self._ipc_owned, 1)
+            self._ipc_owned = None
+        self.peer_buffers = None
+
+    def capture(self) -> None:
+        dist.barrier(group=self.group)  # the ranks' first steps start together
+        super().capture()
 
     @classmethod
     def synthetic(cls, spec: DenseSpec | MoESpec, rank: int, world: int, device="cuda", max_ctx: int = 512,
@@ -176,7 +227,14 @@ class ShardedDecoder(MixedDecoder):
         return cls(spec, tensors, rank, world, device=device, max_ctx=max_ctx, replicate=replicate, group=group)
 
     # ------------------------------------------------------------------ one step
-    def _allreduce_into_hidden(self) -> None:
+    def _allreduce_into_hidden(self, stream: int) -> None:
+        """hidden += sum over ranks of part: one kernel over NVLink peer
+        memory (pyrite_cuda_allreduce_sum), or NCCL when p2p is off."""
+        if self.peer_buffers is not None:
+            _check(self.lib.pyrite_cuda_allreduce_sum(self.part.data_ptr(), self.hidden.data_ptr(), self.part.numel(),
+                                                      self.peer_buffers.data_ptr(), self.world, self.rank,
+                                                      self.ar_epoch.data_ptr(), stream), "allreduce")
+            return
         dist.all_reduce(self.part, group=self.group)
         self.hidden.add_(self.part)
 
@@ -197,7 +255,7 @@ class ShardedDecoder(MixedDecoder):
                 self.vcache[li].data_ptr(), self.attn.data_ptr(), wq, wql, self.attn_scratch.data_ptr(),
                 self.attn_scratch.numel(), stream), "attention_step")
             self._mv(ly.o, self.attn, self.ws_q, self.part, 0, stream)
-            self._allreduce_into_hidden()
+            self._allreduce_into_hidden(stream)
             if not self.moe:
                 self._mvx(ly.gate_up, self.hidden, _lib.X_RMSNORM, ly.ffn_norm, self.normed, self.ws_h, self.gu, 0,
                           stream)
@@ -211,7 +269,7 @@ class ShardedDecoder(MixedDecoder):
                                                          self.act.data_ptr(), wa, wal, stream), "moe silu")
                 self.part.zero_()
                 self._down_combine(ly, self.part, stream)
-            self._allreduce_into_hidden()
+            self._allreduce_into_hidden(stream)
         self._norm(self.hidden, self.out_norm, self.normed, self.ws_h, stream)
         self._mv(self.lm_head, self.normed, self.ws_h, self.logits_local, 0, stream)
         dist.all_gather_into_tensor(self.logits, self.logits_local, group=self.group)

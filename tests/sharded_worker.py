@@ -33,6 +33,8 @@ def main() -> int:
     dev = torch.device("cuda", local)
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if sys.argv[1] == "allreduce":
+        return allreduce_check(rank, world, dev)
     g = json.loads(Path(sys.argv[1]).read_text())
     cls = MoESpec if g["spec"].get("architecture") == "qwen3moe" else DenseSpec
     names = {f.name for f in fields(cls)}
@@ -56,8 +58,92 @@ def main() -> int:
                           "status": status}), flush=True)
     dec.graph = None
     dist.barrier()
+    dec.close()
+    dist.barrier()
     dist.destroy_process_group()
     return 0 if ok and routed_ok in (None, True) and status == 0 else 1
+
+
+def allreduce_check(rank: int, world: int, dev) -> int:
+    """pyrite_cuda_allreduce_sum against NCCL's allreduce on seeded partials:
+    within fp32 summation-order rounding of it, bit-identical on every rank,
+    over many calls in a row (alternating slots, growing flags) and inside a
+    replayed CUDA graph."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from pyrite_b200 import _lib
+    from pyrite_b200.kernels import cuda as K
+    from pyrite_b200.kernels.cuda import _check
+    lib = _lib.require()
+    n = 4096
+    ptr, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
+    _check(lib.pyrite_cuda_ipc_buffer_create(lib.pyrite_cuda_allreduce_buffer_size(n), ctypes.byref(ptr), handle), "c")
+    handles = [None] * world
+    dist.all_gather_object(handles, bytes(handle))
+    ptrs, opened = [], []
+    for r, hb in enumerate(handles):
+        if r == rank:
+            ptrs.append(ptr.value)
+        else:
+            p = ctypes.c_void_p()
+            _check(lib.pyrite_cuda_ipc_buffer_open(hb, ctypes.byref(p)), "open")
+            opened.append(p.value)
+            ptrs.append(p.value)
+    peers = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+    epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    ok, worst = True, 0.0
+    s = torch.cuda.current_stream(dev)
+    for it in range(20):
+        g = torch.Generator(device=dev).manual_seed(1000 * it + rank)
+        part = torch.randn(n, device=dev, generator=g)
+        base = torch.full((n,), float(it), device=dev)
+        out = base.clone()
+        assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), n, peers.data_ptr(), world, rank,
+                                             epoch.data_ptr(), s.cuda_stream) == 0
+        ref = part.clone()
+        dist.all_reduce(ref)
+        torch.cuda.synchronize(dev)
+        worst = max(worst, float((out - (base + ref)).abs().max()))
+        everyone = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(everyone, out)
+        ok &= all(torch.equal(everyone[0], o) for o in everyone)
+    # the same call replayed from a CUDA graph
+    part = torch.randn(n, device=dev, generator=torch.Generator(device=dev).manual_seed(7 + rank))
+    out = torch.zeros(n, device=dev)
+    side = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(side):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), n, peers.data_ptr(), world, rank,
+                                                 epoch.data_ptr(), side.cuda_stream) == 0
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    for _ in range(5):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    ref = part.clone()
+    dist.all_reduce(ref)
+    torch.cuda.synchronize(dev)
+    worst = max(worst, float((out - 5 * ref).abs().max()) / 5)
+    status = K.status()
+    del graph
+    dist.barrier()
+    for p in opened:
+        lib.pyrite_cuda_ipc_buffer_close(p, 0)
+    dist.barrier()
+    lib.pyrite_cuda_ipc_buffer_close(ptr.value, 1)
+    good = ok and worst <= 1e-5 and status == 0
+    if rank == 0:
+        print(json.dumps({"world": world, "identical_on_ranks": ok, "max_abs_diff_vs_nccl": worst, "status": status,
+                          "allreduce_ok": good}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0 if good else 1
 
 
 if __name__ == "__main__":

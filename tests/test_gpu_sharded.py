@@ -1,5 +1,6 @@
-"""Tensor-parallel decode on 2 GPUs (B200, NCCL over NVLink): greedy ids (and
-routed experts) equal the reference executor's on the golden checkpoints.
+"""Tensor-parallel decode on 2 GPUs (B200, NVLink): greedy ids (and routed
+experts) equal the reference executor's on the golden checkpoints, and the
+one-shot NVLink sum (pyrite_cuda_allreduce_sum) equals NCCL's allreduce.
 Needs at least two GPUs; runs tests/sharded_worker.py under torchrun."""
 from __future__ import annotations
 
@@ -33,3 +34,16 @@ def test_two_gpu_sharded_decode_matches_reference(cuda_device, golden):
     assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-3000:]
     out = json.loads(lines[-1])
     assert out["ids_match"] and out["routed_match"] in (None, True), out
+
+
+def test_two_gpu_nvlink_allreduce_equals_nccl(cuda_device):
+    if _gpus() < 2:
+        pytest.skip("the allreduce needs 2 GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29534", str(ROOT / "tests" / "sharded_worker.py"), "allreduce"]
+    res = subprocess.run(["timeout", "-k", "30", "300", *cmd], capture_output=True, text=True, env=env, cwd=ROOT)
+    lines = [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-3000:]
+    out = json.loads(lines[-1])
+    assert out["allreduce_ok"], out
