@@ -358,7 +358,7 @@ int pyrite_cuda_moe_combine(const float *expert_out, const float *expert_weights
  * device array `peer_buffers`, zero a device counter `epoch`, and let all
  * ranks pass a host barrier.  Every rank then makes the same calls in the
  * same order; inout += sum over ranks (rank order, identical bits on every
- * rank) of part.  A wait longer than 5 s sets status bit 0 (see
+ * rank) of part.  n % 4 == 0, part and inout 16-byte aligned.  A wait longer than 5 s sets status bit 0 (see
  * pyrite_cuda_status) and returns. */
 size_t pyrite_cuda_allreduce_buffer_size(size_t n);
 int pyrite_cuda_ipc_buffer_create(size_t bytes, void **dev_ptr, void *handle_out);

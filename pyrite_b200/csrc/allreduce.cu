@@ -58,9 +58,10 @@ __global__ void __launch_bounds__(1024) allreduce_oneshot_kernel(const float* __
   const unsigned e = *epoch + 1u;
   const size_t sb = slot_bytes((size_t)n);
   const size_t off = kFlagBytes + (size_t)(e & 1u) * sb;
-  // 1. this GPU's partial into its own slot
-  float* mine = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(peers[rank]) + off);
-  for (int i = tid; i < n; i += blockDim.x) mine[i] = part[i];
+  // 1. this GPU's partial into its own slot (n % 4 == 0: float4 throughout)
+  float4* mine = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(peers[rank]) + off);
+  const int n4 = n >> 2;
+  for (int i = tid; i < n4; i += blockDim.x) mine[i] = reinterpret_cast<const float4*>(part)[i];
   if (tid == 0) timed_out = 0;
   __syncthreads();
   // 2. publish: raise flag `rank` of every GPU (a system-scope release after
@@ -91,14 +92,32 @@ __global__ void __launch_bounds__(1024) allreduce_oneshot_kernel(const float* __
     }
     return;
   }
-  // 4. every partial over NVLink, summed in rank order (the same bits on every GPU)
-  for (int i = tid; i < n; i += blockDim.x) {
-    float acc = 0.f;
-    for (int r = 0; r < world; ++r) {
-      const float* src = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(peers[r]) + off);
-      acc += __ldcv(src + i);
+  // 4. every partial over NVLink, summed in rank order (the same bits on every
+  //    GPU); the loads of up to 8 ranks are issued before the adds, so a
+  //    thread waits for one NVLink round trip per 8 ranks, not one per rank
+  for (int i = tid; i < n4; i += blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r0 = 0; r0 < world; r0 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (r0 + j < world)
+          v[j] = __ldcv(reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(peers[r0 + j]) + off) + i);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (r0 + j < world) {
+          acc.x += v[j].x;
+          acc.y += v[j].y;
+          acc.z += v[j].z;
+          acc.w += v[j].w;
+        }
     }
-    inout[i] += acc;
+    float4 io = reinterpret_cast<float4*>(inout)[i];
+    io.x += acc.x;
+    io.y += acc.y;
+    io.z += acc.z;
+    io.w += acc.w;
+    reinterpret_cast<float4*>(inout)[i] = io;
   }
   __syncthreads();
   if (tid == 0) *epoch = e;
@@ -148,8 +167,8 @@ int pyrite_cuda_ipc_buffer_close(void* dev_ptr, int owned) {
 
 int pyrite_cuda_allreduce_sum(const float* part, float* inout, size_t n, const unsigned long long* peer_buffers,
                               int world, int rank, unsigned* epoch, void* stream) {
-  if (!part || !inout || !peer_buffers || !epoch || n == 0 || n > (1u << 20) || world < 1 || world > kMaxRanks ||
-      rank < 0 || rank >= world)
+  if (!part || !inout || !peer_buffers || !epoch || n == 0 || n % 4 || n > (1u << 20) || world < 1 ||
+      world > kMaxRanks || rank < 0 || rank >= world || (((uintptr_t)part | (uintptr_t)inout) & 15))
     return PYRITE_E_BUFFER;
   const int r = launch_pdl(allreduce_oneshot_kernel, dim3(1), dim3(1024), 0, static_cast<cudaStream_t>(stream), part,
                            inout, (int)n, peer_buffers, world, rank, epoch, device_status_word());
