@@ -47,3 +47,45 @@ def test_two_gpu_nvlink_allreduce_equals_nccl(cuda_device):
     assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-3000:]
     out = json.loads(lines[-1])
     assert out["allreduce_ok"], out
+
+
+def test_nvlink_allreduce_wait_gives_up_and_reports(cuda_device):
+    """Failure detection on one GPU, without a fault: a sum over two ranks
+    whose second rank never raises its flag (its buffer is a second local
+    allocation nothing writes) waits its bounded 5 s, sets status bit 0,
+    leaves `inout` untouched and returns; the context stays usable."""
+    import ctypes
+
+    import torch
+
+    from pyrite_b200 import _lib
+    from pyrite_b200.kernels import cuda as K
+    lib = _lib.require()
+    n = 256
+    size = int(lib.pyrite_cuda_allreduce_buffer_size(n))
+    bufs, handle = [], (ctypes.c_ubyte * 64)()
+    for _ in range(2):
+        p = ctypes.c_void_p()
+        assert lib.pyrite_cuda_ipc_buffer_create(size, ctypes.byref(p), handle) == 0
+        bufs.append(p.value)
+    peers = torch.tensor(bufs, dtype=torch.int64, device="cuda")
+    epoch = torch.zeros(1, dtype=torch.int32, device="cuda")
+    part = torch.ones(n, device="cuda")
+    out = torch.full((n,), 3.0, device="cuda")
+    K.status()  # start clean
+    assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), n, peers.data_ptr(), 2, 0, epoch.data_ptr(),
+                                         torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert K.status() & 1  # the wait gave up (and the bit is cleared again)
+    assert bool((out == 3.0).all())
+    assert int(epoch.item()) == 1
+    # the context still runs work
+    assert float((part * 2).sum().item()) == 2 * n
+    for p in bufs:
+        assert lib.pyrite_cuda_ipc_buffer_close(p, 1) == 0
+    # argument checks: n not a multiple of 4, rank outside the world
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), 6, peers.data_ptr(), 2, 0, epoch.data_ptr(),
+                                         s) == -3
+    assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), n, peers.data_ptr(), 2, 2, epoch.data_ptr(),
+                                         s) == -3
