@@ -12,7 +12,7 @@ Defaults are configs[0] in full (28 layers, vocab 151936, 16-token prompt,
 8 new tokens, KV limit 512); ``--spec c3`` is the Llama-3-8B-shaped Q4_K_M
 model of configs[2] (use --layers to keep the reference run short), ``c3tiny``
 the same architecture and mix at toy width.  Needs the reference tree (``PYRITE_REF_ROOT``,
-default /root/reference); the committed JSON is what the tests read.
+default: a ``reference`` directory beside the repository); the committed JSON is what the tests read.
 """
 from __future__ import annotations
 
@@ -27,7 +27,7 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
-REF = Path(os.environ.get("PYRITE_REF_ROOT", "/root/reference"))
+REF = Path(os.environ.get("PYRITE_REF_ROOT", ROOT.parent / "reference"))
 
 
 def main() -> None:

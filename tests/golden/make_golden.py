@@ -1,8 +1,8 @@
 """Generate the golden vectors under tests/golden from the reference itself.
 
-Run in a container that holds the reference tree (default ``/root/reference``,
-override with ``PYRITE_REF_ROOT``); the GPU box and the test suite never need
-it, they read the committed ``.npz`` files.
+Run where the reference tree is (``PYRITE_REF_ROOT``, default: a
+``reference`` directory beside the repository); the GPU box and the test
+suite never need it, they read the committed ``.npz`` files.
 
     python tests/golden/make_golden.py
 
@@ -33,7 +33,8 @@ from pathlib import Path
 
 import numpy as np
 
-REF = Path(os.environ.get("PYRITE_REF_ROOT", "/root/reference"))
+ROOT = Path(__file__).resolve().parents[2]
+REF = Path(os.environ.get("PYRITE_REF_ROOT", ROOT.parent / "reference"))
 OUT = Path(__file__).resolve().parent
 
 

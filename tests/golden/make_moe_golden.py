@@ -11,7 +11,7 @@ and the experts routed at every layer of every pass:
     python tests/golden/make_moe_golden.py --spec c4 --layers 2 --out moe_c4_2l.json
     python tests/golden/make_moe_golden.py --spec c5 --layers 2 --out moe_c5_2l.json
 
-Needs the reference tree (``PYRITE_REF_ROOT``, default /root/reference); the
+Needs the reference tree (``PYRITE_REF_ROOT``, default: a ``reference`` directory beside the repository); the
 committed JSON is what the tests read.
 """
 from __future__ import annotations
@@ -27,7 +27,7 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
-REF = Path(os.environ.get("PYRITE_REF_ROOT", "/root/reference"))
+REF = Path(os.environ.get("PYRITE_REF_ROOT", ROOT.parent / "reference"))
 
 
 def main() -> None:
