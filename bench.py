@@ -440,8 +440,8 @@ def model_leg(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
     take minutes; the bytes streamed per token are the same).  Parity for these
     architectures is tested on 2-layer full-width models against the reference.
     With several GPUs the model is split tensor-parallel over them
-    (pyrite_b200.sharded: heads / rows / experts by id, NCCL allreduce after the
-    output and down projections); the time is the max over ranks."""
+    (pyrite_b200.sharded: heads / rows / experts by id, a one-kernel NVLink sum
+    after the output and down projections); the time is the max over ranks."""
     import time as _t
 
     import torch
