@@ -34,7 +34,6 @@ B200 layout choices:
 from __future__ import annotations
 
 import ctypes
-import math
 from dataclasses import dataclass
 
 import numpy as np

@@ -127,7 +127,6 @@ class ShardedDecoder(MixedDecoder):
         self.qkv, self.attn = z(nq_l + 2 * nkv_l), z(nq_l)
         if self.moe:
             ff, k = spec.moe_intermediate_size, spec.num_experts_per_tok
-            self.n_local_experts = len(owned_experts(spec.num_experts, world, rank))
             self.router_logits = z(spec.num_experts)
             self.route_ticket = z(1, dt=torch.int32)
             self.expert_ids, self.expert_w = z(k, dt=torch.int32), z(k)
