@@ -101,3 +101,31 @@ def test_chunked_expert_subset_equals_slices_of_full_stack():
             assert p == b"".join(fp[e * per:(e + 1) * per] for e in mine)
         else:
             assert p == fp
+
+
+@pytest.mark.parametrize("which", ["c3", "c4", "c5"])
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_model_configs_shard_over_one_box(which, world):
+    """configs[2]-[4] split over 2, 4 and 8 GPUs (bench.py's tensor-parallel
+    legs): every rank gets whole heads, block-aligned column ranges, an even
+    vocabulary range and E / world experts, and the ranks cover everything once."""
+    from pyrite_b200.synthetic import DenseSpec, MoESpec
+    spec = {"c3": DenseSpec.c3, "c4": MoESpec.c4, "c5": MoESpec.c5}[which]()
+    q_seen, e_seen, v_seen = [], [], []
+    for rank in range(world):
+        hs = head_shard(spec.num_attention_heads, spec.num_key_value_heads, world, rank)
+        q_seen += list(range(hs.q0, hs.q0 + hs.nq))
+        group = spec.num_attention_heads // spec.num_key_value_heads
+        assert all(hs.kv0 <= q // group < hs.kv0 + hs.nkv for q in range(hs.q0, hs.q0 + hs.nq))
+        assert (hs.q0 * spec.head_dim) % 256 == 0  # output-projection columns stay super-block aligned
+        v0, v1 = even_range(spec.vocab_size, world, rank)
+        v_seen += [v0, v1]
+        if isinstance(spec, MoESpec):
+            e_seen += owned_experts(spec.num_experts, world, rank)
+        else:
+            f0, f1 = even_range(spec.intermediate_size, world, rank)
+            assert f0 % 256 == 0 and f1 % 256 == 0
+    assert sorted(q_seen) == list(range(spec.num_attention_heads))
+    assert v_seen[0] == 0 and v_seen[-1] == spec.vocab_size
+    if e_seen:
+        assert sorted(e_seen) == list(range(spec.num_experts))
