@@ -50,7 +50,7 @@ def workload():
 
 
 def row_bytes(t: int, cols: int) -> int:
-    from pyrite_b200.ggml_types import spec
+    from pyrite_b200.ggml_types import spec  # a plain table: loads no library
     s = spec(t)
     return cols // s.block_size * s.bytes_per_block
 
@@ -60,8 +60,17 @@ def algo_bytes(t: int, rows: int, cols: int, ncols: int = 1) -> int:
     return rows * row_bytes(t, cols) + ncols * (rows + cols) * 4
 
 
-def build_payloads() -> dict[tuple[int, int, int], bytes]:
-    from pyrite_b200.quantize import gaussian_weights, quantize
+def gaussian_weights(rows: int, cols: int, seed: int) -> np.ndarray:
+    """Seeded N(0, 0.02) fp32 weights (the same draw as pyrite_b200.quantize.gaussian_weights)."""
+    return np.random.default_rng(seed).normal(0.0, 0.02, rows * cols).astype(np.float32)
+
+
+def build_payloads(quantize=None) -> dict[tuple[int, int, int], bytes]:
+    """The 15 payloads of the step.  quantize: the library's quantizer by
+    default; the reference arm passes the numpy encoders (identical bytes,
+    tests/test_quantize.py) so its process never loads libpyrite_b200.so."""
+    if quantize is None:
+        from pyrite_b200.quantize import quantize
     out = {}
     wl = workload()
     for (rows, cols) in SHAPES:
@@ -312,7 +321,9 @@ def run_ours(args) -> None:
                "payload copied to HBM every call; pinned host payload)", "ms_per_step": round(dt * 1e3, 3),
                "steps": e2e_steps}
 
-    cpu = cpu_baseline(payloads, xs, wl, budget_s=args.cpu_seconds) if (rank == 0 and not args.no_cpu) else None
+    ours_y = {k: v.cpu().numpy() for k, v in Y.items()} if rank == 0 else None
+    cpu = (cpu_baseline(payloads, xs, wl, budget_s=args.cpu_seconds, ours=ours_y)
+           if (rank == 0 and not args.no_cpu) else None)
     decode = decode_leg(dev) if (rank == 0 and not args.no_decode) else None
     batched = batched_leg(dev, W, X, wl, stream) if (rank == 0 and not args.no_batched) else None
     del W, X, Y
@@ -584,16 +595,21 @@ def _ref_kernel():
     return O.matvec, "port"
 
 
-def cpu_baseline(payloads, xs, wl, budget_s: float = 12.0, threads: int = 1) -> dict:
+def cpu_baseline(payloads, xs, wl, budget_s: float = 12.0, threads: int = 1, ours=None) -> dict:
     """Reference C kernel (oracle/_ref, built from pyrite/kernels/native.c) on the
     host cores: a bounded sample -- the first rows of each of the 15 matrices,
     about budget_s / 15 seconds each -- timed single threaded (the reference
-    kernel is scalar and single threaded)."""
+    kernel is scalar and single threaded).  ours: this build's outputs of the
+    same step (rows x 1 arrays per matrix); the sampled rows are then also a
+    parity check, reported as the largest error relative to sum |w x| (the
+    oracle's decoded weights), outside any timed region."""
+    from oracle import oracle as O
     fn, kind = _ref_kernel()
     total_b, total_t = 0, 0.0
     per = budget_s / len(wl)
     rows_done = {}
-    for _, t, r, c in wl:
+    worst, worst_at = 0.0, None
+    for name, t, r, c in wl:
         rb = row_bytes(t, c)
         x64 = xs[c].astype(np.float64)
         # calibrate with 8 rows, then size the sample to ~per seconds
@@ -602,41 +618,57 @@ def cpu_baseline(payloads, xs, wl, budget_s: float = 12.0, threads: int = 1) -> 
         dt8 = max(time.perf_counter() - t0, 1e-6)
         n = int(min(r, max(8, 8 * per / dt8)))
         t0 = time.perf_counter()
-        fn(t, payloads[(t, r, c)][: n * rb], x64, n, c)
+        want = fn(t, payloads[(t, r, c)][: n * rb], x64, n, c)
         dt = time.perf_counter() - t0
         total_b += n * rb + (n + c) * 4
         total_t += dt
         rows_done[f"{t}:{r}x{c}"] = n
+        if ours is not None:
+            w = O.dequantize_rows(t, payloads[(t, r, c)][: n * rb], n, c)
+            bound = np.abs(w) @ np.abs(x64)
+            err = float(np.max(np.abs(np.asarray(ours[(t, r, c)][:n], dtype=np.float64) - want) /
+                               np.maximum(bound, 1e-30)))
+            if err >= worst:
+                worst, worst_at = err, f"{name} {r}x{c}"
     full = all(rows_done[f"{t}:{r}x{c}"] == r for _, t, r, c in wl)
     what = ("all rows of all 15 matrices (the whole step)" if full else
             f"the first rows of each of the 15 matrices ({sum(rows_done.values())} rows, ~{per:.1f} s each)")
-    return {"value": round(total_b / total_t / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": kind,
-            "sample": f"{what}, single thread, fp64 as the reference computes", "seconds": round(total_t, 2)}
+    out = {"value": round(total_b / total_t / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": kind,
+           "sample": f"{what}, single thread, fp64 as the reference computes", "seconds": round(total_t, 2)}
+    if ours is not None:
+        out["parity"] = {"max_rel_err": worst, "worst_matrix": worst_at, "tolerance": 1e-4, "ok": worst <= 1e-4,
+                         "against": f"{kind} kernel outputs on the sampled rows, relative to sum |w x|"}
+    return out
 
 
 def run_reference(args) -> None:
-    """Reference arm: the reference's own CPU kernel on this box's host cores."""
+    """Reference arm: the reference's own CPU kernel (oracle/_ref, compiled from
+    pyrite/kernels/native.c) on this box's host cores, over the same workload
+    as ours -- every row of all 15 matrices per step -- with each matrix split
+    into one contiguous row range per host thread (ctypes releases the GIL
+    during the call).  Inputs come from the numpy encoders, so this process
+    loads none of this build's libraries."""
     world, rank, _ = dist_setup(args.gpus)
     if rank != 0:
         return
     from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import encoders
     fn, kind = _ref_kernel()
-    payloads = build_payloads()
+    payloads = build_payloads(encoders.quantize)
     xs = x_vectors()
     wl = workload()
     threads = os.cpu_count() or 1
-    # each step: the same fraction of every matrix's rows (a bounded sample)
-    frac = args.ref_fraction
     jobs = []
     for _, t, r, c in wl:
-        n = max(threads, int(r * frac))
         rb = row_bytes(t, c)
         x64 = xs[c].astype(np.float64)
+        buf = memoryview(payloads[(t, r, c)])
         for i in range(threads):
-            a, b = n * i // threads, n * (i + 1) // threads
+            a, b = r * i // threads, r * (i + 1) // threads
             if b > a:
-                jobs.append((t, payloads[(t, r, c)][a * rb:b * rb], x64, b - a, c))
-    step_bytes = sum(len(j[1]) + (j[3] + j[4]) * 4 for j in jobs)
+                jobs.append((t, buf[a * rb:b * rb], x64, b - a, c))
+    step_bytes = sum(algo_bytes(t, r, c) for _, t, r, c in wl)
 
     def step(pool):
         list(pool.map(lambda j: fn(*j), jobs))
@@ -652,12 +684,13 @@ def run_reference(args) -> None:
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp64", "data": "synthetic (same payloads as ours)",
-        "config": {"workload": f"configs[1] kernel microbench, batch 1, each step the first {frac:.0%} of the "
-                               "rows of each of the 15 matrices", "global_batch": 1, "ncols": 1,
-                   "parallelism": f"{threads} host threads over row ranges"},
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp64", "data": "synthetic (the same payloads as ours)",
+        "config": {"workload": "configs[1] kernel microbench, batch 1: {Q8_0,Q4_K,Q5_K,Q6_K,IQ4_XS} x "
+                               "{4096x4096,14336x4096,4096x14336}, 15 matvecs per step, every row",
+                   "global_batch": 1, "ncols": 1, "step_bytes": step_bytes, "same_config": True,
+                   "parallelism": f"{threads} host threads, one contiguous row range per thread per matrix"},
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": kind,
-                         "sample": f"{frac:.0%} of the rows of each matrix per step"},
+                         "sample": "the whole step (all rows of the 15 matrices) every step"},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -670,7 +703,6 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--ref-fraction", type=float, default=0.02)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the configs[0] decode tok/s leg")

@@ -142,7 +142,8 @@ size_t pyrite_cuda_workspace_size(int type_id, size_t cols, size_t ncols);
  * device pointers; fp32 activations, fp32 outputs within 1e-4 of the exact
  * product relative to sum_k |W[r,k] x[k]|.  `workspace` (256-byte aligned, at
  * least pyrite_cuda_workspace_size bytes) holds the activation re-encoded as
- * two int8 digits per value with per-32-value scales; it must not be shared
+ * int8 digits with per-32-value scales (three digits where a block holds
+ * values far below its largest, e.g. an outlier channel); it must not be shared
  * by calls that overlap on the GPU.  Enqueued on `stream` (a cudaStream_t,
  * NULL = legacy default stream); returns without waiting.  Same validation
  * codes as pyrite_matvec.  This is the row-range call of the reference's
@@ -167,8 +168,9 @@ int pyrite_cuda_matvec_prepared(int type_id, const void *weights, size_t weights
                                 const void *workspace, size_t workspace_len, float *y, size_t rows,
                                 size_t cols, unsigned flags, void *stream);
 
-/* Largest `cols` pyrite_cuda_matvec_noalloc accepts (the size of its fixed
- * scratch array: 152 KiB per GPU). */
+/* Largest `cols` pyrite_cuda_matvec_noalloc accepts.  Its fixed scratch array
+ * (108 KiB per GPU) holds the encoding of up to 32768 values; wider
+ * activations take the generic kernel, which reads x directly. */
 #define PYRITE_NOALLOC_MAX_COLS 65536
 
 /* No counterpart in the reference.  pyrite_cuda_matvec for one column, for
@@ -358,15 +360,17 @@ int pyrite_cuda_moe_combine(const float *expert_out, const float *expert_weights
  * device array `peer_buffers`, zero a device counter `epoch`, and let all
  * ranks pass a host barrier.  Every rank then makes the same calls in the
  * same order; inout += sum over ranks (rank order, identical bits on every
- * rank) of part.  n % 4 == 0, part and inout 16-byte aligned.  A wait longer than 5 s sets status bit 0 (see
+ * rank) of part.  n % 4 == 0, part and inout 16-byte aligned; buffer_len is
+ * the size every rank's buffer was created with (n beyond what it holds is
+ * PYRITE_E_BUFFER).  A wait longer than 5 s sets status bit 0 (see
  * pyrite_cuda_status) and returns. */
 size_t pyrite_cuda_allreduce_buffer_size(size_t n);
 int pyrite_cuda_ipc_buffer_create(size_t bytes, void **dev_ptr, void *handle_out);
 int pyrite_cuda_ipc_buffer_open(const void *handle, void **dev_ptr);
 int pyrite_cuda_ipc_buffer_close(void *dev_ptr, int owned);
 int pyrite_cuda_allreduce_sum(const float *part, float *inout, size_t n,
-                              const unsigned long long *peer_buffers, int world, int rank,
-                              unsigned *epoch, void *stream);
+                              const unsigned long long *peer_buffers, size_t buffer_len, int world,
+                              int rank, unsigned *epoch, void *stream);
 
 /* Static description of a return code. */
 const char *pyrite_error_string(int code);

@@ -166,10 +166,12 @@ int pyrite_cuda_ipc_buffer_close(void* dev_ptr, int owned) {
 }
 
 int pyrite_cuda_allreduce_sum(const float* part, float* inout, size_t n, const unsigned long long* peer_buffers,
-                              int world, int rank, unsigned* epoch, void* stream) {
+                              size_t buffer_len, int world, int rank, unsigned* epoch, void* stream) {
   if (!part || !inout || !peer_buffers || !epoch || n == 0 || n % 4 || n > (1u << 20) || world < 1 ||
       world > kMaxRanks || rank < 0 || rank >= world || (((uintptr_t)part | (uintptr_t)inout) & 15))
     return PYRITE_E_BUFFER;
+  // every rank's buffer must hold the flags and both slots of n values
+  if (buffer_len < pyrite_cuda_allreduce_buffer_size(n)) return PYRITE_E_BUFFER;
   const int r = launch_pdl(allreduce_oneshot_kernel, dim3(1), dim3(1024), 0, static_cast<cudaStream_t>(stream), part,
                            inout, (int)n, peer_buffers, world, rank, epoch, device_status_word());
   return r > 0 ? PYRITE_E_CUDA : r;

@@ -9,6 +9,7 @@
 //   * pyrite_cuda_*: the device-resident path.  Weights, x and y live in device
 //     memory; fp32 activations; the call enqueues on the caller's stream and
 //     returns without synchronising.
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -20,15 +21,18 @@ namespace pyr {
 __device__ int g_status_word;
 
 int* device_status_word() {
-  static int* addr[64] = {};
+  // one lookup per device; concurrent first calls look up the same address
+  static std::atomic<int*> addr[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!addr[dev]) {
+  int* a = addr[dev].load(std::memory_order_acquire);
+  if (!a) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
-    addr[dev] = static_cast<int*>(p);
+    a = static_cast<int*>(p);
+    addr[dev].store(a, std::memory_order_release);
   }
-  return addr[dev];
+  return a;
 }
 
 namespace {

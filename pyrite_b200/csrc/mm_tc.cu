@@ -37,6 +37,8 @@
 // Every mbarrier wait is bounded (2 s); on a time-out the kernel records it
 // in the device status word, stops waiting, and still drains its copies and
 // MMAs before releasing TMEM.
+#include <atomic>
+
 #include <cuda_bf16.h>
 
 #include "kernels.cuh"
@@ -563,12 +565,12 @@ template <int TY, int NP, bool FAST>
 int launch_tc_t(const TcArgs& ta, int ks, size_t smem, cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -4;
-  static bool smem_set[64] = {};
-  if (!smem_set[dev]) {
+  static std::atomic<bool> smem_set[64];  // idempotent: concurrent first calls only repeat it
+  if (!smem_set[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(mm_tc_kernel<TY, NP, FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemMax) !=
         cudaSuccess)
       return -100 - (int)cudaGetLastError();
-    smem_set[dev] = true;
+    smem_set[dev].store(true, std::memory_order_release);
   }
   const int m_tiles = (ta.rows + kBM - 1) / kBM;
   cudaLaunchConfig_t cfg = {};

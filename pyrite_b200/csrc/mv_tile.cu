@@ -7,11 +7,14 @@
 // keeping the per-byte instruction count low.
 //
 //  * x is prepared once per vector (xprep_kernel): per 32-value block b a
-//    scale s_b = max|x|/127 and two int8 digits, x ~= s_b (x0 + x1/254)
-//    (|error| <= s_b/508 = 1.6e-5 max|x_b|), plus fp32 sums of x per 16
-//    values.  Codes are multiplied by both digit vectors with dp4a (exact
-//    int32 sums); scales and mins are applied once per 16 or 32 values:
-//        sum (d*sc*q - m) x = d*sc*(s_b/254)*(254*sum q x0 + sum q x1) - m*sum x.
+//    scale s_b = max|x|/127 and int8 digits, x ~= s_b (x0 + x1/254 + x2/254^2),
+//    plus fp32 sums of x per 16 values.  Codes are multiplied by the digit
+//    vectors with dp4a (exact int32 sums); scales and mins are applied once
+//    per 16 or 32 values:
+//        sum (d*sc*q - m) x = d*sc*(s_b/254)*(254*sum q x0 + sum q x1 [+ sum q x2 / 254]) - m*sum x.
+//    The third digit is used only for "wide" blocks (flagged by a negative
+//    scale: a few values far below the block's largest, i.e. an outlier
+//    channel), where two digits would lose the small values' precision.
 //  * A CTA (256 threads) owns whole rows.  Its lanes are split into RS row
 //    slots; lane l of a slot always handles the same units (32-value pieces)
 //    of a row, so it loads its x digits once, into registers, for the whole
@@ -31,6 +34,8 @@
 //    the preceding kernel (programmatic dependent launch), so the weight
 //    stream overlaps its tail.  Every mbarrier wait is bounded (2 s); on
 //    time-out the kernel sets the device status word and drains its copies.
+#include <atomic>
+
 #include "kernels.cuh"
 #include "post_ops.cuh"
 #include "ptx.cuh"
@@ -57,9 +62,8 @@ __device__ __forceinline__ void lds_32b(uint32_t a, uint32_t (&out)[8]) {
 }  // namespace
 
 // ---- x preparation ------------------------------------------------------------------
-// One warp per 32-value block; lane l owns value l.  Workspace of one column
-// (cols values): xq0[cols] int8 | xq1[cols] int8 | xscale[cols/32] fp32
-// (s_b / 254) | xsum16[cols/16] fp32.
+// One warp per 32-value block; lane l owns value l.  Workspace of one column:
+// the layout of post_ops.cuh (x0 | x1 | scale | sum16 | x2).
 __global__ void __launch_bounds__(256) xprep_kernel(const float* __restrict__ x, long long ldx, int cols, int ncols,
                                                     uint8_t* __restrict__ ws, long long ws_col_bytes) {
   pdl_wait();
@@ -70,23 +74,7 @@ __global__ void __launch_bounds__(256) xprep_kernel(const float* __restrict__ x,
   const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
   for (long long it = gw; it < (long long)nblk * ncols; it += nw) {
     const int c = (int)(it / nblk), b = (int)(it % nblk);
-    const float v = x[c * ldx + 32LL * b + lane];
-    float amax = fabsf(v);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float s = amax / 127.0f;
-    int d0, d1;
-    two_digits(v, digit_ratio(amax), d0, d1);
-    float s16 = v;
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
-    uint8_t* w = ws + c * ws_col_bytes;
-    w[32LL * b + lane] = (uint8_t)(int8_t)d0;
-    w[(long long)cols + 32LL * b + lane] = (uint8_t)(int8_t)d1;
-    float* xscale = reinterpret_cast<float*>(w + 2LL * cols);
-    float* xsum16 = xscale + nblk;
-    if (lane == 0) xscale[b] = s / 254.0f;
-    if ((lane & 15) == 0) xsum16[2 * b + (lane >> 4)] = s16;
+    encode_block(x[c * ldx + 32LL * b + lane], lane, b, cols, ws + c * ws_col_bytes);
   }
 }
 
@@ -101,8 +89,9 @@ namespace {
 struct XView {  // one column of prepared x (global, or this CTA's shared copy)
   const uint8_t* q0;
   const uint8_t* q1;
-  const float* scale;
+  const float* scale;  // negative: a wide block (its third digit is used)
   const float* sum16;
+  const uint8_t* q2;   // third digits
 };
 __device__ __forceinline__ XView xview(const uint8_t* ws, int cols) {
   XView v;
@@ -110,7 +99,15 @@ __device__ __forceinline__ XView xview(const uint8_t* ws, int cols) {
   v.q1 = ws + cols;
   v.scale = reinterpret_cast<const float*>(ws + 2LL * cols);
   v.sum16 = v.scale + cols / 32;
+  v.q2 = ws + x2_offset(cols);
   return v;
+}
+constexpr float kInv254 = 1.0f / 254.0f;
+__device__ __forceinline__ bool is_wide(float scale) { return __float_as_uint(scale) >> 31; }
+// 8 words of third digits at p (16-byte aligned)
+__device__ __forceinline__ void x2_words(const uint8_t* p, uint32_t (&w)[8]) {
+  const uint4 lo = *reinterpret_cast<const uint4*>(p), hi = *reinterpret_cast<const uint4*>(p + 16);
+  w[0] = lo.x; w[1] = lo.y; w[2] = lo.z; w[3] = lo.w; w[4] = hi.x; w[5] = hi.y; w[6] = hi.z; w[7] = hi.w;
 }
 
 struct Dig16 { uint4 a, b; };  // 16 digits of each plane
@@ -178,14 +175,15 @@ __device__ __forceinline__ float reduce_rows(const float (&acc)[M], int lane) {
 }
 
 // ---- per-type unit decoders ------------------------------------------------------
-// A unit is 32 values of one block.  XU: the x data of one unit, held in
-// registers for the whole kernel.  dot(blk, j, XU): the unit's contribution
-// to one row; blk is the shared address of the unit's block, j the unit's
-// index inside it.
+// A unit is 32 (or 64) values of one block.  XU: the x data of one unit, held
+// in registers for the whole kernel.  dot(blk, j, XU): the unit's contribution
+// to one row from the two leading digits; blk is the shared address of the
+// unit's block, j the unit's index inside it.  wide(blk, j, XU, q2f, boff):
+// the third digits' contribution of the unit's wide blocks, taken only where
+// has_wide(XU); it reads everything it needs from shared memory again, so the
+// common path keeps its registers.  q2f() returns the third-digit plane and
+// boff is the block's byte offset in its row (which locates the unit's columns).
 
-// Q4_K / Q5_K (native.c:173-197, 410-437).  Unit j = qs bytes 16j..16j+15:
-// low nibbles are values 64p+16h+i (sub-block 2p), high nibbles values
-// 64p+32+16h+i (sub-block 2p+1), p = j/2, h = j%2.  16-byte aligned blocks.
 // 32-value digit words (8 per plane) starting at column c.
 struct Dig32 { uint32_t a[8], b[8]; };
 __device__ __forceinline__ void dig32(const XView& x, int c, Dig32& d) {
@@ -213,6 +211,22 @@ __device__ __forceinline__ int dot32(const uint32_t (&c)[8], const Dig32& d) {
   }
   return (a0 + a1) * 254 + (b0 + b1);
 }
+// dot(codes, x2) over 32 values with the third digits at p (16-byte aligned)
+template <bool U>
+__device__ __forceinline__ int dot32_x2(const uint32_t (&c)[8], const uint8_t* p) {
+  uint32_t w[8];
+  x2_words(p, w);
+  int a0 = 0, a1 = 0;
+#pragma unroll
+  for (int k = 0; k < 8; k += 2) {
+    if constexpr (U) {
+      a0 = dp4a_us(c[k], w[k], a0); a1 = dp4a_us(c[k + 1], w[k + 1], a1);
+    } else {
+      a0 = __dp4a((int)c[k], (int)w[k], a0); a1 = __dp4a((int)c[k + 1], (int)w[k + 1], a1);
+    }
+  }
+  return a0 + a1;
+}
 
 // Q4_K / Q5_K (native.c:173-197, 410-437).  A unit is 64 values: pair p of
 // sub-blocks = qs bytes 32p..32p+31, whose low nibbles are values 64p+i
@@ -222,7 +236,7 @@ __device__ __forceinline__ int dot32(const uint32_t (&c)[8], const Dig32& d) {
 // values.  16-byte aligned blocks.
 template <int TY> struct UnitK45 {
   static constexpr int UPB = 4, VALS = 64;
-  struct XU { Dig32 a, b; float sa, sb, ma, mb; };
+  struct XU { Dig32 a, b; float sa, sb, ma, mb; };  // sa, sb < 0: a wide block
   __device__ static void load_x(const XView& x, int unit, XU& u, int) {
     const int ca = 256 * (unit >> 2) + 64 * (unit & 3), cb = ca + 32;
     dig32(x, ca, u.a);
@@ -233,11 +247,11 @@ template <int TY> struct UnitK45 {
     u.ma = *(x.sum16 + (ca >> 4)) + *(x.sum16 + (ca >> 4) + 1);
     u.mb = *(x.sum16 + (cb >> 4)) + *(x.sum16 + (cb >> 4) + 1);
   }
-  __device__ static float dot(uint32_t blk, int p, const XU& u, int) {
-    const uint4 hdr = lds128(blk);
+  __device__ static bool has_wide(const XU& u) { return is_wide(u.sa) || is_wide(u.sb); }
+  // code words of pair p: lo = sub-block 2p, hi = sub-block 2p+1 (Q4_K: 16 * code)
+  __device__ static void codes(uint32_t blk, int p, uint32_t (&lo)[8], uint32_t (&hi)[8]) {
     const uint32_t qa = blk + (TY == Q4_K ? 16 : 48) + 32 * p;
     const uint4 q0 = lds128(qa), q1 = lds128(qa + 16);
-    uint32_t lo[8], hi[8];
     if constexpr (TY == Q5_K) {
       const uint4 h0 = lds128(blk + 16), h1 = lds128(blk + 32);
 #pragma unroll
@@ -254,20 +268,45 @@ template <int TY> struct UnitK45 {
         hi[k] = q & 0xF0F0F0F0u;  // 16 * code, read unsigned
       }
     }
-    const int ia = dot32<false>(lo, u.a), ib = dot32<TY == Q4_K>(hi, u.b);
-    // (scale, min) pairs 2p and 2p+1 (native.c:52-60): for j < 4 bytes j, j+4;
-    // for j >= 4 the low 4 bits in byte j+4 and the top 2 in bytes j-4 / j.
-    // All eight of each, four per word, without branches (the four lanes of
-    // a super-block take different p); a byte permute picks the lane's pair.
+  }
+  // d * sc and the (scale, min) pairs 2p and 2p+1 (native.c:52-60): for j < 4
+  // bytes j, j+4; for j >= 4 the low 4 bits in byte j+4 and the top 2 in bytes
+  // j-4 / j.  All eight of each, four per word, without branches (the four
+  // lanes of a super-block take different p); a byte permute picks the pair.
+  __device__ static void scales(const uint4& hdr, int p, uint32_t& sca, uint32_t& scb, uint32_t& mna,
+                                uint32_t& mnb) {
     const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu, mn_lo = hdr.z & 0x3F3F3F3Fu;
     const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
     const uint32_t mn_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
     const uint32_t sel = (uint32_t)(34 * p + 16);  // bytes 2p, 2p + 1 of (lo, hi)
     const uint32_t scp = __byte_perm(sc_lo, sc_hi, sel), mnp = __byte_perm(mn_lo, mn_hi, sel);
-    const uint32_t sca = scp & 0xffu, scb = (scp >> 8) & 0xffu, mna = mnp & 0xffu, mnb = (mnp >> 8) & 0xffu;
+    sca = scp & 0xffu;
+    scb = (scp >> 8) & 0xffu;
+    mna = mnp & 0xffu;
+    mnb = (mnp >> 8) & 0xffu;
+  }
+  __device__ static float dot(uint32_t blk, int p, const XU& u) {
+    const uint4 hdr = lds128(blk);
+    uint32_t lo[8], hi[8];
+    codes(blk, p, lo, hi);
+    const int ia = dot32<false>(lo, u.a), ib = dot32<TY == Q4_K>(hi, u.b);
+    uint32_t sca, scb, mna, mnb;
+    scales(hdr, p, sca, scb, mna, mnb);
     const float d = half_f(hdr.x & 0xffff), dmin = half_f(hdr.x >> 16);
-    return d * ((float)sca * u.sa * (float)ia + (float)scb * u.sb * (float)ib) -
+    return d * ((float)sca * fabsf(u.sa) * (float)ia + (float)scb * fabsf(u.sb) * (float)ib) -
            dmin * ((float)mna * u.ma + (float)mnb * u.mb);
+  }
+  template <class Q2>
+  __device__ static float wide(uint32_t blk, int p, const XU& u, const Q2& q2f, int boff) {
+    const uint4 hdr = lds128(blk);
+    uint32_t lo[8], hi[8];
+    codes(blk, p, lo, hi);
+    const uint8_t* x2 = q2f() + 256 * (boff / Geo<TY>::bpb) + 64 * p;
+    const float ea = is_wide(u.sa) ? (float)dot32_x2<false>(lo, x2) : 0.f;
+    const float eb = is_wide(u.sb) ? (float)dot32_x2<TY == Q4_K>(hi, x2 + 32) : 0.f;
+    uint32_t sca, scb, mna, mnb;
+    scales(hdr, p, sca, scb, mna, mnb);
+    return half_f(hdr.x & 0xffff) * kInv254 * ((float)sca * fabsf(u.sa) * ea + (float)scb * fabsf(u.sb) * eb);
   }
 };
 
@@ -294,7 +333,7 @@ __device__ __forceinline__ void words8(const Dig16& lo, const Dig16& hi, bool pl
 // shifted to match, the 9 aligned words feed dp4a directly.
 struct UnitQ80 {
   static constexpr int UPB = 1, VALS = 32;
-  struct XU { uint32_t a[9], b[9]; float s; };
+  struct XU { uint32_t a[9], b[9]; float s; };  // s < 0: a wide block
   __device__ static void load_x(const XView& x, int unit, XU& u, int wmod4) {
     const int mis = (wmod4 + 34 * unit + 2) & 3;  // offset of qs past a word boundary
     const Dig16 lo = dig16(x, 32 * unit), hi = dig16(x, 32 * unit + 16);
@@ -305,7 +344,8 @@ struct UnitQ80 {
     shift_digits(w, mis, u.b);
     u.s = *(x.scale + unit);
   }
-  __device__ static float dot(uint32_t blk, int, const XU& u, int) {
+  __device__ static bool has_wide(const XU& u) { return is_wide(u.s); }
+  __device__ static float dot(uint32_t blk, int, const XU& u) {
     const uint32_t base = (blk + 2) & ~3u;
     int a0 = 0, a1 = 0, b0 = 0, b1 = 0;
 #pragma unroll
@@ -320,7 +360,19 @@ struct UnitQ80 {
       }
     }
     const float d = half_f(lds16(blk));
-    return d * u.s * (float)((a0 + a1) * 254 + (b0 + b1));
+    return d * fabsf(u.s) * (float)((a0 + a1) * 254 + (b0 + b1));
+  }
+  template <class Q2>
+  __device__ static float wide(uint32_t blk, int, const XU& u, const Q2& q2f, int boff) {
+    if (!is_wide(u.s)) return 0.f;
+    const uint32_t base = (blk + 2) & ~3u;
+    uint32_t w[8], sw[9];
+    x2_words(q2f() + 32 * (boff / 34), w);
+    shift_digits(w, (int)((blk + 2) & 3u), sw);  // shared and global addresses agree mod 16
+    int e = 0;
+#pragma unroll
+    for (int k = 0; k < 9; ++k) e = __dp4a((int)lds32(base + 4 * k), (int)sw[k], e);
+    return half_f(lds16(blk)) * fabsf(u.s) * kInv254 * (float)e;
   }
 };
 
@@ -343,53 +395,63 @@ template <bool REALIGN>
 struct UnitQ6K {
   static constexpr int UPB = 4, VALS = 64;
   // [part][group g: l<16 -> words 0..4, l>=16 -> words 4..8] x 5 words, per plane;
-  // mis: the block alignment (0 or 2) the digits are shifted for
+  // mis: the block alignment (0 or 2) the digits are shifted for; s[p] < 0:
+  // part p is a wide block
   struct XU { uint32_t a[2][10], b[2][10]; float s[2], m[2][2]; int mis; };
+  // the 9 digit words of a 32-value run shifted to alignment mis, split at l = 16
+  __device__ static void split_words(const uint32_t (&w)[8], int mis, uint32_t (&dst)[10]) {
+    uint32_t sw[9];
+    shift_digits(w, mis, sw);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) dst[k] = sw[k];
+    dst[4] = sw[4] & (mis ? 0x0000FFFFu : 0u);
+    dst[5] = sw[4] & (mis ? 0xFFFF0000u : 0xFFFFFFFFu);
+#pragma unroll
+    for (int k = 5; k < 9; ++k) dst[k + 1] = sw[k];
+  }
   __device__ static void load_x(const XView& x, int unit, XU& u, int wmod4) {
     const int blk = unit >> 2, j = unit & 3, h = j >> 1, tt = j & 1;
     const int mis = (wmod4 + 210 * blk) & 3;  // 0 or 2 (in row 0)
     u.mis = mis;
-    const uint32_t m4g0 = mis ? 0x0000FFFFu : 0u, m4g1 = mis ? 0xFFFF0000u : 0xFFFFFFFFu;
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
       const int c = 256 * blk + 128 * h + 64 * p + 32 * tt;
       const Dig16 lo = dig16(x, c), hi = dig16(x, c + 16);
-      uint32_t w[8], sw[9];
+      uint32_t w[8];
 #pragma unroll
       for (int plane = 0; plane < 2; ++plane) {
         words8(lo, hi, plane == 1, w);
-        shift_digits(w, mis, sw);
-        uint32_t* dst = plane ? u.b[p] : u.a[p];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) dst[k] = sw[k];
-        dst[4] = sw[4] & m4g0;
-        dst[5] = sw[4] & m4g1;
-#pragma unroll
-        for (int k = 5; k < 9; ++k) dst[k + 1] = sw[k];
+        split_words(w, mis, plane ? u.b[p] : u.a[p]);
       }
       u.s[p] = *(x.scale + (c >> 5));
       u.m[p][0] = *(x.sum16 + (c >> 4));
       u.m[p][1] = *(x.sum16 + (c >> 4) + 1);
     }
   }
-  __device__ static float dot(uint32_t blk, int j, const XU& u, int) {
-    const int h = j >> 1, tt = j & 1;
-    uint32_t aql = (blk + 64 * h + 32 * tt) & ~3u, aqh = (blk + 128 + 32 * h) & ~3u;
-    uint32_t sh = 0, pq = 0, ph = 0;  // realignment: shift and the word before word k
-    if constexpr (REALIGN) {
-      const bool flip = (int)(blk & 3u) != u.mis;
-      sh = flip ? 16u : 0u;
-      if (flip && u.mis == 2) {  // weights 2 bytes before the digits' positions
-        aql -= 4;
-        aqh -= 4;
-      } else {
-        pq = lds32(aql);
-        ph = lds32(aqh);
+  __device__ static bool has_wide(const XU& u) { return is_wide(u.s[0]) || is_wide(u.s[1]); }
+  // Code words k of both parts, aligned like the digits: call with k = 0..8 in
+  // order (REALIGN carries the previous word).
+  struct Reader {
+    uint32_t aql, aqh, sh = 0, pq = 0, ph = 0;
+    int tt;
+    __device__ Reader(uint32_t blk, int j, int mis) {
+      const int h = j >> 1;
+      tt = j & 1;
+      aql = (blk + 64 * h + 32 * tt) & ~3u;
+      aqh = (blk + 128 + 32 * h) & ~3u;
+      if constexpr (REALIGN) {
+        const bool flip = (int)(blk & 3u) != mis;
+        sh = flip ? 16u : 0u;
+        if (flip && mis == 2) {  // weights 2 bytes before the digits' positions
+          aql -= 4;
+          aqh -= 4;
+        } else {
+          pq = lds32(aql);
+          ph = lds32(aqh);
+        }
       }
     }
-    int acc[2][2][2] = {};  // [part][group][plane]
-#pragma unroll
-    for (int k = 0; k < 9; ++k) {
+    __device__ void next(int k, uint32_t& c0, uint32_t& c1) {
       uint32_t ql, s;
       if constexpr (REALIGN) {
         const uint32_t nq = lds32(aql + 4 * k + 4), nh = lds32(aqh + 4 * k + 4);
@@ -401,8 +463,18 @@ struct UnitQ6K {
         ql = lds32(aql + 4 * k);
         s = lds32(aqh + 4 * k) >> (2 * tt);
       }
-      const uint32_t c0 = (ql & 0x0F0F0F0Fu) | ((s & 0x03030303u) << 4);
-      const uint32_t c1 = ((ql >> 4) & 0x0F0F0F0Fu) | (s & 0x30303030u);
+      c0 = (ql & 0x0F0F0F0Fu) | ((s & 0x03030303u) << 4);
+      c1 = ((ql >> 4) & 0x0F0F0F0Fu) | (s & 0x30303030u);
+    }
+  };
+  __device__ static float dot(uint32_t blk, int j, const XU& u) {
+    const int h = j >> 1, tt = j & 1;
+    Reader rd(blk, j, u.mis);
+    int acc[2][2][2] = {};  // [part][group][plane]
+#pragma unroll
+    for (int k = 0; k < 9; ++k) {
+      uint32_t c0, c1;
+      rd.next(k, c0, c1);
       if (k <= 4) {
         acc[0][0][0] = __dp4a((int)c0, (int)u.a[0][k], acc[0][0][0]);
         acc[0][0][1] = __dp4a((int)c0, (int)u.b[0][k], acc[0][0][1]);
@@ -424,10 +496,51 @@ struct UnitQ6K {
       for (int g = 0; g < 2; ++g) {
         const int sc = (int)(int8_t)(((p ? sc23 : sc01) >> (8 * g)) & 0xff);
         // codes are 0..63 and value = d * sc * (code - 32)
-        const float q = u.s[p] * (float)(acc[p][g][0] * 254 + acc[p][g][1]) - 32.0f * u.m[p][g];
+        const float q = fabsf(u.s[p]) * (float)(acc[p][g][0] * 254 + acc[p][g][1]) - 32.0f * u.m[p][g];
         r = fmaf((float)sc, q, r);
       }
     return half_f(lds16(blk + 208)) * r;
+  }
+  template <class Q2>
+  __device__ static float wide(uint32_t blk, int j, const XU& u, const Q2& q2f, int boff) {
+    const int h = j >> 1, tt = j & 1;
+    const uint8_t* x2 = q2f() + 256 * (boff / 210) + 128 * h + 32 * tt;  // part p at + 64 p
+    uint32_t d[2][10];
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      uint32_t w[8];
+      x2_words(x2 + 64 * p, w);
+      if (!is_wide(u.s[p])) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) w[k] = 0u;
+      }
+      split_words(w, u.mis, d[p]);
+    }
+    Reader rd(blk, j, u.mis);
+    int e[2][2] = {};
+#pragma unroll
+    for (int k = 0; k < 9; ++k) {
+      uint32_t c0, c1;
+      rd.next(k, c0, c1);
+      if (k <= 4) {
+        e[0][0] = __dp4a((int)c0, (int)d[0][k], e[0][0]);
+        e[1][0] = __dp4a((int)c1, (int)d[1][k], e[1][0]);
+      }
+      if (k >= 4) {
+        e[0][1] = __dp4a((int)c0, (int)d[0][k + 1], e[0][1]);
+        e[1][1] = __dp4a((int)c1, (int)d[1][k + 1], e[1][1]);
+      }
+    }
+    const uint32_t sc01 = lds16(blk + 192 + 8 * h + 2 * tt), sc23 = lds16(blk + 196 + 8 * h + 2 * tt);
+    float r = 0.f;
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        const int sc = (int)(int8_t)(((p ? sc23 : sc01) >> (8 * g)) & 0xff);
+        r = fmaf((float)sc * fabsf(u.s[p]), (float)e[p][g], r);
+      }
+    return half_f(lds16(blk + 208)) * kInv254 * r;
   }
 };
 
@@ -438,33 +551,47 @@ struct UnitQ6K {
 // way once, when they are loaded.  8-byte aligned blocks.
 struct UnitIQ4XS {
   static constexpr int UPB = 8, VALS = 32;
-  struct XU { uint32_t a[8], b[8]; float s; };
-  __device__ static void load_x(const XView& x, int unit, XU& u, int) {
-    const Dig16 lo = dig16(x, 32 * unit), hi = dig16(x, 32 * unit + 16);
+  struct XU { uint32_t a[8], b[8]; float s; };  // s < 0: a wide block
+  // 16 digits from each half of a 32-value run, interleaved as the book's bytes come out
+  __device__ static void interleave(const uint4& lo, const uint4& hi, uint32_t (&o)[8]) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      u.a[2 * k] = __byte_perm(w4(lo.a, k), w4(hi.a, k), 0x5140);
-      u.a[2 * k + 1] = __byte_perm(w4(lo.a, k), w4(hi.a, k), 0x7362);
-      u.b[2 * k] = __byte_perm(w4(lo.b, k), w4(hi.b, k), 0x5140);
-      u.b[2 * k + 1] = __byte_perm(w4(lo.b, k), w4(hi.b, k), 0x7362);
+      o[2 * k] = __byte_perm(w4(lo, k), w4(hi, k), 0x5140);
+      o[2 * k + 1] = __byte_perm(w4(lo, k), w4(hi, k), 0x7362);
     }
+  }
+  __device__ static void load_x(const XView& x, int unit, XU& u, int) {
+    const Dig16 lo = dig16(x, 32 * unit), hi = dig16(x, 32 * unit + 16);
+    interleave(lo.a, hi.a, u.a);
+    interleave(lo.b, hi.b, u.b);
     u.s = *(x.scale + unit);
   }
-  __device__ static float dot(uint32_t blk, int j, const XU& u, int) {
-    const uint2 hdr = lds64(blk);  // d | scales_h | scales_l[4]
-    const uint2 q01 = lds64(blk + 8 + 16 * j), q23 = lds64(blk + 16 + 16 * j);
-    const uint32_t qw[4] = {q01.x, q01.y, q23.x, q23.y};
+  __device__ static bool has_wide(const XU& u) { return is_wide(u.s); }
+  // book values of the 8 codes in word q: v0 = codes of bytes 0-1, v1 = bytes 2-3
+  __device__ static void book(uint32_t q, uint32_t& v0, uint32_t& v1) {
     // the book as int8: -127 -104 -83 -65 -49 -35 -22 -10 | 1 13 25 38 53 69 89 113
     const uint32_t T0 = 0xBFAD9881u, T1 = 0xF6EADDCFu, T2 = 0x26190D01u, T3 = 0x71594535u;
+    // the selectors of all 8 nibbles at once (prmt reads the low 16 bits):
+    // bits 0-2 index a half of the book, bit 3 picks the half
+    const uint32_t sel = q & 0x77777777u, pick = ((q >> 1) & 0x44444444u) | 0x32103210u;
+    v0 = __byte_perm(__byte_perm(T0, T1, sel), __byte_perm(T2, T3, sel), pick);
+    const uint32_t sel1 = sel >> 16, pick1 = pick >> 16;
+    v1 = __byte_perm(__byte_perm(T0, T1, sel1), __byte_perm(T2, T3, sel1), pick1);
+  }
+  __device__ static float block_scale(uint32_t blk, int j) {
+    const uint2 hdr = lds64(blk);  // d | scales_h | scales_l[4]
+    const uint32_t sh = hdr.x >> 16;
+    const int ls = ((hdr.y >> (4 * j)) & 15) | (int)(((sh >> (2 * j)) & 3u) << 4);
+    return half_f(hdr.x & 0xffff) * (float)(ls - 32);
+  }
+  __device__ static float dot(uint32_t blk, int j, const XU& u) {
+    const uint2 q01 = lds64(blk + 8 + 16 * j), q23 = lds64(blk + 16 + 16 * j);
+    const uint32_t qw[4] = {q01.x, q01.y, q23.x, q23.y};
     int a = 0, b = 0, a1 = 0, b1 = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      // the selectors of all 8 nibbles at once (prmt reads the low 16 bits):
-      // bits 0-2 index a half of the book, bit 3 picks the half
-      const uint32_t sel = qw[k] & 0x77777777u, pick = ((qw[k] >> 1) & 0x44444444u) | 0x32103210u;
-      const uint32_t v0 = __byte_perm(__byte_perm(T0, T1, sel), __byte_perm(T2, T3, sel), pick);
-      const uint32_t sel1 = sel >> 16, pick1 = pick >> 16;
-      const uint32_t v1 = __byte_perm(__byte_perm(T0, T1, sel1), __byte_perm(T2, T3, sel1), pick1);
+      uint32_t v0, v1;
+      book(qw[k], v0, v1);
       a = __dp4a((int)v0, (int)u.a[2 * k], a);
       b = __dp4a((int)v0, (int)u.b[2 * k], b);
       a1 = __dp4a((int)v1, (int)u.a[2 * k + 1], a1);
@@ -472,9 +599,25 @@ struct UnitIQ4XS {
     }
     a += a1;
     b += b1;
-    const uint32_t sh = hdr.x >> 16;
-    const int ls = ((hdr.y >> (4 * j)) & 15) | (int)(((sh >> (2 * j)) & 3u) << 4);
-    return half_f(hdr.x & 0xffff) * (float)(ls - 32) * u.s * (float)(a * 254 + b);
+    return block_scale(blk, j) * fabsf(u.s) * (float)(a * 254 + b);
+  }
+  template <class Q2>
+  __device__ static float wide(uint32_t blk, int j, const XU& u, const Q2& q2f, int boff) {
+    if (!is_wide(u.s)) return 0.f;
+    const uint8_t* x2 = q2f() + 256 * (boff / 136) + 32 * j;
+    uint32_t d[8];
+    interleave(*reinterpret_cast<const uint4*>(x2), *reinterpret_cast<const uint4*>(x2 + 16), d);
+    const uint2 q01 = lds64(blk + 8 + 16 * j), q23 = lds64(blk + 16 + 16 * j);
+    const uint32_t qw[4] = {q01.x, q01.y, q23.x, q23.y};
+    int e = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t v0, v1;
+      book(qw[k], v0, v1);
+      e = __dp4a((int)v0, (int)d[2 * k], e);
+      e = __dp4a((int)v1, (int)d[2 * k + 1], e);
+    }
+    return block_scale(blk, j) * fabsf(u.s) * kInv254 * (float)e;
   }
 };
 
@@ -487,6 +630,7 @@ template <> struct UnitOf<kQ6KRealign> { using T = UnitQ6K<true>; };
 template <> struct UnitOf<IQ4_XS> { using T = UnitIQ4XS; };
 
 constexpr int kThreads = 256, kWarps = 8, kMaxRowsPerStage = 64, kStages = 3;
+constexpr size_t kMaxTileSmem = 150 * 1024;  // dynamic shared memory a tile CTA may take
 
 // The last CTA to finish (a ticket counter, no waiting) runs one operation on
 // the complete output vector y (n = rows values).  Every CTA publishes its
@@ -671,8 +815,15 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   }
   typename U::XU xu[UL];  // this lane's x, for the whole kernel
   const XView xv = xview(xws, a.cols);
+  // the third-digit plane, rebuilt from the kernel arguments where a wide block needs it
+  auto q2f = [&]() -> const uint8_t* {
+    if (a.xmode) return smem + a.xenc_off + x2_offset(a.cols);
+    const int g = a.experts ? (int)(blockIdx.x / (gridDim.x / a.n_sel)) % a.n_ids : 0;
+    return a.ws + (size_t)g * (size_t)a.ws_stride + x2_offset(a.cols);
+  };
 #pragma unroll
   for (int k = 0; k < UL; ++k) U::load_x(xv, ls + k * lps < units ? ls + k * lps : 0, xu[k], wmod4);
+
 
   float best_v = -FLT_MAX;  // POST_ARGMAX: this thread's best finalized row
   int best_i = 0x7fffffff;
@@ -691,14 +842,21 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   };
 
   int k = 0;
+  __shared__ int landed[2];  // thread 0's verdict on stage k, in slot k & 1
   for (; k < my; ++k) {
-    // stage k landed; the barrier also retires iteration k-1, whose slot the
-    // refill below reuses
-    if (!mbar_wait_bounded(smem_addr(&bars[k % S]), (uint32_t)(k / S) & 1u)) {
-      if (lane == 0) atomicOr(status, (int)kStatusWaitTimeout);
+    // stage k landed?  One thread waits (bounded) and shares the verdict, so
+    // every thread leaves the loop at the same iteration; the barrier also
+    // retires iteration k-1, whose slot the refill below reuses
+    const uint32_t bar = smem_addr(&bars[k % S]), parity = (uint32_t)(k / S) & 1u;
+    if (tid == 0) landed[k & 1] = mbar_wait_bounded(bar, parity) ? 1 : 0;
+    __syncthreads();
+    if (!landed[k & 1]) {
+      if (tid == 0) atomicOr(status, (int)kStatusWaitTimeout);
       break;
     }
-    __syncthreads();
+    // the phase is complete: each thread's own wait returns at once and orders
+    // its reads of the slot after the copy
+    (void)mbar_wait_bounded(bar, parity);
     if (k > 0) finalize(k - 1);
     if (tid == 0 && k + S - 1 < my) {
       fence_proxy_async();  // generic reads of the slot precede its async refill
@@ -717,7 +875,12 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
       const uint32_t rowa = base + (uint32_t)i * (uint32_t)a.row_bytes;
       float v = 0.f;
 #pragma unroll
-      for (int kk = 0; kk < UL; ++kk) v += uon[kk] * U::dot(rowa + (uint32_t)uoff[kk], uj[kk], xu[kk], lane);
+      for (int kk = 0; kk < UL; ++kk) {
+        const uint32_t blk = rowa + (uint32_t)uoff[kk];
+        float d = U::dot(blk, uj[kk], xu[kk]);
+        if (U::has_wide(xu[kk])) d += U::wide(blk, uj[kk], xu[kk], q2f, uoff[kk]);  // rare
+        v += uon[kk] * d;
+      }
       acc[i] = on * v;
     }
     float* r = red + (size_t)(k & 1) * kWarps * M;
@@ -753,14 +916,18 @@ TilePlan plan_tile(size_t row_bytes, int rows, int cols, int vals, size_t xenc_b
   p.m = m_for(32 * 1024);
   if ((long long)rows / ((long long)rs * p.m) < 148LL * 3) p.m = m_for(20 * 1024);
   if (rs * p.m > kMaxRowsPerStage) p.m = kMaxRowsPerStage / rs;
-  const size_t sb = ((size_t)rs * p.m * row_bytes + 16 + 32 + 127) & ~(size_t)127;
-  p.stage_bytes = (int)sb;
-  p.smem = (size_t)kStages * sb + 2 * kWarps * p.m * sizeof(float) + (size_t)kStages * 8;
-  if (xenc_bytes) {
-    p.xenc_off = (int)((p.smem + 255) & ~(size_t)255);
-    p.smem = (size_t)p.xenc_off + xenc_bytes;
+  for (;;) {
+    const size_t sb = ((size_t)rs * p.m * row_bytes + 16 + 32 + 127) & ~(size_t)127;
+    p.stage_bytes = (int)sb;
+    p.smem = (size_t)kStages * sb + 2 * kWarps * p.m * sizeof(float) + (size_t)kStages * 8;
+    if (xenc_bytes) {
+      p.xenc_off = (int)((p.smem + 255) & ~(size_t)255);
+      p.smem = (size_t)p.xenc_off + xenc_bytes;
+    }
+    // a prologue's copy of x shares the CTA's shared memory: smaller stages
+    if (p.smem <= kMaxTileSmem || p.m == 1) return p;
+    p.m /= 2;
   }
-  return p;
 }
 
 template <int TY, int UL, int M>
@@ -768,15 +935,22 @@ int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return -4;
-  static int sms[64] = {};
-  static bool smem_set[64] = {};
-  if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-  constexpr int kMaxSmem = 150 * 1024;
-  if (!smem_set[dev]) {
+  // First-call caches per device, safe under concurrent callers: both values
+  // are idempotent, so two threads racing on a first call only repeat the query.
+  static std::atomic<int> sms[64];
+  static std::atomic<bool> smem_set[64];
+  int nsm = sms[dev].load(std::memory_order_relaxed);
+  if (!nsm) {
+    if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || nsm <= 0)
+      return -100 - (int)cudaGetLastError();
+    sms[dev].store(nsm, std::memory_order_relaxed);
+  }
+  constexpr int kMaxSmem = (int)kMaxTileSmem;
+  if (!smem_set[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(mv_tile_kernel<TY, UL, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
         cudaSuccess)
       return -100 - (int)cudaGetLastError();
-    smem_set[dev] = true;
+    smem_set[dev].store(true, std::memory_order_release);
   }
   if (smem > (size_t)kMaxSmem) return 1;
   const int rows_per_stage = M << ta.rs_log2;
@@ -785,7 +959,7 @@ int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
   const int minb = tile_min_blocks<TY>();
   if (per_sm > minb) per_sm = minb;
   if (per_sm < 1) per_sm = 1;
-  int grid = sms[dev] * per_sm;
+  int grid = nsm * per_sm;
   if (ta.experts) {  // n_sel equal CTA groups
     int cpe = grid / ta.n_sel;
     if (cpe > nstages) cpe = nstages;
@@ -816,7 +990,7 @@ int lane_max_grid() {
   return sms * 3;  // tile_min_blocks <= 3 CTAs per SM
 }
 
-size_t lane_workspace_bytes(int cols) { return (size_t)cols * 2 + (size_t)(cols / 32) * 4 + (size_t)(cols / 16) * 4; }
+size_t lane_workspace_bytes(int cols) { return (size_t)encoded_bytes(cols); }
 
 bool lane_supported(int type_id, const uint8_t* w, size_t row_bytes, int cols) {
   if (cols % 256 != 0 || cols / 32 > 4 * kThreads) return false;

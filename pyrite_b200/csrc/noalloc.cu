@@ -16,16 +16,19 @@
 #include <mutex>
 
 #include "kernels.cuh"
+#include "post_ops.cuh"
 #include "../../include/pyrite_b200.h"
 
 namespace pyr {
 namespace {
 
-// Encoded-activation bytes for PYRITE_NOALLOC_MAX_COLS columns: two int8 digit
-// planes, one fp32 scale per 32 values and one fp32 sum per 16 values.
-constexpr size_t kNoAllocScratchBytes =
-    (size_t)PYRITE_NOALLOC_MAX_COLS * 2 + (size_t)(PYRITE_NOALLOC_MAX_COLS / 32) * 4 +
-    (size_t)(PYRITE_NOALLOC_MAX_COLS / 16) * 4;
+// Encoded-activation bytes for the widest activation the batch-1 kernel takes
+// (kNoAllocLaneCols values): three int8 digit planes, one fp32 scale per 32
+// values and one fp32 sum per 16 values -- 108 KiB.  Wider activations (up to
+// PYRITE_NOALLOC_MAX_COLS) go to the generic kernel, which reads x directly
+// and needs no scratch.
+constexpr int kNoAllocLaneCols = 32768;
+constexpr size_t kNoAllocScratchBytes = (size_t)encoded_bytes(kNoAllocLaneCols);
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -77,7 +80,7 @@ extern "C" int pyrite_cuda_matvec_noalloc(int type_id, const void* weights, size
   if ((rc = scratch_for_current_device(&scratch))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint8_t* w = static_cast<const uint8_t*>(weights);
-  if (lane_supported(type_id, w, rb, (int)cols)) {
+  if (cols <= (size_t)kNoAllocLaneCols && lane_supported(type_id, w, rb, (int)cols)) {
     // The encoding kernel writes every byte the product kernel then reads, so
     // nothing in the array has to start at zero; what an earlier call left
     // there is simply overwritten.

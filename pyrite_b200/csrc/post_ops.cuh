@@ -8,35 +8,53 @@
 
 namespace pyr {
 
-// The two int8 digits of v in a 32-value block of largest magnitude amax:
-// t = v * r with r = 127 / amax (0 for an all-zero block), d0 = rint(t),
-// d1 = rint((t - d0) * 254), so v ~ (d0 + d1 / 254) * amax / 127.  No clamp is
-// needed: |t| rounds to at most 127 and |t - d0| <= 1/2.
+// Encoded activation (the batch-1 kernels' prepared x), per column of `cols`
+// values (cols % 32 == 0):
+//   x0[cols] int8 | x1[cols] int8 | scale[cols/32] fp32 | sum16[cols/16] fp32 | x2[cols] int8
+// For a 32-value block of largest magnitude amax, t = v * 127 / amax and
+//   v ~ (amax / 127) * (x0 + x1 / 254 + x2 / 254^2),
+// x0 = rint(t), x1 = rint((t - x0) * 254), x2 = rint(((t - x0) * 254 - x1) * 254)
+// (no clamps: |t| rounds to at most 127 and each remainder is at most 1/2).
+// scale[b] = amax / 127 / 254, stored NEGATIVE for a "wide" block: one in which
+// at least 4 nonzero values lie more than 2^8 below amax.  The kernels use the
+// third digit only for wide blocks: two digits bound each value's error by
+// amax / 64516, which for a block whose other values sit far below one
+// outlier (an outlier channel) is large next to those values; the third digit
+// brings the bound to amax / 16.4e6.  Near-Gaussian data is essentially never
+// wide (1e-4 of blocks), so the common path pays nothing for it.
+__host__ __device__ constexpr long long x2_offset(long long cols) { return 2 * cols + cols / 8 + cols / 4; }
+__host__ __device__ constexpr long long encoded_bytes(long long cols) { return x2_offset(cols) + cols; }
+constexpr int kWideCount = 4;         // nonzero values far below amax that make a block wide
+constexpr float kWideRatio = 256.0f;  // "far below": |v| * 256 < amax
+
 __device__ __forceinline__ float digit_ratio(float amax) { return amax > 0.0f ? 127.0f / amax : 0.0f; }
-__device__ __forceinline__ void two_digits(float v, float r, int& d0, int& d1) {
+__device__ __forceinline__ void three_digits(float v, float r, int& d0, int& d1, int& d2) {
   const float t = v * r;
   d0 = __float2int_rn(t);
-  d1 = __float2int_rn((t - (float)d0) * 254.0f);
+  const float u = (t - (float)d0) * 254.0f;
+  d1 = __float2int_rn(u);
+  d2 = __float2int_rn((u - (float)d1) * 254.0f);
 }
+__device__ __forceinline__ bool far_below(float v, float amax) { return v != 0.0f && fabsf(v) * kWideRatio < amax; }
 
-// Encode 32 values (lane l holds value l of block b) into the prepared-x
-// layout of mv_tile.cu: digits x0, x1, scale s/254 (s = amax / 127), and the
-// two 16-value sums.
+// Encode 32 values (lane l holds value l of block b) into the layout above.
 __device__ __forceinline__ void encode_block(float v, int lane, int b, int cols, uint8_t* ws) {
   float amax = fabsf(v);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   const float s = amax / 127.0f;
-  int d0, d1;
-  two_digits(v, digit_ratio(amax), d0, d1);
+  const bool wide = __popc(__ballot_sync(0xffffffffu, far_below(v, amax))) >= kWideCount;
+  int d0, d1, d2;
+  three_digits(v, digit_ratio(amax), d0, d1, d2);
   float s16 = v;
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
   ws[32 * b + lane] = (uint8_t)(int8_t)d0;
   ws[cols + 32 * b + lane] = (uint8_t)(int8_t)d1;
+  ws[x2_offset(cols) + 32 * b + lane] = (uint8_t)(int8_t)d2;
   float* scale = reinterpret_cast<float*>(ws + 2 * cols);
   float* sum16 = scale + cols / 32;
-  if (lane == 0) scale[b] = s / 254.0f;
+  if (lane == 0) scale[b] = wide ? -(s / 254.0f) : s / 254.0f;
   if ((lane & 15) == 0) sum16[2 * b + (lane >> 4)] = s16;
 }
 
@@ -109,17 +127,23 @@ __device__ __forceinline__ void encode_group(const float (&v)[16], int g, int co
   for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
   amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
   const float s = amax / 127.0f, r = digit_ratio(amax);
-  uint32_t p0[4], p1[4];
+  int nsmall = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) nsmall += far_below(v[i], amax) ? 1 : 0;
+  nsmall += __shfl_xor_sync(0xffffffffu, nsmall, 1);
+  uint32_t p0[4], p1[4], p2[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     p0[q] = 0u;
     p1[q] = 0u;
+    p2[q] = 0u;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      int d0, d1;
-      two_digits(v[4 * q + j], r, d0, d1);
+      int d0, d1, d2;
+      three_digits(v[4 * q + j], r, d0, d1, d2);
       p0[q] |= ((uint32_t)d0 & 0xffu) << (8 * j);
       p1[q] |= ((uint32_t)d1 & 0xffu) << (8 * j);
+      p2[q] |= ((uint32_t)d2 & 0xffu) << (8 * j);
     }
   }
   float a8[8], a4[4];
@@ -131,8 +155,9 @@ __device__ __forceinline__ void encode_group(const float (&v)[16], int g, int co
   if (!on) return;
   *reinterpret_cast<uint4*>(enc + 16 * g) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
   *reinterpret_cast<uint4*>(enc + cols + 16 * g) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+  *reinterpret_cast<uint4*>(enc + x2_offset(cols) + 16 * g) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
   float* scale = reinterpret_cast<float*>(enc + 2 * cols);
-  if ((g & 1) == 0) scale[g >> 1] = s / 254.0f;
+  if ((g & 1) == 0) scale[g >> 1] = nsmall >= kWideCount ? -(s / 254.0f) : s / 254.0f;
   scale[cols / 32 + g] = s16;
   if (out) {
     float4* o = reinterpret_cast<float4*>(out + 16 * g);
@@ -153,7 +178,8 @@ __device__ __forceinline__ void load16(const float* p, float (&v)[16]) {  // thr
   }
 }
 
-// block_rmsnorm_encode for a CTA prologue (x, w 16-byte aligned, n % 32 == 0).
+// block_rmsnorm_encode for a CTA prologue (x, w 16-byte aligned, n % 128 == 0:
+// the x2 plane's 16-byte stores need x2_offset(n) % 16 == 0).
 // Each thread's first group of x and w stays in registers, so for n up to
 // 16 * blockDim.x the statistics and the encoding cost one round trip to L2.
 // 1 / sqrt(mean(x^2) + eps) of n values (x 16-byte aligned, n % 16 == 0) for
@@ -213,7 +239,7 @@ __device__ __forceinline__ void cta_rmsnorm_encode(const float* x, const float* 
   }
 }
 
-// warps_silu_mul_encode for a CTA prologue (gu 16-byte aligned, f % 32 == 0).
+// warps_silu_mul_encode for a CTA prologue (gu 16-byte aligned, f % 128 == 0).
 __device__ __forceinline__ void cta_silu_mul_encode(const float* gu, int f, float* out, uint8_t* enc) {
   const int G = f / 16, nt = blockDim.x;
   for (int g0 = 0; g0 < G; g0 += nt) {

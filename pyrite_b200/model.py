@@ -417,4 +417,16 @@ class MixedDecoder:
         self.reset(prompt)
         self.run_steps(len(prompt) + max_new_tokens - 1)
         torch.cuda.synchronize(self.dev)
+        self.check_status()
         return [int(t) for t in self.tokens[: len(prompt) + max_new_tokens].cpu()]
+
+    def check_status(self) -> None:
+        """Raise if a kernel of the steps run so far gave up a bounded wait (a
+        copy that never landed, or, across GPUs, a peer of the NVLink sum that
+        never arrived: its partials were then not added and the ranks' tokens
+        are no longer valid).  Reads and clears the device status word; call
+        after a synchronize."""
+        code = int(self.lib.pyrite_cuda_status(1))
+        if code != 0:
+            raise RuntimeError(f"decode step failed on the device (status word {code:#x}): a bounded wait timed out "
+                               "or an expert id was out of range; the generated tokens are not valid")

@@ -175,8 +175,8 @@ class ShardedDecoder(MixedDecoder):
         buffer address and this rank's call counter."""
         L, d, h = self.lib, self.dev, self.spec.hidden_size
         ptr, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
-        _check(L.pyrite_cuda_ipc_buffer_create(L.pyrite_cuda_allreduce_buffer_size(h), ctypes.byref(ptr), handle),
-               "ipc buffer")
+        self.ar_buffer_len = int(L.pyrite_cuda_allreduce_buffer_size(h))
+        _check(L.pyrite_cuda_ipc_buffer_create(self.ar_buffer_len, ctypes.byref(ptr), handle), "ipc buffer")
         self._ipc_owned = ptr.value
         handles: list[bytes | None] = [None] * self.world
         dist.all_gather_object(handles, bytes(handle), group=self.group)
@@ -231,7 +231,8 @@ class ShardedDecoder(MixedDecoder):
         memory (pyrite_cuda_allreduce_sum), or NCCL when p2p is off."""
         if self.peer_buffers is not None:
             _check(self.lib.pyrite_cuda_allreduce_sum(self.part.data_ptr(), self.hidden.data_ptr(), self.part.numel(),
-                                                      self.peer_buffers.data_ptr(), self.world, self.rank,
+                                                      self.peer_buffers.data_ptr(), self.ar_buffer_len, self.world,
+                                                      self.rank,
                                                       self.ar_epoch.data_ptr(), stream), "allreduce")
             return
         dist.all_reduce(self.part, group=self.group)

@@ -80,7 +80,8 @@ def allreduce_check(rank: int, world: int, dev) -> int:
     lib = _lib.require()
     n = 4096
     ptr, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
-    _check(lib.pyrite_cuda_ipc_buffer_create(lib.pyrite_cuda_allreduce_buffer_size(n), ctypes.byref(ptr), handle), "c")
+    size = int(lib.pyrite_cuda_allreduce_buffer_size(n))
+    _check(lib.pyrite_cuda_ipc_buffer_create(size, ctypes.byref(ptr), handle), "c")
     handles = [None] * world
     dist.all_gather_object(handles, bytes(handle))
     ptrs, opened = [], []
@@ -103,7 +104,7 @@ def allreduce_check(rank: int, world: int, dev) -> int:
         part = torch.randn(n, device=dev, generator=g)
         base = torch.full((n,), float(it), device=dev)
         out = base.clone()
-        assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), n, peers.data_ptr(), world, rank,
+        assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), n, peers.data_ptr(), size, world, rank,
                                              epoch.data_ptr(), s.cuda_stream) == 0
         ref = part.clone()
         dist.all_reduce(ref)
@@ -119,7 +120,7 @@ def allreduce_check(rank: int, world: int, dev) -> int:
     with torch.cuda.stream(side):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=side):
-            assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), n, peers.data_ptr(), world, rank,
+            assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), n, peers.data_ptr(), size, world, rank,
                                                  epoch.data_ptr(), side.cuda_stream) == 0
     torch.cuda.synchronize(dev)
     dist.barrier()
@@ -139,7 +140,7 @@ def allreduce_check(rank: int, world: int, dev) -> int:
                 for _ in range(100):
                     if name == "nvlink":
                         assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), n, peers.data_ptr(),
-                                                             world, rank, epoch.data_ptr(), side.cuda_stream) == 0
+                                                             size, world, rank, epoch.data_ptr(), side.cuda_stream) == 0
                     else:
                         dist.all_reduce(part)
         torch.cuda.synchronize(dev)

@@ -73,7 +73,7 @@ def test_nvlink_allreduce_wait_gives_up_and_reports(cuda_device):
     part = torch.ones(n, device="cuda")
     out = torch.full((n,), 3.0, device="cuda")
     K.status()  # start clean
-    assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), n, peers.data_ptr(), 2, 0, epoch.data_ptr(),
+    assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), n, peers.data_ptr(), size, 2, 0, epoch.data_ptr(),
                                          torch.cuda.current_stream().cuda_stream) == 0
     torch.cuda.synchronize()
     assert K.status() & 1  # the wait gave up (and the bit is cleared again)
@@ -85,7 +85,10 @@ def test_nvlink_allreduce_wait_gives_up_and_reports(cuda_device):
         assert lib.pyrite_cuda_ipc_buffer_close(p, 1) == 0
     # argument checks: n not a multiple of 4, rank outside the world
     s = torch.cuda.current_stream().cuda_stream
-    assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), 6, peers.data_ptr(), 2, 0, epoch.data_ptr(),
+    assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), 6, peers.data_ptr(), size, 2, 0, epoch.data_ptr(),
                                          s) == -3
-    assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), n, peers.data_ptr(), 2, 2, epoch.data_ptr(),
+    assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), n, peers.data_ptr(), size, 2, 2, epoch.data_ptr(),
                                          s) == -3
+    # n beyond what the buffers were created for
+    assert lib.pyrite_cuda_allreduce_sum(part.data_ptr(), out.data_ptr(), 2 * n, peers.data_ptr(), size, 2, 0,
+                                         epoch.data_ptr(), s) == -3

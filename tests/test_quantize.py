@@ -68,3 +68,18 @@ def test_q4_k_m_mix_rule():
     assert moe_tensor_type(c4, "blk.0.ffn_gate_inp.weight") == 0
     assert [moe_tensor_type(c4, f"blk.{i}.ffn_down_exps.weight") for i in range(2)] == [14, 12]
     assert moe_tensor_type(c4, "blk.5.ffn_up_exps.weight") == 12
+
+
+@pytest.mark.parametrize("ggml_type", [8, 12, 13, 14, 23])
+def test_numpy_encoders_equal_the_library_quantizer(ggml_type):
+    """oracle/encoders.py (the reference arm's input builder, which must not
+    load libpyrite_b200.so) writes the same bytes as pyrite_b200.quantize on
+    Gaussian weights and on edge blocks (zeros, tiny, huge, constant, ties)."""
+    from oracle import encoders as E
+    from pyrite_b200.quantize import gaussian_weights, quantize
+
+    rng = np.random.default_rng(ggml_type)
+    edge = np.concatenate([np.zeros(256), rng.normal(0, 1, 256) * 1e-6, rng.normal(0, 1, 512) * 300,
+                           np.full(256, 0.5), rng.integers(-3, 4, 256).astype(float) * 0.01])
+    for v in (gaussian_weights(16, 4096, 11), edge):
+        assert E.quantize(ggml_type, v) == quantize(ggml_type, v)
