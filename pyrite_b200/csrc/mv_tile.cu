@@ -14,7 +14,9 @@
 //        sum (d*sc*q - m) x = d*sc*(s_b/254)*(254*sum q x0 + sum q x1 [+ sum q x2 / 254]) - m*sum x.
 //    The third digit is used only for "wide" blocks (flagged by a negative
 //    scale: a few values far below the block's largest, i.e. an outlier
-//    channel), where two digits would lose the small values' precision.
+//    channel), where two digits would lose the small values' precision; a
+//    CTA adds those terms to its rows after streaming them (wide_pass), and
+//    only when x has a wide block, so the streaming loop is the same either way.
 //  * A CTA (256 threads) owns whole rows.  Its lanes are split into RS row
 //    slots; lane l of a slot always handles the same units (32-value pieces)
 //    of a row, so it loads its x digits once, into registers, for the whole
@@ -91,7 +93,7 @@ struct XView {  // one column of prepared x (global, or this CTA's shared copy)
   const uint8_t* q1;
   const float* scale;  // negative: a wide block (its third digit is used)
   const float* sum16;
-  const uint8_t* q2;   // third digits
+  const uint8_t* q2;   // third digits (read by wide_pass only)
 };
 __device__ __forceinline__ XView xview(const uint8_t* ws, int cols) {
   XView v;
@@ -103,12 +105,6 @@ __device__ __forceinline__ XView xview(const uint8_t* ws, int cols) {
   return v;
 }
 constexpr float kInv254 = 1.0f / 254.0f;
-__device__ __forceinline__ bool is_wide(float scale) { return __float_as_uint(scale) >> 31; }
-// 8 words of third digits at p (16-byte aligned)
-__device__ __forceinline__ void x2_words(const uint8_t* p, uint32_t (&w)[8]) {
-  const uint4 lo = *reinterpret_cast<const uint4*>(p), hi = *reinterpret_cast<const uint4*>(p + 16);
-  w[0] = lo.x; w[1] = lo.y; w[2] = lo.z; w[3] = lo.w; w[4] = hi.x; w[5] = hi.y; w[6] = hi.z; w[7] = hi.w;
-}
 
 struct Dig16 { uint4 a, b; };  // 16 digits of each plane
 __device__ __forceinline__ Dig16 dig16(const XView& x, int c) {
@@ -175,15 +171,15 @@ __device__ __forceinline__ float reduce_rows(const float (&acc)[M], int lane) {
 }
 
 // ---- per-type unit decoders ------------------------------------------------------
-// A unit is 32 (or 64) values of one block.  XU: the x data of one unit, held
-// in registers for the whole kernel.  dot(blk, j, XU): the unit's contribution
-// to one row from the two leading digits; blk is the shared address of the
-// unit's block, j the unit's index inside it.  wide(blk, j, XU, q2f, boff):
-// the third digits' contribution of the unit's wide blocks, taken only where
-// has_wide(XU); it reads everything it needs from shared memory again, so the
-// common path keeps its registers.  q2f() returns the third-digit plane and
-// boff is the block's byte offset in its row (which locates the unit's columns).
+// A unit is 32 (or 64) values of one block.  XU: the x data of one unit (the
+// two leading digits and the block scales, as magnitudes), held in registers
+// for the whole kernel.  dot(blk, j, XU): the unit's contribution to one row;
+// blk is the shared address of the unit's block, j the unit's index inside it.
+// The third digits of wide blocks are added after the rows (wide_pass).
 
+// Q4_K / Q5_K (native.c:173-197, 410-437).  Unit j = qs bytes 16j..16j+15:
+// low nibbles are values 64p+16h+i (sub-block 2p), high nibbles values
+// 64p+32+16h+i (sub-block 2p+1), p = j/2, h = j%2.  16-byte aligned blocks.
 // 32-value digit words (8 per plane) starting at column c.
 struct Dig32 { uint32_t a[8], b[8]; };
 __device__ __forceinline__ void dig32(const XView& x, int c, Dig32& d) {
@@ -211,22 +207,6 @@ __device__ __forceinline__ int dot32(const uint32_t (&c)[8], const Dig32& d) {
   }
   return (a0 + a1) * 254 + (b0 + b1);
 }
-// dot(codes, x2) over 32 values with the third digits at p (16-byte aligned)
-template <bool U>
-__device__ __forceinline__ int dot32_x2(const uint32_t (&c)[8], const uint8_t* p) {
-  uint32_t w[8];
-  x2_words(p, w);
-  int a0 = 0, a1 = 0;
-#pragma unroll
-  for (int k = 0; k < 8; k += 2) {
-    if constexpr (U) {
-      a0 = dp4a_us(c[k], w[k], a0); a1 = dp4a_us(c[k + 1], w[k + 1], a1);
-    } else {
-      a0 = __dp4a((int)c[k], (int)w[k], a0); a1 = __dp4a((int)c[k + 1], (int)w[k + 1], a1);
-    }
-  }
-  return a0 + a1;
-}
 
 // Q4_K / Q5_K (native.c:173-197, 410-437).  A unit is 64 values: pair p of
 // sub-blocks = qs bytes 32p..32p+31, whose low nibbles are values 64p+i
@@ -236,22 +216,24 @@ __device__ __forceinline__ int dot32_x2(const uint32_t (&c)[8], const uint8_t* p
 // values.  16-byte aligned blocks.
 template <int TY> struct UnitK45 {
   static constexpr int UPB = 4, VALS = 64;
-  struct XU { Dig32 a, b; float sa, sb, ma, mb; };  // sa, sb < 0: a wide block
-  __device__ static void load_x(const XView& x, int unit, XU& u, int) {
+  struct XU { Dig32 a, b; float sa, sb, ma, mb; };
+  __device__ static void load_x(const XView& x, int unit, XU& u, int, bool& wide) {
     const int ca = 256 * (unit >> 2) + 64 * (unit & 3), cb = ca + 32;
     dig32(x, ca, u.a);
     dig32(x, cb, u.b);
-    u.sa = *(x.scale + (ca >> 5));
+    const float sa = *(x.scale + (ca >> 5)), sb = *(x.scale + (cb >> 5));
+    wide |= (sa < 0.f) | (sb < 0.f);
+    u.sa = fabsf(sa);
     // Q4_K multiplies the high nibbles in place (16 * code): fold the 1/16 here
-    u.sb = *(x.scale + (cb >> 5)) * (TY == Q4_K ? 0.0625f : 1.0f);
+    u.sb = fabsf(sb) * (TY == Q4_K ? 0.0625f : 1.0f);
     u.ma = *(x.sum16 + (ca >> 4)) + *(x.sum16 + (ca >> 4) + 1);
     u.mb = *(x.sum16 + (cb >> 4)) + *(x.sum16 + (cb >> 4) + 1);
   }
-  __device__ static bool has_wide(const XU& u) { return is_wide(u.sa) || is_wide(u.sb); }
-  // code words of pair p: lo = sub-block 2p, hi = sub-block 2p+1 (Q4_K: 16 * code)
-  __device__ static void codes(uint32_t blk, int p, uint32_t (&lo)[8], uint32_t (&hi)[8]) {
+  __device__ static float dot(uint32_t blk, int p, const XU& u, int) {
+    const uint4 hdr = lds128(blk);
     const uint32_t qa = blk + (TY == Q4_K ? 16 : 48) + 32 * p;
     const uint4 q0 = lds128(qa), q1 = lds128(qa + 16);
+    uint32_t lo[8], hi[8];
     if constexpr (TY == Q5_K) {
       const uint4 h0 = lds128(blk + 16), h1 = lds128(blk + 32);
 #pragma unroll
@@ -268,45 +250,20 @@ template <int TY> struct UnitK45 {
         hi[k] = q & 0xF0F0F0F0u;  // 16 * code, read unsigned
       }
     }
-  }
-  // d * sc and the (scale, min) pairs 2p and 2p+1 (native.c:52-60): for j < 4
-  // bytes j, j+4; for j >= 4 the low 4 bits in byte j+4 and the top 2 in bytes
-  // j-4 / j.  All eight of each, four per word, without branches (the four
-  // lanes of a super-block take different p); a byte permute picks the pair.
-  __device__ static void scales(const uint4& hdr, int p, uint32_t& sca, uint32_t& scb, uint32_t& mna,
-                                uint32_t& mnb) {
+    const int ia = dot32<false>(lo, u.a), ib = dot32<TY == Q4_K>(hi, u.b);
+    // (scale, min) pairs 2p and 2p+1 (native.c:52-60): for j < 4 bytes j, j+4;
+    // for j >= 4 the low 4 bits in byte j+4 and the top 2 in bytes j-4 / j.
+    // All eight of each, four per word, without branches (the four lanes of
+    // a super-block take different p); a byte permute picks the lane's pair.
     const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu, mn_lo = hdr.z & 0x3F3F3F3Fu;
     const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
     const uint32_t mn_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
     const uint32_t sel = (uint32_t)(34 * p + 16);  // bytes 2p, 2p + 1 of (lo, hi)
     const uint32_t scp = __byte_perm(sc_lo, sc_hi, sel), mnp = __byte_perm(mn_lo, mn_hi, sel);
-    sca = scp & 0xffu;
-    scb = (scp >> 8) & 0xffu;
-    mna = mnp & 0xffu;
-    mnb = (mnp >> 8) & 0xffu;
-  }
-  __device__ static float dot(uint32_t blk, int p, const XU& u) {
-    const uint4 hdr = lds128(blk);
-    uint32_t lo[8], hi[8];
-    codes(blk, p, lo, hi);
-    const int ia = dot32<false>(lo, u.a), ib = dot32<TY == Q4_K>(hi, u.b);
-    uint32_t sca, scb, mna, mnb;
-    scales(hdr, p, sca, scb, mna, mnb);
+    const uint32_t sca = scp & 0xffu, scb = (scp >> 8) & 0xffu, mna = mnp & 0xffu, mnb = (mnp >> 8) & 0xffu;
     const float d = half_f(hdr.x & 0xffff), dmin = half_f(hdr.x >> 16);
-    return d * ((float)sca * fabsf(u.sa) * (float)ia + (float)scb * fabsf(u.sb) * (float)ib) -
+    return d * ((float)sca * u.sa * (float)ia + (float)scb * u.sb * (float)ib) -
            dmin * ((float)mna * u.ma + (float)mnb * u.mb);
-  }
-  template <class Q2>
-  __device__ static float wide(uint32_t blk, int p, const XU& u, const Q2& q2f, int boff) {
-    const uint4 hdr = lds128(blk);
-    uint32_t lo[8], hi[8];
-    codes(blk, p, lo, hi);
-    const uint8_t* x2 = q2f() + 256 * (boff / Geo<TY>::bpb) + 64 * p;
-    const float ea = is_wide(u.sa) ? (float)dot32_x2<false>(lo, x2) : 0.f;
-    const float eb = is_wide(u.sb) ? (float)dot32_x2<TY == Q4_K>(hi, x2 + 32) : 0.f;
-    uint32_t sca, scb, mna, mnb;
-    scales(hdr, p, sca, scb, mna, mnb);
-    return half_f(hdr.x & 0xffff) * kInv254 * ((float)sca * fabsf(u.sa) * ea + (float)scb * fabsf(u.sb) * eb);
   }
 };
 
@@ -333,8 +290,8 @@ __device__ __forceinline__ void words8(const Dig16& lo, const Dig16& hi, bool pl
 // shifted to match, the 9 aligned words feed dp4a directly.
 struct UnitQ80 {
   static constexpr int UPB = 1, VALS = 32;
-  struct XU { uint32_t a[9], b[9]; float s; };  // s < 0: a wide block
-  __device__ static void load_x(const XView& x, int unit, XU& u, int wmod4) {
+  struct XU { uint32_t a[9], b[9]; float s; };
+  __device__ static void load_x(const XView& x, int unit, XU& u, int wmod4, bool& wide) {
     const int mis = (wmod4 + 34 * unit + 2) & 3;  // offset of qs past a word boundary
     const Dig16 lo = dig16(x, 32 * unit), hi = dig16(x, 32 * unit + 16);
     uint32_t w[8];
@@ -342,10 +299,11 @@ struct UnitQ80 {
     shift_digits(w, mis, u.a);
     words8(lo, hi, true, w);
     shift_digits(w, mis, u.b);
-    u.s = *(x.scale + unit);
+    const float s = *(x.scale + unit);
+    wide |= s < 0.f;
+    u.s = fabsf(s);
   }
-  __device__ static bool has_wide(const XU& u) { return is_wide(u.s); }
-  __device__ static float dot(uint32_t blk, int, const XU& u) {
+  __device__ static float dot(uint32_t blk, int, const XU& u, int) {
     const uint32_t base = (blk + 2) & ~3u;
     int a0 = 0, a1 = 0, b0 = 0, b1 = 0;
 #pragma unroll
@@ -360,19 +318,7 @@ struct UnitQ80 {
       }
     }
     const float d = half_f(lds16(blk));
-    return d * fabsf(u.s) * (float)((a0 + a1) * 254 + (b0 + b1));
-  }
-  template <class Q2>
-  __device__ static float wide(uint32_t blk, int, const XU& u, const Q2& q2f, int boff) {
-    if (!is_wide(u.s)) return 0.f;
-    const uint32_t base = (blk + 2) & ~3u;
-    uint32_t w[8], sw[9];
-    x2_words(q2f() + 32 * (boff / 34), w);
-    shift_digits(w, (int)((blk + 2) & 3u), sw);  // shared and global addresses agree mod 16
-    int e = 0;
-#pragma unroll
-    for (int k = 0; k < 9; ++k) e = __dp4a((int)lds32(base + 4 * k), (int)sw[k], e);
-    return half_f(lds16(blk)) * fabsf(u.s) * kInv254 * (float)e;
+    return d * u.s * (float)((a0 + a1) * 254 + (b0 + b1));
   }
 };
 
@@ -395,63 +341,55 @@ template <bool REALIGN>
 struct UnitQ6K {
   static constexpr int UPB = 4, VALS = 64;
   // [part][group g: l<16 -> words 0..4, l>=16 -> words 4..8] x 5 words, per plane;
-  // mis: the block alignment (0 or 2) the digits are shifted for; s[p] < 0:
-  // part p is a wide block
+  // mis: the block alignment (0 or 2) the digits are shifted for
   struct XU { uint32_t a[2][10], b[2][10]; float s[2], m[2][2]; int mis; };
-  // the 9 digit words of a 32-value run shifted to alignment mis, split at l = 16
-  __device__ static void split_words(const uint32_t (&w)[8], int mis, uint32_t (&dst)[10]) {
-    uint32_t sw[9];
-    shift_digits(w, mis, sw);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) dst[k] = sw[k];
-    dst[4] = sw[4] & (mis ? 0x0000FFFFu : 0u);
-    dst[5] = sw[4] & (mis ? 0xFFFF0000u : 0xFFFFFFFFu);
-#pragma unroll
-    for (int k = 5; k < 9; ++k) dst[k + 1] = sw[k];
-  }
-  __device__ static void load_x(const XView& x, int unit, XU& u, int wmod4) {
+  __device__ static void load_x(const XView& x, int unit, XU& u, int wmod4, bool& wide) {
     const int blk = unit >> 2, j = unit & 3, h = j >> 1, tt = j & 1;
     const int mis = (wmod4 + 210 * blk) & 3;  // 0 or 2 (in row 0)
     u.mis = mis;
+    const uint32_t m4g0 = mis ? 0x0000FFFFu : 0u, m4g1 = mis ? 0xFFFF0000u : 0xFFFFFFFFu;
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
       const int c = 256 * blk + 128 * h + 64 * p + 32 * tt;
       const Dig16 lo = dig16(x, c), hi = dig16(x, c + 16);
-      uint32_t w[8];
+      uint32_t w[8], sw[9];
 #pragma unroll
       for (int plane = 0; plane < 2; ++plane) {
         words8(lo, hi, plane == 1, w);
-        split_words(w, mis, plane ? u.b[p] : u.a[p]);
+        shift_digits(w, mis, sw);
+        uint32_t* dst = plane ? u.b[p] : u.a[p];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k] = sw[k];
+        dst[4] = sw[4] & m4g0;
+        dst[5] = sw[4] & m4g1;
+#pragma unroll
+        for (int k = 5; k < 9; ++k) dst[k + 1] = sw[k];
       }
-      u.s[p] = *(x.scale + (c >> 5));
+      const float s = *(x.scale + (c >> 5));
+      wide |= s < 0.f;
+      u.s[p] = fabsf(s);
       u.m[p][0] = *(x.sum16 + (c >> 4));
       u.m[p][1] = *(x.sum16 + (c >> 4) + 1);
     }
   }
-  __device__ static bool has_wide(const XU& u) { return is_wide(u.s[0]) || is_wide(u.s[1]); }
-  // Code words k of both parts, aligned like the digits: call with k = 0..8 in
-  // order (REALIGN carries the previous word).
-  struct Reader {
-    uint32_t aql, aqh, sh = 0, pq = 0, ph = 0;
-    int tt;
-    __device__ Reader(uint32_t blk, int j, int mis) {
-      const int h = j >> 1;
-      tt = j & 1;
-      aql = (blk + 64 * h + 32 * tt) & ~3u;
-      aqh = (blk + 128 + 32 * h) & ~3u;
-      if constexpr (REALIGN) {
-        const bool flip = (int)(blk & 3u) != mis;
-        sh = flip ? 16u : 0u;
-        if (flip && mis == 2) {  // weights 2 bytes before the digits' positions
-          aql -= 4;
-          aqh -= 4;
-        } else {
-          pq = lds32(aql);
-          ph = lds32(aqh);
-        }
+  __device__ static float dot(uint32_t blk, int j, const XU& u, int) {
+    const int h = j >> 1, tt = j & 1;
+    uint32_t aql = (blk + 64 * h + 32 * tt) & ~3u, aqh = (blk + 128 + 32 * h) & ~3u;
+    uint32_t sh = 0, pq = 0, ph = 0;  // realignment: shift and the word before word k
+    if constexpr (REALIGN) {
+      const bool flip = (int)(blk & 3u) != u.mis;
+      sh = flip ? 16u : 0u;
+      if (flip && u.mis == 2) {  // weights 2 bytes before the digits' positions
+        aql -= 4;
+        aqh -= 4;
+      } else {
+        pq = lds32(aql);
+        ph = lds32(aqh);
       }
     }
-    __device__ void next(int k, uint32_t& c0, uint32_t& c1) {
+    int acc[2][2][2] = {};  // [part][group][plane]
+#pragma unroll
+    for (int k = 0; k < 9; ++k) {
       uint32_t ql, s;
       if constexpr (REALIGN) {
         const uint32_t nq = lds32(aql + 4 * k + 4), nh = lds32(aqh + 4 * k + 4);
@@ -463,18 +401,8 @@ struct UnitQ6K {
         ql = lds32(aql + 4 * k);
         s = lds32(aqh + 4 * k) >> (2 * tt);
       }
-      c0 = (ql & 0x0F0F0F0Fu) | ((s & 0x03030303u) << 4);
-      c1 = ((ql >> 4) & 0x0F0F0F0Fu) | (s & 0x30303030u);
-    }
-  };
-  __device__ static float dot(uint32_t blk, int j, const XU& u) {
-    const int h = j >> 1, tt = j & 1;
-    Reader rd(blk, j, u.mis);
-    int acc[2][2][2] = {};  // [part][group][plane]
-#pragma unroll
-    for (int k = 0; k < 9; ++k) {
-      uint32_t c0, c1;
-      rd.next(k, c0, c1);
+      const uint32_t c0 = (ql & 0x0F0F0F0Fu) | ((s & 0x03030303u) << 4);
+      const uint32_t c1 = ((ql >> 4) & 0x0F0F0F0Fu) | (s & 0x30303030u);
       if (k <= 4) {
         acc[0][0][0] = __dp4a((int)c0, (int)u.a[0][k], acc[0][0][0]);
         acc[0][0][1] = __dp4a((int)c0, (int)u.b[0][k], acc[0][0][1]);
@@ -496,51 +424,10 @@ struct UnitQ6K {
       for (int g = 0; g < 2; ++g) {
         const int sc = (int)(int8_t)(((p ? sc23 : sc01) >> (8 * g)) & 0xff);
         // codes are 0..63 and value = d * sc * (code - 32)
-        const float q = fabsf(u.s[p]) * (float)(acc[p][g][0] * 254 + acc[p][g][1]) - 32.0f * u.m[p][g];
+        const float q = u.s[p] * (float)(acc[p][g][0] * 254 + acc[p][g][1]) - 32.0f * u.m[p][g];
         r = fmaf((float)sc, q, r);
       }
     return half_f(lds16(blk + 208)) * r;
-  }
-  template <class Q2>
-  __device__ static float wide(uint32_t blk, int j, const XU& u, const Q2& q2f, int boff) {
-    const int h = j >> 1, tt = j & 1;
-    const uint8_t* x2 = q2f() + 256 * (boff / 210) + 128 * h + 32 * tt;  // part p at + 64 p
-    uint32_t d[2][10];
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      uint32_t w[8];
-      x2_words(x2 + 64 * p, w);
-      if (!is_wide(u.s[p])) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) w[k] = 0u;
-      }
-      split_words(w, u.mis, d[p]);
-    }
-    Reader rd(blk, j, u.mis);
-    int e[2][2] = {};
-#pragma unroll
-    for (int k = 0; k < 9; ++k) {
-      uint32_t c0, c1;
-      rd.next(k, c0, c1);
-      if (k <= 4) {
-        e[0][0] = __dp4a((int)c0, (int)d[0][k], e[0][0]);
-        e[1][0] = __dp4a((int)c1, (int)d[1][k], e[1][0]);
-      }
-      if (k >= 4) {
-        e[0][1] = __dp4a((int)c0, (int)d[0][k + 1], e[0][1]);
-        e[1][1] = __dp4a((int)c1, (int)d[1][k + 1], e[1][1]);
-      }
-    }
-    const uint32_t sc01 = lds16(blk + 192 + 8 * h + 2 * tt), sc23 = lds16(blk + 196 + 8 * h + 2 * tt);
-    float r = 0.f;
-#pragma unroll
-    for (int p = 0; p < 2; ++p)
-#pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        const int sc = (int)(int8_t)(((p ? sc23 : sc01) >> (8 * g)) & 0xff);
-        r = fmaf((float)sc * fabsf(u.s[p]), (float)e[p][g], r);
-      }
-    return half_f(lds16(blk + 208)) * kInv254 * r;
   }
 };
 
@@ -551,47 +438,35 @@ struct UnitQ6K {
 // way once, when they are loaded.  8-byte aligned blocks.
 struct UnitIQ4XS {
   static constexpr int UPB = 8, VALS = 32;
-  struct XU { uint32_t a[8], b[8]; float s; };  // s < 0: a wide block
-  // 16 digits from each half of a 32-value run, interleaved as the book's bytes come out
-  __device__ static void interleave(const uint4& lo, const uint4& hi, uint32_t (&o)[8]) {
+  struct XU { uint32_t a[8], b[8]; float s; };
+  __device__ static void load_x(const XView& x, int unit, XU& u, int, bool& wide) {
+    const Dig16 lo = dig16(x, 32 * unit), hi = dig16(x, 32 * unit + 16);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      o[2 * k] = __byte_perm(w4(lo, k), w4(hi, k), 0x5140);
-      o[2 * k + 1] = __byte_perm(w4(lo, k), w4(hi, k), 0x7362);
+      u.a[2 * k] = __byte_perm(w4(lo.a, k), w4(hi.a, k), 0x5140);
+      u.a[2 * k + 1] = __byte_perm(w4(lo.a, k), w4(hi.a, k), 0x7362);
+      u.b[2 * k] = __byte_perm(w4(lo.b, k), w4(hi.b, k), 0x5140);
+      u.b[2 * k + 1] = __byte_perm(w4(lo.b, k), w4(hi.b, k), 0x7362);
     }
+    const float s = *(x.scale + unit);
+    wide |= s < 0.f;
+    u.s = fabsf(s);
   }
-  __device__ static void load_x(const XView& x, int unit, XU& u, int) {
-    const Dig16 lo = dig16(x, 32 * unit), hi = dig16(x, 32 * unit + 16);
-    interleave(lo.a, hi.a, u.a);
-    interleave(lo.b, hi.b, u.b);
-    u.s = *(x.scale + unit);
-  }
-  __device__ static bool has_wide(const XU& u) { return is_wide(u.s); }
-  // book values of the 8 codes in word q: v0 = codes of bytes 0-1, v1 = bytes 2-3
-  __device__ static void book(uint32_t q, uint32_t& v0, uint32_t& v1) {
-    // the book as int8: -127 -104 -83 -65 -49 -35 -22 -10 | 1 13 25 38 53 69 89 113
-    const uint32_t T0 = 0xBFAD9881u, T1 = 0xF6EADDCFu, T2 = 0x26190D01u, T3 = 0x71594535u;
-    // the selectors of all 8 nibbles at once (prmt reads the low 16 bits):
-    // bits 0-2 index a half of the book, bit 3 picks the half
-    const uint32_t sel = q & 0x77777777u, pick = ((q >> 1) & 0x44444444u) | 0x32103210u;
-    v0 = __byte_perm(__byte_perm(T0, T1, sel), __byte_perm(T2, T3, sel), pick);
-    const uint32_t sel1 = sel >> 16, pick1 = pick >> 16;
-    v1 = __byte_perm(__byte_perm(T0, T1, sel1), __byte_perm(T2, T3, sel1), pick1);
-  }
-  __device__ static float block_scale(uint32_t blk, int j) {
+  __device__ static float dot(uint32_t blk, int j, const XU& u, int) {
     const uint2 hdr = lds64(blk);  // d | scales_h | scales_l[4]
-    const uint32_t sh = hdr.x >> 16;
-    const int ls = ((hdr.y >> (4 * j)) & 15) | (int)(((sh >> (2 * j)) & 3u) << 4);
-    return half_f(hdr.x & 0xffff) * (float)(ls - 32);
-  }
-  __device__ static float dot(uint32_t blk, int j, const XU& u) {
     const uint2 q01 = lds64(blk + 8 + 16 * j), q23 = lds64(blk + 16 + 16 * j);
     const uint32_t qw[4] = {q01.x, q01.y, q23.x, q23.y};
+    // the book as int8: -127 -104 -83 -65 -49 -35 -22 -10 | 1 13 25 38 53 69 89 113
+    const uint32_t T0 = 0xBFAD9881u, T1 = 0xF6EADDCFu, T2 = 0x26190D01u, T3 = 0x71594535u;
     int a = 0, b = 0, a1 = 0, b1 = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      uint32_t v0, v1;
-      book(qw[k], v0, v1);
+      // the selectors of all 8 nibbles at once (prmt reads the low 16 bits):
+      // bits 0-2 index a half of the book, bit 3 picks the half
+      const uint32_t sel = qw[k] & 0x77777777u, pick = ((qw[k] >> 1) & 0x44444444u) | 0x32103210u;
+      const uint32_t v0 = __byte_perm(__byte_perm(T0, T1, sel), __byte_perm(T2, T3, sel), pick);
+      const uint32_t sel1 = sel >> 16, pick1 = pick >> 16;
+      const uint32_t v1 = __byte_perm(__byte_perm(T0, T1, sel1), __byte_perm(T2, T3, sel1), pick1);
       a = __dp4a((int)v0, (int)u.a[2 * k], a);
       b = __dp4a((int)v0, (int)u.b[2 * k], b);
       a1 = __dp4a((int)v1, (int)u.a[2 * k + 1], a1);
@@ -599,27 +474,12 @@ struct UnitIQ4XS {
     }
     a += a1;
     b += b1;
-    return block_scale(blk, j) * fabsf(u.s) * (float)(a * 254 + b);
-  }
-  template <class Q2>
-  __device__ static float wide(uint32_t blk, int j, const XU& u, const Q2& q2f, int boff) {
-    if (!is_wide(u.s)) return 0.f;
-    const uint8_t* x2 = q2f() + 256 * (boff / 136) + 32 * j;
-    uint32_t d[8];
-    interleave(*reinterpret_cast<const uint4*>(x2), *reinterpret_cast<const uint4*>(x2 + 16), d);
-    const uint2 q01 = lds64(blk + 8 + 16 * j), q23 = lds64(blk + 16 + 16 * j);
-    const uint32_t qw[4] = {q01.x, q01.y, q23.x, q23.y};
-    int e = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      uint32_t v0, v1;
-      book(qw[k], v0, v1);
-      e = __dp4a((int)v0, (int)d[2 * k], e);
-      e = __dp4a((int)v1, (int)d[2 * k + 1], e);
-    }
-    return block_scale(blk, j) * fabsf(u.s) * kInv254 * (float)e;
+    const uint32_t sh = hdr.x >> 16;
+    const int ls = ((hdr.y >> (4 * j)) & 15) | (int)(((sh >> (2 * j)) & 3u) << 4);
+    return half_f(hdr.x & 0xffff) * (float)(ls - 32) * u.s * (float)(a * 254 + b);
   }
 };
+
 
 template <int TY> struct UnitOf;
 template <> struct UnitOf<Q4_K> { using T = UnitK45<Q4_K>; };
@@ -726,6 +586,87 @@ struct TileArgs {
 // CTAs per SM each format's register budget allows (launch bounds).
 template <int TY> constexpr int tile_min_blocks() { return (TY == Q6_K || TY == kQ6KRealign) ? 2 : 3; }
 
+// The part of 32 weights (unit u of block b) that the streaming loop multiplies
+// by the encoded x: d*sc*q, without the offsets it applies to the exact fp32
+// sums of x (Q4_K / Q5_K: dmin*m, native.c:173-197 and 410-437; Q6_K: the
+// -32 of d*sc*(q - 32), native.c:199-225).  Q8_0 and IQ4_XS have no offset.
+template <int TY>
+__device__ __forceinline__ void code_part(const uint8_t* b, int u, float (&v)[32]) {
+  if constexpr (TY == Q4_K || TY == Q5_K) {
+    int sc, mn;
+    k4_scale_min(b + 4, u, sc, mn);
+    const float d1 = half_val<float>(ld_u16(b)) * (float)sc;
+    const uint8_t* qs = b + (TY == Q4_K ? 16 : 48) + 32 * (u >> 1);
+#pragma unroll
+    for (int l = 0; l < 32; ++l) {
+      int q = (u & 1) ? (qs[l] >> 4) : (qs[l] & 15);
+      if constexpr (TY == Q5_K) q += ((b[16 + l] >> u) & 1) ? 16 : 0;
+      v[l] = d1 * (float)q;
+    }
+  } else if constexpr (TY == Q6_K) {
+    const float d = half_val<float>(ld_u16(b + 208));
+    const int h = u >> 2, t = u & 3;
+#pragma unroll
+    for (int l = 0; l < 32; ++l) {
+      const unsigned lq = b[64 * h + 32 * (t & 1) + l];
+      const int low = (t >= 2) ? (int)(lq >> 4) : (int)(lq & 15);
+      const int high = (b[128 + 32 * h + l] >> (2 * t)) & 3;
+      v[l] = d * (float)(int8_t)b[192 + 8 * h + 2 * t + (l >> 4)] * (float)(low | (high << 4));
+    }
+  } else {
+    decode_unit<TY, float>(b, u, v);
+  }
+}
+
+// The third digits of the wide blocks of x (negative scales), for the rows a
+// CTA owns (stages cta, cta + ncta, ... of rps rows).  Warp 0 lists the wide
+// blocks in increasing order in `list` (shared memory: list[0] = count, then
+// the block indices); then a warp per row, its lanes over the listed blocks
+// in turn, each decoding the d*sc*q part of its 32 weights (code_part, fp32)
+// and dotting it with the block's third digits; a fixed-order warp sum, added
+// to y.  Runs after the rows are final, only when x has a wide block, so the
+// streaming loop keeps its registers and instruction mix.
+template <int TY>
+__device__ __forceinline__ void wide_pass(const uint8_t* wb, size_t row_bytes, int cols, const float* scale,
+                                          const uint8_t* q2, float* yb, int cta, int ncta, int rps, int rows, int my,
+                                          int* list) {
+  constexpr int DT = TY == kQ6KRealign ? (int)Q6_K : TY;  // the format the realigning kernel reads
+  constexpr int BS = Geo<DT>::bs, BPB = Geo<DT>::bpb, UPB = BS / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nblk = cols / 32;
+  if (warp == 0) {
+    int n = 0;
+    for (int b0 = 0; b0 < nblk; b0 += 32) {
+      const int b = b0 + lane;
+      const bool w = b < nblk && (__float_as_uint(scale[b]) >> 31);
+      const unsigned m = __ballot_sync(0xffffffffu, w);
+      if (w) list[1 + n + __popc(m & ((1u << lane) - 1u))] = b;
+      n += __popc(m);
+    }
+    if (lane == 0) list[0] = n;
+  }
+  __syncthreads();
+  const int n = list[0];
+  for (int idx = warp; idx < my * rps; idx += kWarps) {
+    const int row = (cta + (idx / rps) * ncta) * rps + idx % rps;
+    if (row >= rows) continue;  // warp-uniform
+    const uint8_t* rp = wb + (size_t)row * row_bytes;
+    float part = 0.f;
+    for (int j = lane; j < n; j += 32) {
+      const int b = list[1 + j];
+      float w[32];
+      code_part<DT>(rp + (size_t)(b / UPB) * BPB, b % UPB, w);
+      const int8_t* d2 = reinterpret_cast<const int8_t*>(q2 + 32 * b);
+      float t = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) t = fmaf(w[i], (float)d2[i], t);
+      part = fmaf(-scale[b], t, part);  // a negative scale: its magnitude is s_b / 254
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (lane == 0) yb[row] += part * kInv254;
+  }
+}
+
 template <int TY, int UL, int M>
 __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kernel(TileArgs a, int* status) {
   using U = typename UnitOf<TY>::T;
@@ -815,15 +756,9 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   }
   typename U::XU xu[UL];  // this lane's x, for the whole kernel
   const XView xv = xview(xws, a.cols);
-  // the third-digit plane, rebuilt from the kernel arguments where a wide block needs it
-  auto q2f = [&]() -> const uint8_t* {
-    if (a.xmode) return smem + a.xenc_off + x2_offset(a.cols);
-    const int g = a.experts ? (int)(blockIdx.x / (gridDim.x / a.n_sel)) % a.n_ids : 0;
-    return a.ws + (size_t)g * (size_t)a.ws_stride + x2_offset(a.cols);
-  };
+  bool lane_wide = false;  // a unit of this lane touches a wide block (every unit is some lane's)
 #pragma unroll
-  for (int k = 0; k < UL; ++k) U::load_x(xv, ls + k * lps < units ? ls + k * lps : 0, xu[k], wmod4);
-
+  for (int k = 0; k < UL; ++k) U::load_x(xv, ls + k * lps < units ? ls + k * lps : 0, xu[k], wmod4, lane_wide);
 
   float best_v = -FLT_MAX;  // POST_ARGMAX: this thread's best finalized row
   int best_i = 0x7fffffff;
@@ -842,21 +777,20 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   };
 
   int k = 0;
-  __shared__ int landed[2];  // thread 0's verdict on stage k, in slot k & 1
+  __shared__ int gave_up;
+  if (tid == 0) gave_up = 0;
+  __syncthreads();
   for (; k < my; ++k) {
-    // stage k landed?  One thread waits (bounded) and shares the verdict, so
-    // every thread leaves the loop at the same iteration; the barrier also
-    // retires iteration k-1, whose slot the refill below reuses
-    const uint32_t bar = smem_addr(&bars[k % S]), parity = (uint32_t)(k / S) & 1u;
-    if (tid == 0) landed[k & 1] = mbar_wait_bounded(bar, parity) ? 1 : 0;
+    // stage k landed; the barrier also retires iteration k-1, whose slot the
+    // refill below reuses.  A thread whose bounded wait gives up raises the
+    // shared flag before the barrier, so every thread leaves the loop at the
+    // same iteration.
+    if (!mbar_wait_bounded(smem_addr(&bars[k % S]), (uint32_t)(k / S) & 1u)) gave_up = 1;
     __syncthreads();
-    if (!landed[k & 1]) {
+    if (gave_up) {
       if (tid == 0) atomicOr(status, (int)kStatusWaitTimeout);
       break;
     }
-    // the phase is complete: each thread's own wait returns at once and orders
-    // its reads of the slot after the copy
-    (void)mbar_wait_bounded(bar, parity);
     if (k > 0) finalize(k - 1);
     if (tid == 0 && k + S - 1 < my) {
       fence_proxy_async();  // generic reads of the slot precede its async refill
@@ -875,12 +809,7 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
       const uint32_t rowa = base + (uint32_t)i * (uint32_t)a.row_bytes;
       float v = 0.f;
 #pragma unroll
-      for (int kk = 0; kk < UL; ++kk) {
-        const uint32_t blk = rowa + (uint32_t)uoff[kk];
-        float d = U::dot(blk, uj[kk], xu[kk]);
-        if (U::has_wide(xu[kk])) d += U::wide(blk, uj[kk], xu[kk], q2f, uoff[kk]);  // rare
-        v += uon[kk] * d;
-      }
+      for (int kk = 0; kk < UL; ++kk) v += uon[kk] * U::dot(rowa + (uint32_t)uoff[kk], uj[kk], xu[kk], lane);
       acc[i] = on * v;
     }
     float* r = red + (size_t)(k & 1) * kWarps * M;
@@ -892,6 +821,27 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   if (k < my && tid == 0) {
     // a copy timed out: wait (bounded) for every copy still in flight
     for (int t = k; t < min(my, k + S - 1); ++t) (void)mbar_wait_bounded(smem_addr(&bars[t % S]), (uint32_t)(t / S) & 1u);
+  }
+  // x holds a wide block (a negative scale): its third digits are added now
+  if (__syncthreads_or(lane_wide) && k == my) {
+    // add them to this CTA's rows, then take the argmax post op's candidate
+    // again from the corrected rows (the barrier above ordered finalize's writes)
+    // (the list of wide blocks goes to the stage ring: every copy has landed and been read)
+    // (x's encoding is located again from the arguments, so no pointer to it
+    // stays live through the streaming loop)
+    const uint8_t* xe = a.xmode ? smem + a.xenc_off
+                                : a.ws + (size_t)(a.experts ? sel % a.n_ids : 0) * (size_t)a.ws_stride;
+    wide_pass<TY>(wb, a.row_bytes, a.cols, reinterpret_cast<const float*>(xe + 2LL * a.cols), xe + x2_offset(a.cols),
+                  yb, cta, ncta, rows_per_stage, a.rows, my, reinterpret_cast<int*>(smem));
+    __syncthreads();
+    if (a.post.op == kPostArgmax) {
+      best_v = -FLT_MAX;
+      best_i = 0x7fffffff;
+      for (int kk = 0; kk < my; ++kk) {
+        const int st = cta + kk * ncta;
+        if (tid < stage_rows(st)) better(best_v, best_i, yb[(size_t)st * rows_per_stage + tid], st * rows_per_stage + tid);
+      }
+    }
   }
   if (a.post.op != kPostNone) run_post(a.post, a.y, a.rows, best_v, best_i);
 }

@@ -16,26 +16,29 @@ namespace pyr {
 // x0 = rint(t), x1 = rint((t - x0) * 254), x2 = rint(((t - x0) * 254 - x1) * 254)
 // (no clamps: |t| rounds to at most 127 and each remainder is at most 1/2).
 // scale[b] = amax / 127 / 254, stored NEGATIVE for a "wide" block: one in which
-// at least 4 nonzero values lie more than 2^8 below amax.  The kernels use the
-// third digit only for wide blocks: two digits bound each value's error by
-// amax / 64516, which for a block whose other values sit far below one
-// outlier (an outlier channel) is large next to those values; the third digit
-// brings the bound to amax / 16.4e6.  Near-Gaussian data is essentially never
-// wide (1e-4 of blocks), so the common path pays nothing for it.
+// at most 8 of the 32 values lie within a factor 32 of amax, i.e. one or a few
+// outliers (an outlier channel) over values far smaller.  Two digits bound
+// each value's error by amax / 64516, which is large next to those smaller
+// values; the kernels add the third digit for wide blocks, bringing the bound
+// to amax / 16.4e6.  Gaussian, Laplace and SiLU(gate) * up activations are
+// almost never wide (0 to ~4% of blocks), so the common path pays nothing.
 __host__ __device__ constexpr long long x2_offset(long long cols) { return 2 * cols + cols / 8 + cols / 4; }
 __host__ __device__ constexpr long long encoded_bytes(long long cols) { return x2_offset(cols) + cols; }
-constexpr int kWideCount = 4;         // nonzero values far below amax that make a block wide
-constexpr float kWideRatio = 256.0f;  // "far below": |v| * 256 < amax
+constexpr int kWideMaxBig = 8;      // a block is wide when at most this many values are "big":
+constexpr float kBigRatio = 32.0f;  // within this factor of the block's largest magnitude
 
 __device__ __forceinline__ float digit_ratio(float amax) { return amax > 0.0f ? 127.0f / amax : 0.0f; }
+// Every step rounded on its own (no fused multiply-add), so every encoder
+// writes the same digits for the same value whatever the compiler contracts.
 __device__ __forceinline__ void three_digits(float v, float r, int& d0, int& d1, int& d2) {
-  const float t = v * r;
+  const float t = __fmul_rn(v, r);
   d0 = __float2int_rn(t);
-  const float u = (t - (float)d0) * 254.0f;
+  const float u = __fmul_rn(__fsub_rn(t, (float)d0), 254.0f);
   d1 = __float2int_rn(u);
-  d2 = __float2int_rn((u - (float)d1) * 254.0f);
+  d2 = __float2int_rn(__fmul_rn(__fsub_rn(u, (float)d1), 254.0f));
 }
-__device__ __forceinline__ bool far_below(float v, float amax) { return v != 0.0f && fabsf(v) * kWideRatio < amax; }
+__device__ __forceinline__ bool is_big(float v, float amax) { return fabsf(v) * kBigRatio >= amax; }
+__device__ __forceinline__ bool wide_block(int n_big, float amax) { return amax > 0.0f && n_big <= kWideMaxBig; }
 
 // Encode 32 values (lane l holds value l of block b) into the layout above.
 __device__ __forceinline__ void encode_block(float v, int lane, int b, int cols, uint8_t* ws) {
@@ -43,7 +46,7 @@ __device__ __forceinline__ void encode_block(float v, int lane, int b, int cols,
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   const float s = amax / 127.0f;
-  const bool wide = __popc(__ballot_sync(0xffffffffu, far_below(v, amax))) >= kWideCount;
+  const bool wide = wide_block(__popc(__ballot_sync(0xffffffffu, is_big(v, amax))), amax);
   int d0, d1, d2;
   three_digits(v, digit_ratio(amax), d0, d1, d2);
   float s16 = v;
@@ -127,10 +130,10 @@ __device__ __forceinline__ void encode_group(const float (&v)[16], int g, int co
   for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
   amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
   const float s = amax / 127.0f, r = digit_ratio(amax);
-  int nsmall = 0;
+  int nbig = 0;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) nsmall += far_below(v[i], amax) ? 1 : 0;
-  nsmall += __shfl_xor_sync(0xffffffffu, nsmall, 1);
+  for (int i = 0; i < 16; ++i) nbig += is_big(v[i], amax) ? 1 : 0;
+  nbig += __shfl_xor_sync(0xffffffffu, nbig, 1);
   uint32_t p0[4], p1[4], p2[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -157,7 +160,7 @@ __device__ __forceinline__ void encode_group(const float (&v)[16], int g, int co
   *reinterpret_cast<uint4*>(enc + cols + 16 * g) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
   *reinterpret_cast<uint4*>(enc + x2_offset(cols) + 16 * g) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
   float* scale = reinterpret_cast<float*>(enc + 2 * cols);
-  if ((g & 1) == 0) scale[g >> 1] = nsmall >= kWideCount ? -(s / 254.0f) : s / 254.0f;
+  if ((g & 1) == 0) scale[g >> 1] = wide_block(nbig, amax) ? -(s / 254.0f) : s / 254.0f;
   scale[cols / 32 + g] = s16;
   if (out) {
     float4* o = reinterpret_cast<float4*>(out + 16 * g);
