@@ -1,6 +1,6 @@
-"""Benchmark: fused GGML dequantize x matvec on B200.
+"""Benchmark: fused GGML dequantize x matvec on B200 (the kernel microbench).
 
-Workload (one "step"): the kernel microbench of BASELINE.json configs[1] at
+Workload (one "step"): the kernel microbench at
 batch 1 -- y = W x for W in {Q8_0, Q4_K, Q5_K, Q6_K, IQ4_XS} x {4096x4096,
 14336x4096, 4096x14336} (rows x cols), 15 matrices, quantized by the package's
 quantizers (byte-identical to the reference's fixture encoders; IQ4_XS by the

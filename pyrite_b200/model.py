@@ -1,6 +1,6 @@
 """Device-resident batch-1 decode of mixed-type checkpoints: dense
-``llama`` / ``qwen3`` models in a K-quant mix (the
-Llama-3-8B Q4_K_M model) and ``qwen3moe`` models with routed experts
+``llama`` / ``qwen3`` models in a K-quant mix (configs[2], the
+Llama-3-8B-shaped Q4_K_M model) and ``qwen3moe`` models with routed experts
 (configs[3] and [4]).
 
 The B200 counterpart of the reference's executors (``pyrite/dense.py:440-513``

@@ -1,4 +1,4 @@
-"""Seeded synthetic dense checkpoints (no public weights).
+"""Seeded synthetic checkpoints of the benchmarked model shapes (no public weights exist for them).
 
 ``dense_tensors(spec)`` yields every tensor of a dense ``qwen3`` / ``llama``
 GGUF checkpoint -- name, GGML dims, GGML type and payload bytes -- in the
@@ -52,12 +52,12 @@ class DenseSpec:
 
     @classmethod
     def c1(cls) -> "DenseSpec":
-        """BASELINE configs[0]: Qwen3-0.6B-shaped, all matrices Q8_0."""
+        """configs[0]: Qwen3-0.6B-shaped, all matrices Q8_0."""
         return cls()
 
     @classmethod
     def c3(cls) -> "DenseSpec":
-        """BASELINE configs[2]: Llama-3-8B-shaped, Q4_K_M mix."""
+        """configs[2]: Llama-3-8B-shaped, Q4_K_M mix."""
         return cls(architecture="llama", hidden_size=4096, num_hidden_layers=32, num_attention_heads=32,
                    num_key_value_heads=8, head_dim=128, intermediate_size=14336, vocab_size=128256,
                    rope_theta=500_000.0, rms_norm_eps=1e-5, qk_norm=False, tied_embeddings=False,
@@ -146,9 +146,9 @@ def layer_matrices(spec: DenseSpec) -> list[tuple[str, int, int]]:
 
 
 def dense_tensor_type(spec: DenseSpec, name: str) -> int:
-    """GGML type of a matrix: ``weight_type``, or for the Q4_K_M mix (as
-    BASELINE states it) Q6_K for attn_v, ffn_down of the even layers (half of
-    them) and the output projection, Q4_K for the rest."""
+    """GGML type of a matrix: ``weight_type``, or for the Q4_K_M mix Q6_K for
+    attn_v, ffn_down of the even layers (half of them) and the output
+    projection, Q4_K for the rest."""
     if spec.mix != "q4_k_m":
         return spec.weight_type
     if name == "output.weight" or name.endswith("attn_v.weight"):
@@ -182,14 +182,14 @@ def dense_tensors(spec: DenseSpec) -> Iterator[tuple[str, tuple[int, ...], int, 
 
 
 def prompt_ids(spec: DenseSpec, n: int = 16, seed: int = 7) -> list[int]:
-    """BASELINE's prompt: ``n`` seeded uniform token ids."""
+    """The benchmark prompt: ``n`` seeded uniform token ids."""
     return [int(v) for v in np.random.default_rng(seed).integers(0, spec.vocab_size, n)]
 
 
 # ---------------------------------------------------------------- MoE (qwen3moe)
 @dataclass(frozen=True)
 class MoESpec:
-    """A ``qwen3moe`` checkpoint: BASELINE configs[3] (Qwen3-30B-A3B-shaped)
+    """A ``qwen3moe`` checkpoint: configs[3] (Qwen3-30B-A3B-shaped)
     and smaller variants for parity runs."""
 
     architecture: str = "qwen3moe"
@@ -222,12 +222,12 @@ class MoESpec:
 
     @classmethod
     def c4(cls) -> "MoESpec":
-        """BASELINE configs[3]: Qwen3-30B-A3B-shaped, Q4_K_M mix."""
+        """configs[3]: Qwen3-30B-A3B-shaped, Q4_K_M mix."""
         return cls()
 
     @classmethod
     def c5(cls) -> "MoESpec":
-        """BASELINE configs[4]: Qwen3-235B-A22B-shaped, Q4_K_M mix (~142 GB)."""
+        """configs[4]: Qwen3-235B-A22B-shaped, Q4_K_M mix (~142 GB)."""
         return cls(hidden_size=4096, num_hidden_layers=94, num_attention_heads=64, num_key_value_heads=4,
                    intermediate_size=12288, moe_intermediate_size=1536, chunked_weights=True)
 
@@ -239,7 +239,7 @@ class MoESpec:
                    vocab_size=2048)
 
 
-#: Q4_K_M mix as BASELINE states it: Q4_K for most tensors, Q6_K for attn_v,
+#: The Q4_K_M mix: Q4_K for most tensors, Q6_K for attn_v,
 #: half of ffn_down (the even layers) and the output projection; the router
 #: (ffn_gate_inp) stays F32 as llama.cpp keeps it.
 Q4_K, Q6_K, F32 = 12, 14, 0

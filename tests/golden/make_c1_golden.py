@@ -1,4 +1,4 @@
-"""Golden greedy decode of BASELINE configs[0] by the reference executor.
+"""Golden greedy decode of configs[0] (Qwen3-0.6B-shaped, Q8_0) by the reference executor.
 
 Writes the seeded synthetic checkpoint (pyrite_b200.synthetic) as a real GGUF
 file with the reference's own writer (tests/gguf_builder.py), opens it with

@@ -1,7 +1,7 @@
 """Golden greedy decode of a synthetic Qwen3-MoE checkpoint by the reference.
 
 Writes the seeded checkpoint (pyrite_b200.synthetic.moe_tensors: the Q4_K_M
-mix BASELINE configs[3] states) as a real GGUF file with the reference's own
+mix of configs[3]) as a real GGUF file with the reference's own
 writer (tests/gguf_builder.py), opens it with the reference's
 ``open_executor`` (a ``Qwen3MoEExecutor``, native C kernels on) and records
 the greedy decode of a seeded prompt, the top logits of every forward pass

@@ -4,7 +4,7 @@
 (``tests/test_native_kernels.py:32-87``): pseudo-random bytes with every fp16
 scale / min word of each block overwritten by a finite half, so the payload
 exercises every code path of the decoders without NaN scales.  It is
-vectorised with numpy so BASELINE-size matrices take milliseconds.
+vectorised with numpy so benchmark-size matrices take milliseconds.
 """
 from __future__ import annotations
 

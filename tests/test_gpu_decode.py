@@ -1,4 +1,4 @@
-"""Device-resident decode against the reference executor.
+"""Device-resident decode against the reference executor (configs[0], Qwen3-0.6B-shaped).
 
 tests/golden/c1_decode.json holds what the reference's DenseExecutor
 (pyrite.executor.open_executor, native kernels, fp64) produced on the seeded
@@ -6,7 +6,7 @@ synthetic Qwen3-0.6B-shaped Q8_0 checkpoint: the greedy continuation of a
 16-token prompt and the top-16 logits of each of its 24 forward passes
 (tests/golden/make_c1_golden.py).  The B200 decoder rebuilds the same weights
 from the same seeds (pyrite_b200.synthetic) and must produce identical greedy
-token ids; its logits must match the reference's within 2e-3 absolute
+token ids; its logits must match the reference's within LOGIT_TOL absolute
 (the logits are O(1): fp32 residual stream and the encoded-activation matvec
 against the reference's fp64).  c1_small.json is a 2-layer, 4096-token
 variant that runs in seconds.

@@ -243,9 +243,9 @@ def test_moe_decode_matches_reference(cuda_device, golden):
     import torch
 
     from pyrite_b200.kernels import cuda as K
-    from pyrite_b200.moe import MoEDecoder
+    from pyrite_b200.model import MixedDecoder
     g = json.loads((GOLDEN / golden).read_text())
-    dec = MoEDecoder.synthetic(_moe_spec(g), device=cuda_device, max_ctx=128)
+    dec = MixedDecoder.synthetic(_moe_spec(g), device=cuda_device, max_ctx=128)
     prompt, want = g["prompt"], g["generated"]
     got = dec.generate(prompt, len(want))
     assert K.status() == 0
