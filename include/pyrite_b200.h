@@ -271,6 +271,20 @@ int pyrite_cuda_silu_mul_encode(const float *gate_up, size_t f, float *act, void
 int pyrite_cuda_argmax_step(const float *logits, size_t n, void *scratch, size_t scratch_len,
                             int *tokens, int *pos, int prompt_len, int max_ctx, void *stream);
 
+/* Greedy sampling over a vocabulary split across GPUs (each holds a contiguous
+ * slice of the LM head's rows): pyrite_cuda_argmax_local reduces this GPU's
+ * n logits to one 8-byte pair {float value, int32 id} with id = index_base +
+ * the first index of the slice's largest logit (scratch as for
+ * pyrite_cuda_argmax_step); after the pairs of all GPUs are exchanged (e.g.
+ * an all-gather of 8 bytes per GPU), pyrite_cuda_argmax_pick takes the
+ * largest value, the lowest id on ties -- sampler.py:12-15 over the whole
+ * vocabulary -- and writes it like pyrite_cuda_argmax_step.  pair / pairs
+ * 8-byte aligned device memory. */
+int pyrite_cuda_argmax_local(const float *logits, size_t n, long long index_base, void *scratch,
+                             size_t scratch_len, void *pair, void *stream);
+int pyrite_cuda_argmax_pick(const void *pairs, size_t n_pairs, int *tokens, int *pos, int prompt_len,
+                            int max_ctx, void *stream);
+
 /* ---- routed experts (Qwen3-MoE feed-forward, executor.py:672-683, 757-793) ---- */
 
 /* Router softmax (fp64) over n_experts logits, the top_k experts ordered by

@@ -383,6 +383,41 @@ __global__ void __launch_bounds__(32) argmax_final_kernel(const float* __restric
   pdl_launch_dependents();
 }
 
+// One (value, index) pair from the partials of argmax_partial_kernel: this
+// GPU's best logit of its vocabulary slice and its global id (base + index).
+__global__ void __launch_bounds__(32) argmax_pair_kernel(const float* __restrict__ pv, const int* __restrict__ pi,
+                                                         int parts, long long base, float* __restrict__ pair) {
+  pdl_wait();
+  float v = -FLT_MAX;
+  int idx = 0x7fffffff;
+  for (int k = threadIdx.x; k < parts; k += 32) better(v, idx, pv[k], pi[k]);
+  warp_best(v, idx);
+  if (threadIdx.x == 0) {
+    pair[0] = v;
+    reinterpret_cast<int*>(pair)[1] = (int)(base + idx);
+  }
+  pdl_launch_dependents();
+}
+
+// The greedy token from every GPU's pair (larger value first, then the lower
+// id: sampler.py:12-15 over the whole vocabulary), written like argmax_final.
+__global__ void __launch_bounds__(32) argmax_pick_kernel(const float* __restrict__ pairs, int n_pairs,
+                                                         int* __restrict__ tokens, int* __restrict__ pos, int prompt_len,
+                                                         int max_ctx) {
+  pdl_wait();
+  float v = -FLT_MAX;
+  int idx = 0x7fffffff;
+  for (int k = threadIdx.x; k < n_pairs; k += 32)
+    better(v, idx, pairs[2 * k], reinterpret_cast<const int*>(pairs)[2 * k + 1]);
+  warp_best(v, idx);
+  if (threadIdx.x == 0) {
+    const int p = *pos;
+    if (p + 1 < max_ctx && p + 1 >= prompt_len) tokens[p + 1] = idx;
+    *pos = p + 1;
+  }
+  pdl_launch_dependents();
+}
+
 int rc(int e) { return e > 0 ? PYRITE_E_CUDA : e; }
 
 }  // namespace
@@ -493,6 +528,28 @@ int pyrite_cuda_argmax_step(const float* logits, size_t n, void* scratch, size_t
   if (e) return rc(e);
   return rc(launch_pdl(argmax_final_kernel, dim3(1), dim3(32), 0, s, (const float*)pv, (const int*)pi, kParts, tokens,
                        pos, prompt_len, max_ctx));
+}
+
+int pyrite_cuda_argmax_local(const float* logits, size_t n, long long index_base, void* scratch, size_t scratch_len,
+                             void* pair, void* stream) {
+  constexpr int kParts = 148;
+  if (!logits || n == 0 || n > 0x7fffffffu || index_base < 0 || index_base + (long long)n > 0x7fffffffLL || !pair)
+    return PYRITE_E_SHAPE;
+  if (!scratch || scratch_len < kParts * 8 || ((uintptr_t)pair & 7)) return PYRITE_E_BUFFER;
+  float* pv = static_cast<float*>(scratch);
+  int* pi = reinterpret_cast<int*>(pv + kParts);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int e = launch_pdl(argmax_partial_kernel, dim3(kParts), dim3(1024), 0, s, logits, (int)n, pv, pi);
+  if (e) return rc(e);
+  return rc(launch_pdl(argmax_pair_kernel, dim3(1), dim3(32), 0, s, (const float*)pv, (const int*)pi, kParts,
+                       index_base, static_cast<float*>(pair)));
+}
+
+int pyrite_cuda_argmax_pick(const void* pairs, size_t n_pairs, int* tokens, int* pos, int prompt_len, int max_ctx,
+                            void* stream) {
+  if (!pairs || n_pairs == 0 || n_pairs > 4096 || ((uintptr_t)pairs & 7) || !tokens || !pos) return PYRITE_E_BUFFER;
+  return rc(launch_pdl(argmax_pick_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream),
+                       static_cast<const float*>(pairs), (int)n_pairs, tokens, pos, prompt_len, max_ctx));
 }
 
 }  // extern "C"

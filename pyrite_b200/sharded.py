@@ -13,8 +13,10 @@ per layer, both inside the step's CUDA graph:
 each one kernel (``pyrite_cuda_allreduce_sum``: every rank publishes its
 partial in a buffer the others map by CUDA IPC, raises a flag in every peer's
 buffer and sums all partials over NVLink in rank order; ``p2p=False`` uses
-NCCL instead), and one NCCL ``all_gather`` of the LM head's logits (rows sharded by vocabulary)
-before the greedy argmax, which every rank computes identically.  Norms, the
+NCCL instead), and for the greedy token one NCCL ``all_gather`` of 8 bytes per
+GPU: each rank's best (logit, id) over its slice of the vocabulary (the LM
+head's rows are sharded by vocabulary), from which every rank picks the same
+token (the largest logit, the lowest id on ties).  Norms, the
 embedding lookup and the router are replicated.  Sums across GPUs change the
 fp32 summation order only; greedy ids are checked against the reference's.
 """
@@ -138,7 +140,10 @@ class ShardedDecoder(MixedDecoder):
             self.gu, self.act = z(2 * ff), z(ff)
         self.ff = ff
         self.logits_local = z(v1 - v0)
-        self.logits = z(spec.vocab_size)
+        self.logits = z(spec.vocab_size)  # filled only with gather_logits (the greedy step exchanges pairs)
+        self.gather_logits = False
+        self.pair_local = torch.zeros(2, dtype=torch.int32, device=d)  # {float value, int32 id}
+        self.pairs = torch.zeros(2 * world, dtype=torch.int32, device=d)
         self.kcache = z(spec.num_hidden_layers, max_ctx, nkv_l)
         self.vcache = torch.zeros_like(self.kcache)
         self.tokens, self.pos = z(max_ctx, dt=torch.int32), z(1, dt=torch.int32)
@@ -272,7 +277,13 @@ class ShardedDecoder(MixedDecoder):
             self._allreduce_into_hidden(stream)
         self._norm(self.hidden, self.out_norm, self.normed, self.ws_h, stream)
         self._mv(self.lm_head, self.normed, self.ws_h, self.logits_local, 0, stream)
-        dist.all_gather_into_tensor(self.logits, self.logits_local, group=self.group)
-        _check(L.pyrite_cuda_argmax_step(self.logits.data_ptr(), s.vocab_size, self.argmax_scratch.data_ptr(),
-                                         self.argmax_scratch.numel(), self.tokens.data_ptr(), self.pos.data_ptr(),
-                                         self.prompt_len, self.max_ctx, stream), "argmax")
+        # greedy over the split vocabulary: this GPU's best (value, id) pair, an
+        # all-gather of 8 bytes per GPU, then the same pick on every rank
+        _check(L.pyrite_cuda_argmax_local(self.logits_local.data_ptr(), self.logits_local.numel(), self.vocab_rows[0],
+                                          self.argmax_scratch.data_ptr(), self.argmax_scratch.numel(),
+                                          self.pair_local.data_ptr(), stream), "argmax local")
+        dist.all_gather_into_tensor(self.pairs, self.pair_local, group=self.group)
+        _check(L.pyrite_cuda_argmax_pick(self.pairs.data_ptr(), self.world, self.tokens.data_ptr(),
+                                         self.pos.data_ptr(), self.prompt_len, self.max_ctx, stream), "argmax pick")
+        if self.gather_logits:  # the whole vocabulary's logits, for inspection only
+            dist.all_gather_into_tensor(self.logits, self.logits_local, group=self.group)

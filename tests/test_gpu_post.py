@@ -312,3 +312,39 @@ def test_matvec_transformed_rejects_bad_arguments(cuda_device):
     w2, _, _ = _setup(2, 64, 256, 1)
     assert lib.pyrite_cuda_matvec_transformed(2, w2.data_ptr(), w2.numel(), x.data_ptr(), 2, None, 1e-6, None, None,
                                               0, y.data_ptr(), 64, 256, 0, s) == -3
+
+
+@pytest.mark.parametrize("n_slices,vocab", [(2, 4096), (8, 151936), (4, 128256)])
+def test_argmax_pairs_over_a_split_vocabulary(cuda_device, n_slices, vocab):
+    """pyrite_cuda_argmax_local on each slice of a vocabulary (as each GPU of a
+    vocabulary-sharded LM head would), the pairs concatenated (the all-gather),
+    then pyrite_cuda_argmax_pick: the first index of the global maximum
+    (sampler.py:12-15), with the maximum planted in several slices so the
+    lowest id must win the tie."""
+    import torch
+
+    from pyrite_b200 import _lib
+    lib = _lib.require()
+    s = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator("cuda").manual_seed(vocab + n_slices)
+    logits = torch.randn(vocab, device="cuda", generator=g)
+    per = vocab // n_slices
+    top = float(logits.max()) + 1.0
+    planted = [per * k + 17 * k + 3 for k in range(1, n_slices)]  # in slices 1.. (not 0)
+    logits[planted] = top
+    pairs = torch.zeros(2 * n_slices, dtype=torch.int32, device="cuda")
+    scratch = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    for k in range(n_slices):
+        sl = logits[per * k: per * (k + 1)]
+        assert lib.pyrite_cuda_argmax_local(sl.data_ptr(), per, per * k, scratch.data_ptr(), scratch.numel(),
+                                            pairs[2 * k:].data_ptr(), s) == 0
+    tokens = torch.full((8,), -1, dtype=torch.int32, device="cuda")
+    pos = torch.tensor([3], dtype=torch.int32, device="cuda")
+    assert lib.pyrite_cuda_argmax_pick(pairs.data_ptr(), n_slices, tokens.data_ptr(), pos.data_ptr(), 0, 8, s) == 0
+    torch.cuda.synchronize()
+    assert int(tokens[4]) == min(planted) == int(torch.argmax(logits)) and int(pos) == 4
+    v = pairs.view(-1, 2)
+    for k in range(n_slices):  # each pair: the slice's maximum and its global id
+        sl = logits[per * k: per * (k + 1)]
+        assert int(v[k, 1]) == per * k + int(torch.argmax(sl))
+        assert float(v[k, 0:1].view(torch.float32)) == float(sl.max())
