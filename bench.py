@@ -261,6 +261,8 @@ def run_ours(args) -> None:
     ms_per_step = ms / args.steps
     value = world * step_bytes / (ms_per_step * 1e-3) / 1e9
 
+    strong = strong_leg(dev, W, X, Y, wl, stream, pg, world, rank, args.steps, args.warmup) if pg else None
+
     # ---- per-kernel live timing: each matrix alone, rotating over copies so every
     # launch reads cold HBM (copies total > 4 x L2), timed with events on its stream
     per_kernel = []
@@ -332,7 +334,9 @@ def run_ours(args) -> None:
     if not args.no_models:  # every rank takes part (tensor parallel when world > 1)
         models = {}
         for which in ("c3", "c4", "c5"):
+            parity = golden_parity(dev, which, world, rank, pg)
             models[which] = model_leg(dev, which, world, rank, pg)
+            models[which]["parity"] = parity
             torch.cuda.empty_cache()
 
     if rank == 0:
@@ -364,6 +368,7 @@ def run_ours(args) -> None:
                          "kernel": key, "algorithmic_bytes_per_launch": dom_bytes,
                          "traffic": ncu_traffic(key)},
             "whole_step_frac_of_peak": round(value / world / peak, 4),
+            "strong": strong,
             "kernels": per_kernel,
             "cpu_baseline": cpu,
             "e2e": e2e,
@@ -377,6 +382,63 @@ def run_ours(args) -> None:
     if pg:
         pg.barrier()
         pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------- strong-scaling leg (N > 1)
+def strong_leg(dev, W, X, Y, wl, stream, pg, world: int, rank: int, steps: int, warmup: int) -> dict:
+    """The same step with every matrix's rows split over the GPUs (rank k
+    multiplies rows [k r / N, (k + 1) r / N), the row range of the reference's
+    executor call, executor.py:481-509) and the full outputs assembled on every
+    GPU by an NCCL all_gather per matrix: total work fixed as N grows.  Time:
+    CUDA events around `steps` replays of one graph, max over ranks.  The
+    gathered rows must equal the one-GPU rows bit for bit (any row partition
+    gives the same bits)."""
+    import torch
+
+    from pyrite_b200.kernels import cuda as K
+    parts = {}
+    for _, t, r, c in wl:
+        rr, rb = r // world, row_bytes(t, c)
+        parts[(t, r, c)] = (W[(t, r, c)][rank * rr * rb:(rank + 1) * rr * rb], torch.empty(rr, device=dev),
+                            torch.empty(r, device=dev), rr)
+    WS = {c: torch.empty(K.workspace_size(0, c) + 256, dtype=torch.uint8, device=dev) for c in X}
+
+    def step():
+        px = {c: K.prepare_x(X[c], workspace=WS[c]) for c in X}
+        for _, t, r, c in wl:
+            w, yl, ya, rr = parts[(t, r, c)]
+            K.matvec_prepared(t, w, px[c], rr, c, out=yl, static_weights=True)
+            pg.all_gather_into_tensor(ya, yl)
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    pg.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    same = torch.tensor([int(all(torch.equal(parts[k][2], Y[k]) for k in parts))], device=dev)
+    pg.all_reduce(same, op=pg.ReduceOp.MIN)
+    ms = float(t.item())
+    step_bytes = sum(algo_bytes(t_, r, c) for _, t_, r, c in wl)
+    del graph
+    return {"value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 5),
+            "n_gpus": world, "scaling": "strong", "steps": steps,
+            "parallelism": f"rows of every matrix split over {world} GPUs, NCCL all_gather of each output",
+            "rows_bit_identical_to_one_gpu": bool(same.item())}
 
 
 # ---------------------------------------------------------------- batched leg
@@ -439,6 +501,41 @@ def batched_leg(dev, W, X, wl, stream, ncols_list=(8, 64)) -> dict:
                          "flops": "2 rows cols ncols per launch (algorithmic; the split-bf16 scheme issues 4x)"}}
 
 
+# ---------------------------------------------------------------- greedy parity of the model legs
+GOLDEN_2L = {"c3": "c3_2l.json", "c4": "moe_c4_2l.json", "c5": "moe_c5_2l.json"}
+
+
+def golden_parity(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
+    """The leg's architecture at full width with 2 layers, decoded on the same
+    GPUs in the same way (tensor parallel when world > 1), against the greedy
+    ids the reference executor produced for that checkpoint (tests/golden)."""
+    from dataclasses import fields
+
+    import torch
+
+    from pyrite_b200.model import MixedDecoder
+    from pyrite_b200.synthetic import DenseSpec, MoESpec
+    g = json.loads((ROOT / "tests" / "golden" / GOLDEN_2L[which]).read_text())
+    cls = MoESpec if g["spec"]["architecture"] == "qwen3moe" else DenseSpec
+    spec = cls(**{k: v for k, v in g["spec"].items() if k in {f.name for f in fields(cls)}})
+    if world > 1:
+        from pyrite_b200.sharded import ShardedDecoder
+        dec = ShardedDecoder.synthetic(spec, rank, world, device=dev, max_ctx=64)
+    else:
+        dec = MixedDecoder.synthetic(spec, device=dev, max_ctx=64)
+    prompt, want = g["prompt"], g["generated"]
+    got = dec.generate(prompt, len(want))[len(prompt):]
+    dec.graph = None  # graphs holding NCCL calls go before the process group does
+    if pg:
+        pg.barrier()
+        dec.close()
+    del dec
+    torch.cuda.empty_cache()
+    return {"golden": f"tests/golden/{GOLDEN_2L[which]}", "layers": 2, "prompt_tokens": len(prompt),
+            "generated_tokens": len(want), "greedy_ids_match": got == want,
+            "decoded_as": f"tensor parallel x{world}" if world > 1 else "one GPU"}
+
+
 # ---------------------------------------------------------------- model legs (configs[2], configs[3])
 def model_leg(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
     """Batch-1 decode throughput of a full-depth configs[2] (Llama-3-8B Q4_K_M),
@@ -462,8 +559,8 @@ def model_leg(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
 
     if which == "c3":
         spec, prefill, new, ctx = DenseSpec.c3(), 512, 128, 4096
-        cfg = ("configs[2]: Llama-3-8B-shaped, Q4_K_M mix, 32 layers, prefill 512 seeded tokens (one per step), "
-               "batch-1 decode of 128 tokens, KV ctx 4096")
+        cfg = ("configs[2]: Llama-3-8B-shaped, Q4_K_M mix, 32 layers, prefill 512 seeded tokens (blocks of 64 on one "
+               "GPU, one per step tensor parallel), batch-1 decode of 128 tokens, KV ctx 4096")
     elif which == "c4":
         spec, prefill, new, ctx = MoESpec.c4(), 256, 128, 1024
         cfg = ("configs[3]: Qwen3-30B-A3B-shaped MoE, Q4_K_M mix, 48 layers, 128 experts top-8, prefill 256 "
@@ -489,8 +586,15 @@ def model_leg(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
     if pg:
         pg.barrier()
     e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    batched = dec.batched_prefill  # dense, one GPU: the prompt in 64-position blocks on the tensor cores
+    if batched:
+        dec.prefill(prompt, 64)  # warm: buffers and kernel attributes
+        torch.cuda.synchronize(dev)
     e0.record(stream)
-    dec.run_steps(prefill - 1)
+    if batched:
+        dec.prefill(prompt, 64)
+    else:
+        dec.run_steps(prefill - 1)
     e1.record(stream)
     dec.run_steps(new)
     e2.record(stream)
@@ -526,6 +630,8 @@ def model_leg(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
         dec.close()
     out = {"config": cfg, "decode_tok_s": round(1000.0 / ms_tok, 1), "ms_per_token": round(ms_tok, 4),
            "prefill_tok_s": round((prefill - 1) * 1000.0 / pre_ms, 1),
+           "prefill": ("blocks of 64 positions, projections on the tensor cores (MixedDecoder.prefill)" if batched
+                       else "one position per step, as the reference"),
            "n_gpus": world, "parallelism": f"tensor parallel x{world}" if world > 1 else "one GPU",
            "active_weight_bytes_per_token": int(active),
            "weight_GBps": round(active / (ms_tok * 1e-3) / 1e9, 1),

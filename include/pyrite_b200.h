@@ -62,8 +62,8 @@ int pyrite_type_geometry(int type_id, size_t *block_size, size_t *bytes_per_bloc
                                       this call in the stream: its HBM stream may start
                                       before that kernel finishes (programmatic dependent
                                       launch); x and y are still ordered after it */
-#define PYRITE_F_ACCUMULATE 2u     /* pyrite_cuda_matvec_prepared: y += W x (a residual
-                                      stream) instead of y = W x */
+#define PYRITE_F_ACCUMULATE 2u     /* pyrite_cuda_matvec / _prepared / _transformed:
+                                      y += W x (a residual stream) instead of y = W x */
 
 /* Operations a batch-1 matvec can run on its whole output y (rows values) in
  * the last of its CTAs to finish (pyrite_cuda_matvec_prepared_post): the glue
@@ -270,6 +270,36 @@ int pyrite_cuda_silu_mul_encode(const float *gate_up, size_t f, float *act, void
  * (*pos + 1 < prompt_len); then *pos += 1.  scratch: >= 1184 bytes. */
 int pyrite_cuda_argmax_step(const float *logits, size_t n, void *scratch, size_t scratch_len,
                             int *tokens, int *pos, int prompt_len, int max_ctx, void *stream);
+
+/* ---- a block of prompt positions at once (batched prefill) -----------------
+ * The decode-step glue for `count` consecutive positions; each position's
+ * vector is a row of a row-major array (`ld*` floats between rows) -- the
+ * layout of pyrite_cuda_matvec's columns, so the projections of the whole
+ * block run as one multi-column (tensor-core) product.  The reference runs
+ * the prompt one position at a time (executor.py:920-923); each row here gets
+ * that position's arithmetic. */
+
+/* out row j = table row ids[j] (ids: device, count entries). */
+int pyrite_cuda_embed_rows(int type_id, const void *table, size_t rows, size_t cols, const int *ids, size_t count,
+                           float *out, long long ldo, void *stream);
+/* out row j = x row j * weight / sqrt(mean(x row j ^ 2) + eps), fp64 statistics. */
+int pyrite_cuda_rmsnorm_rows(const float *x, long long ldx, const float *weight, size_t n, size_t count,
+                             double eps, float *out, long long ldo, void *stream);
+/* pyrite_cuda_qk_rope_kv for the positions first .. first + count - 1 (qkv row
+ * j holds position first + j): q rows to q_out, k and v to cache rows first + j. */
+int pyrite_cuda_qk_rope_kv_rows(const float *qkv, long long ldqkv, const float *q_norm, const float *k_norm,
+                                int n_heads, int n_kv_heads, int head_dim, double eps, int first, int count,
+                                const void *rope_table, int max_ctx, float *q_out, long long ldq,
+                                float *k_cache, float *v_cache, void *stream);
+/* Causal GQA attention: query row j (position first + j) over cache rows
+ * 0 .. first + j, scale 1/sqrt(head_dim), fp32 (executor.py:733-755); the
+ * cache rows of the block are written before (pyrite_cuda_qk_rope_kv_rows). */
+int pyrite_cuda_attention_rows(const float *q, long long ldq, const float *k_cache, const float *v_cache,
+                               int first, int count, int n_heads, int n_kv_heads, int head_dim, int max_ctx,
+                               float *out, long long ldo, void *stream);
+/* act row j = silu(gate) * up for gate_up row j = [gate (f) | up (f)]. */
+int pyrite_cuda_silu_mul_rows(const float *gate_up, long long ldgu, size_t f, size_t count, float *act,
+                              long long lda, void *stream);
 
 /* Greedy sampling over a vocabulary split across GPUs (each holds a contiguous
  * slice of the LM head's rows): pyrite_cuda_argmax_local reduces this GPU's

@@ -176,12 +176,13 @@ int pyrite_cuda_matvec(int type_id, const void* weights, size_t weights_len, con
   if (ncols > 1 && (ldx < (long long)cols || ldy < (long long)rows)) return PYRITE_E_BUFFER;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint8_t* w = static_cast<const uint8_t*>(weights);
+  const bool acc = (flags & PYRITE_F_ACCUMULATE) != 0;
   if (ncols == 1 && lane_supported(type_id, w, rb, (int)cols)) {
     const size_t need = ws_col_bytes((int)cols);
     if (!workspace || workspace_len < need || ((uintptr_t)workspace & 255) != 0) return PYRITE_E_BUFFER;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     if ((rc = launch_xprep(x, ldx, (int)cols, 1, ws, (long long)need, s))) return rc > 0 ? PYRITE_E_CUDA : rc;
-    rc = launch_mv_lane(type_id, w, rb, (int)rows, (int)cols, ws, y, (flags & PYRITE_F_STATIC_WEIGHTS) != 0, s);
+    rc = launch_mv_lane(type_id, w, rb, (int)rows, (int)cols, ws, y, (flags & PYRITE_F_STATIC_WEIGHTS) != 0, s, acc);
     return rc > 0 ? PYRITE_E_CUDA : rc;
   }
   // Several columns of the main formats: the tensor-core product.
@@ -189,7 +190,7 @@ int pyrite_cuda_matvec(int type_id, const void* weights, size_t weights_len, con
     const size_t need = tc_workspace_bytes((int)cols, (int)ncols);
     if (!workspace || workspace_len < need || ((uintptr_t)workspace & 255) != 0) return PYRITE_E_BUFFER;
     rc = launch_mm_tc(type_id, w, rb, (int)rows, (int)cols, x, ldx, y, ldy, (int)ncols,
-                      static_cast<uint8_t*>(workspace), false, s);
+                      static_cast<uint8_t*>(workspace), acc, s);
     return rc > 0 ? PYRITE_E_CUDA : rc;
   }
   // Other types, unaligned payloads and several columns: the generic kernels,
@@ -198,10 +199,10 @@ int pyrite_cuda_matvec(int type_id, const void* weights, size_t weights_len, con
   while (c < ncols) {
     const size_t left = ncols - c;
     MatvecArgs<float> a{w, rb, (int)rows, (int)cols, x + c * ldx, ldx, y + c * ldy, ldy};
-    if (left >= 8) { rc = launch_mv_generic<float, 8>(type_id, a, s); c += 8; }
-    else if (left >= 4) { rc = launch_mv_generic<float, 4>(type_id, a, s); c += 4; }
-    else if (left >= 2) { rc = launch_mv_generic<float, 2>(type_id, a, s); c += 2; }
-    else { rc = launch_mv_generic<float, 1>(type_id, a, s); c += 1; }
+    if (left >= 8) { rc = launch_mv_generic<float, 8>(type_id, a, s, acc); c += 8; }
+    else if (left >= 4) { rc = launch_mv_generic<float, 4>(type_id, a, s, acc); c += 4; }
+    else if (left >= 2) { rc = launch_mv_generic<float, 2>(type_id, a, s, acc); c += 2; }
+    else { rc = launch_mv_generic<float, 1>(type_id, a, s, acc); c += 1; }
     if (rc) return rc > 0 ? PYRITE_E_CUDA : rc;
   }
   return 0;

@@ -53,6 +53,32 @@ __global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ 
   pdl_launch_dependents();
 }
 
+// Row j of out (ld values apart) = table row ids[j] (the embedding lookup of
+// several positions; one CTA per row).
+template <int TY>
+__global__ void __launch_bounds__(256) embed_rows_kernel(const uint8_t* __restrict__ table, size_t row_bytes, int rows,
+                                                         int cols, const int* __restrict__ ids,
+                                                         float* __restrict__ out, long long ld) {
+  pdl_wait();
+  const int row = ids[blockIdx.x];
+  float* o = out + (size_t)blockIdx.x * ld;
+  if (row >= 0 && row < rows) {  // ids are validated on the host; never read outside the table
+    const uint8_t* r = table + (size_t)row * row_bytes;
+    constexpr int BS = Geo<TY>::bs, BPB = Geo<TY>::bpb;
+    if constexpr (BS == 1) {
+      for (int c = threadIdx.x; c < cols; c += blockDim.x) o[c] = scalar_val<TY, float>(r + (size_t)c * BPB);
+    } else {
+      for (int u = threadIdx.x; u < cols / 32; u += blockDim.x) {
+        float v[32];
+        decode_unit<TY, float>(r + (size_t)(u / (BS / 32)) * BPB, u % (BS / 32), v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[32 * u + i] = v[i];
+      }
+    }
+  }
+  pdl_launch_dependents();
+}
+
 // out = x * inv * w with inv = 1/sqrt(mean(x^2) + eps) in fp64, then encoded.
 __global__ void __launch_bounds__(1024) rmsnorm_encode_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                               int n, double eps, float* __restrict__ out,
@@ -383,6 +409,153 @@ __global__ void __launch_bounds__(32) argmax_final_kernel(const float* __restric
   pdl_launch_dependents();
 }
 
+// ---- a block of prompt positions at once (batched prefill) ---------------------
+// The same operations as above for `count` consecutive positions, each
+// position's vectors a row of a row-major [count x n] array (the layout of the
+// multi-column products: column j of the tensor-core product is row j here).
+
+// out[j] = x[j] * w / sqrt(mean(x[j]^2) + eps), fp64 statistics like
+// rmsnorm_encode_kernel (executor.py:621-624); one CTA per row.
+__global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restrict__ x, long long ldx,
+                                                           const float* __restrict__ w, int n, double eps,
+                                                           float* __restrict__ out, long long ldo) {
+  __shared__ double shm[32];
+  pdl_wait();
+  const float* xr = x + (size_t)blockIdx.x * ldx;
+  double ss = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) ss += (double)xr[i] * (double)xr[i];
+  const double inv = 1.0 / sqrt(block_sum(ss, shm) / (double)(n > 0 ? n : 1) + eps);
+  float* o = out + (size_t)blockIdx.x * ldo;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = (float)((double)xr[i] * inv * (double)w[i]);
+  pdl_launch_dependents();
+}
+
+// qk_rope_kv_kernel for position first + j of row j of qkv (blockIdx.y = j):
+// q (normed, rotated) to row j of qout, k and v to cache row first + j.
+__global__ void __launch_bounds__(256) qk_rope_kv_rows_kernel(const float* __restrict__ qkv, long long ldqkv,
+                                                              const float* __restrict__ qnw,
+                                                              const float* __restrict__ knw, int nq, int nkv,
+                                                              double eps, int first, const double2* __restrict__ rope,
+                                                              float* __restrict__ qout, long long ldq,
+                                                              float* __restrict__ kcache, float* __restrict__ vcache) {
+  pdl_wait();
+  constexpr int HD = 128;
+  const int lane = threadIdx.x & 31;
+  const int head = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int j = blockIdx.y, pos = first + j;
+  if (head < nq + 2 * nkv) {
+    const int kv_dim = nkv * HD;
+    const double2* rr = rope + (size_t)pos * (HD / 2);
+    const float* src = qkv + (size_t)j * ldqkv + (size_t)head * HD;
+    if (head < nq) head_norm_rope(src, qnw, eps, rr, true, qout + (size_t)j * ldq + (size_t)head * HD, lane);
+    else if (head < nq + nkv)
+      head_norm_rope(src, knw, eps, rr, true, kcache + (size_t)pos * kv_dim + (size_t)(head - nq) * HD, lane);
+    else
+      head_norm_rope(src, nullptr, eps, rr, false, vcache + (size_t)pos * kv_dim + (size_t)(head - nq - nkv) * HD,
+                     lane);
+  }
+  pdl_launch_dependents();
+}
+
+// Causal GQA attention for queries at positions first + j (j < count, rows of
+// q) over cache rows 0..first + j (executor.py:733-755, one new token after
+// the other): one CTA per (q head, 16 queries), keys in tiles of 32 staged in
+// shared memory, online max-subtracted softmax in fp32.  Thread t owns query
+// t / 16 of the tile: scores of keys 2 (t % 16) and 2 (t % 16) + 1, output
+// dimensions 8 (t % 16) .. 8 (t % 16) + 7.
+constexpr int kAttnQB = 16, kAttnKT = 32, kAttnKStride = 129;  // padded K rows: no bank conflicts
+__global__ void __launch_bounds__(256) attention_rows_kernel(const float* __restrict__ q, long long ldq,
+                                                             const float* __restrict__ kcache,
+                                                             const float* __restrict__ vcache, int first, int count,
+                                                             int nq, int nkv, float* __restrict__ out, long long ldo) {
+  constexpr int HD = 128;
+  __shared__ float qs[kAttnQB][HD];
+  __shared__ float ks[kAttnKT * kAttnKStride];
+  __shared__ __align__(16) float vs[kAttnKT][HD];
+  __shared__ float ps[kAttnQB][kAttnKT];
+  pdl_wait();
+  const int tid = threadIdx.x, head = blockIdx.x, j0 = blockIdx.y * kAttnQB;
+  const int kvh = head / (nq / nkv), kv_dim = nkv * HD;
+  const int qi = tid >> 4, sub = tid & 15;
+  const int nqb = min(kAttnQB, count - j0);
+  for (int e = tid; e < kAttnQB * HD; e += blockDim.x) {
+    const int i = e / HD, d = e % HD;
+    qs[i][d] = i < nqb ? q[(size_t)(j0 + i) * ldq + (size_t)head * HD + d] : 0.f;
+  }
+  const int qpos = first + j0 + qi;              // this thread's query position
+  const bool qon = qi < nqb;
+  const int kend = first + j0 + nqb;             // keys 0 .. kend - 1 are needed by some query
+  const float scale = (float)(1.0 / sqrt((double)HD));
+  float m = -FLT_MAX, l = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int t0 = 0; t0 < kend; t0 += kAttnKT) {
+    __syncthreads();  // the previous tile is consumed (and q is staged)
+    for (int e = tid; e < kAttnKT * (HD / 4); e += blockDim.x) {
+      const int k = e / (HD / 4), d4 = e % (HD / 4), t = t0 + k;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (t < kend) {
+        kv = reinterpret_cast<const float4*>(kcache + (size_t)t * kv_dim + (size_t)kvh * HD)[d4];
+        vv = reinterpret_cast<const float4*>(vcache + (size_t)t * kv_dim + (size_t)kvh * HD)[d4];
+      }
+      float* kr = ks + k * kAttnKStride + 4 * d4;
+      kr[0] = kv.x; kr[1] = kv.y; kr[2] = kv.z; kr[3] = kv.w;
+      reinterpret_cast<float4*>(vs[k])[d4] = vv;
+    }
+    __syncthreads();
+    float sc[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int k = 2 * sub + u;
+      const float* kr = ks + k * kAttnKStride;
+      float d = 0.f;
+#pragma unroll 8
+      for (int e = 0; e < HD; ++e) d = fmaf(qs[qi][e], kr[e], d);
+      sc[u] = (qon && t0 + k <= qpos) ? d * scale : -FLT_MAX;
+    }
+    float tm = fmaxf(sc[0], sc[1]);
+#pragma unroll
+    for (int o2 = 8; o2 > 0; o2 >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, o2));
+    const float mn = fmaxf(m, tm);
+    const float alpha = m == -FLT_MAX ? 0.f : expf(m - mn);
+    float p0 = sc[0] == -FLT_MAX ? 0.f : expf(sc[0] - mn), p1 = sc[1] == -FLT_MAX ? 0.f : expf(sc[1] - mn);
+    ps[qi][2 * sub] = p0;
+    ps[qi][2 * sub + 1] = p1;
+    float ps_sum = p0 + p1;
+#pragma unroll
+    for (int o2 = 8; o2 > 0; o2 >>= 1) ps_sum += __shfl_xor_sync(0xffffffffu, ps_sum, o2);
+    l = l * alpha + ps_sum;
+    m = mn;
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] *= alpha;
+    for (int k = 0; k < kAttnKT; ++k) {
+      const float pk = ps[qi][k];
+      const float4 a = reinterpret_cast<const float4*>(vs[k])[2 * sub], b = reinterpret_cast<const float4*>(vs[k])[2 * sub + 1];
+      o[0] = fmaf(pk, a.x, o[0]); o[1] = fmaf(pk, a.y, o[1]); o[2] = fmaf(pk, a.z, o[2]); o[3] = fmaf(pk, a.w, o[3]);
+      o[4] = fmaf(pk, b.x, o[4]); o[5] = fmaf(pk, b.y, o[5]); o[6] = fmaf(pk, b.z, o[6]); o[7] = fmaf(pk, b.w, o[7]);
+    }
+  }
+  if (qon) {
+    float* orow = out + (size_t)(j0 + qi) * ldo + (size_t)head * HD + 8 * sub;
+    const float inv = 1.f / l;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) orow[e] = o[e] * inv;
+  }
+  pdl_launch_dependents();
+}
+
+// act[j][i] = silu(gate) * up for row j = [gate (f) | up (f)] (dense.py:491-494).
+__global__ void __launch_bounds__(256) silu_mul_rows_kernel(const float* __restrict__ gu, long long ldgu, int f,
+                                                            float* __restrict__ act, long long lda) {
+  pdl_wait();
+  const float* g = gu + (size_t)blockIdx.y * ldgu;
+  float* a = act + (size_t)blockIdx.y * lda;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < f; i += gridDim.x * blockDim.x) {
+    const float x = g[i];
+    a[i] = (x > -60.0f ? x / (1.0f + expf(-x)) : 0.0f) * g[f + i];
+  }
+  pdl_launch_dependents();
+}
+
 // One (value, index) pair from the partials of argmax_partial_kernel: this
 // GPU's best logit of its vocabulary slice and its global id (base + index).
 __global__ void __launch_bounds__(32) argmax_pair_kernel(const float* __restrict__ pv, const int* __restrict__ pi,
@@ -528,6 +701,74 @@ int pyrite_cuda_argmax_step(const float* logits, size_t n, void* scratch, size_t
   if (e) return rc(e);
   return rc(launch_pdl(argmax_final_kernel, dim3(1), dim3(32), 0, s, (const float*)pv, (const int*)pi, kParts, tokens,
                        pos, prompt_len, max_ctx));
+}
+
+int pyrite_cuda_embed_rows(int type_id, const void* table, size_t rows, size_t cols, const int* ids, size_t count,
+                           float* out, long long ldo, void* stream) {
+  const TypeGeo* t = find_type(type_id);
+  if (!t) return PYRITE_E_TYPE;
+  if (!table || !ids || !out || rows == 0 || cols == 0 || cols % (size_t)t->bs || count == 0 || count > 65535 ||
+      ldo < (long long)cols)
+    return PYRITE_E_SHAPE;
+  const size_t rb = cols / t->bs * t->bpb;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (type_id) {
+#define PYR_CASE(TY)                                                                                            \
+  case TY:                                                                                                      \
+    return rc(launch_pdl(embed_rows_kernel<TY>, dim3((unsigned)count), dim3(256), 0, s,                         \
+                         static_cast<const uint8_t*>(table), rb, (int)rows, (int)cols, ids, out, ldo));
+    PYR_FOR_EACH_TYPE(PYR_CASE)
+#undef PYR_CASE
+    default:
+      return PYRITE_E_TYPE;
+  }
+}
+
+int pyrite_cuda_rmsnorm_rows(const float* x, long long ldx, const float* weight, size_t n, size_t count, double eps,
+                             float* out, long long ldo, void* stream) {
+  if (!x || !weight || !out || n == 0 || n > (1u << 20) || count == 0 || count > 65535 || ldx < (long long)n ||
+      ldo < (long long)n)
+    return PYRITE_E_SHAPE;
+  return rc(launch_pdl(rmsnorm_rows_kernel, dim3((unsigned)count), dim3(256), 0, static_cast<cudaStream_t>(stream), x,
+                       ldx, weight, (int)n, eps, out, ldo));
+}
+
+int pyrite_cuda_qk_rope_kv_rows(const float* qkv, long long ldqkv, const float* q_norm, const float* k_norm,
+                                int n_heads, int n_kv_heads, int head_dim, double eps, int first, int count,
+                                const void* rope_table, int max_ctx, float* q_out, long long ldq, float* k_cache,
+                                float* v_cache, void* stream) {
+  if (head_dim != 128 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || !qkv || !rope_table || !q_out ||
+      !k_cache || !v_cache || first < 0 || count <= 0 || count > 65535 || first + count > max_ctx ||
+      ldqkv < (long long)(n_heads + 2 * n_kv_heads) * 128 || ldq < (long long)n_heads * 128)
+    return PYRITE_E_SHAPE;
+  const int heads = n_heads + 2 * n_kv_heads;
+  return rc(launch_pdl(qk_rope_kv_rows_kernel, dim3((unsigned)((heads + 7) / 8), (unsigned)count), dim3(256), 0,
+                       static_cast<cudaStream_t>(stream), qkv, ldqkv, q_norm, k_norm, n_heads, n_kv_heads, eps, first,
+                       static_cast<const double2*>(rope_table), q_out, ldq, k_cache, v_cache));
+}
+
+int pyrite_cuda_attention_rows(const float* q, long long ldq, const float* k_cache, const float* v_cache, int first,
+                               int count, int n_heads, int n_kv_heads, int head_dim, int max_ctx, float* out,
+                               long long ldo, void* stream) {
+  if (head_dim != 128 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || !q || !k_cache || !v_cache ||
+      !out || first < 0 || count <= 0 || first + count > max_ctx || ldq < (long long)n_heads * 128 ||
+      ldo < (long long)n_heads * 128 || ((uintptr_t)k_cache | (uintptr_t)v_cache) & 15)
+    return PYRITE_E_SHAPE;
+  const unsigned qblocks = (unsigned)((count + kAttnQB - 1) / kAttnQB);
+  if (qblocks > 65535) return PYRITE_E_SHAPE;
+  return rc(launch_pdl(attention_rows_kernel, dim3((unsigned)n_heads, qblocks), dim3(256), 0,
+                       static_cast<cudaStream_t>(stream), q, ldq, k_cache, v_cache, first, count, n_heads, n_kv_heads,
+                       out, ldo));
+}
+
+int pyrite_cuda_silu_mul_rows(const float* gate_up, long long ldgu, size_t f, size_t count, float* act, long long lda,
+                              void* stream) {
+  if (!gate_up || !act || f == 0 || f > (1u << 24) || count == 0 || count > 65535 || ldgu < 2 * (long long)f ||
+      lda < (long long)f)
+    return PYRITE_E_SHAPE;
+  const unsigned bx = (unsigned)((f + 1023) / 1024);
+  return rc(launch_pdl(silu_mul_rows_kernel, dim3(bx, (unsigned)count), dim3(256), 0,
+                       static_cast<cudaStream_t>(stream), gate_up, ldgu, (int)f, act, lda));
 }
 
 int pyrite_cuda_argmax_local(const float* logits, size_t n, long long index_base, void* scratch, size_t scratch_len,

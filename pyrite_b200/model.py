@@ -370,6 +370,90 @@ class MixedDecoder:
         post.prompt_len, post.max_ctx = self.prompt_len, self.max_ctx
         self._mv(self.lm_head, self.normed, self.ws_h, self.logits, 0, stream, post=post)
 
+    # ------------------------------------------------------------------ batched prefill
+    @property
+    def batched_prefill(self) -> bool:
+        """Whether :meth:`prefill` runs blocks of positions (dense checkpoints on
+        one GPU) or the one-position step."""
+        return not self.moe
+
+    def _mm(self, m: _Mat, x: torch.Tensor, ldx: int, y: torch.Tensor, ldy: int, ncols: int, ws: torch.Tensor,
+            flags: int, stream: int) -> None:
+        """Y[j] (+)= W X[j] for ncols rows of X (row-major, ldx / ldy floats
+        apart): the tensor-core product where the format has one."""
+        off = (-ws.data_ptr()) % 256
+        code = self.lib.pyrite_cuda_matvec(m.ggml_type, m.data.data_ptr(), m.data.numel(), x.data_ptr(), ldx,
+                                           y.data_ptr(), ldy, m.rows, m.cols, ncols, flags | STATIC_WEIGHTS,
+                                           ws.data_ptr() + off, ws.numel() - off, stream)
+        _check(code, "multi-column matvec")
+
+    def prefill(self, prompt: list[int], block: int = 64) -> None:
+        """Reset to ``prompt`` and run positions 0 .. len(prompt) - 2 through
+        the model in blocks of up to ``block`` positions, so that the next
+        decode step (position len(prompt) - 1) yields the first new token.
+
+        The reference runs the prompt one position per forward pass
+        (executor.py:920-923); here every projection of a block is one
+        multi-column product on the tensor cores (pyrite_cuda_matvec with
+        ncols > 1), the glue runs per row (pyrite_cuda_*_rows) and attention is
+        causal inside the block.  Each position gets the arithmetic of the
+        one-token step up to fp32 summation order; the last layer's
+        feed-forward is skipped (it feeds only the logits of prompt positions,
+        which greedy decoding never reads).  Dense checkpoints; MoE
+        checkpoints run their prompt through the one-token step."""
+        self.reset(prompt)
+        n = len(prompt) - 1
+        if n <= 0:
+            return
+        if not self.batched_prefill:
+            self.run_steps(n)
+            return
+        s, L, d = self.spec, self.lib, self.dev
+        h, ff, q, kv = s.hidden_size, self.ff, s.q_dim, s.kv_dim
+        B = max(1, min(block, n))
+        z = lambda *shape: torch.empty(*shape, dtype=torch.float32, device=d)  # noqa: E731
+        hid, nrm, qkv, qr, att = z(B, h), z(B, h), z(B, q + 2 * kv), z(B, q), z(B, q)
+        gu, act = z(B, 2 * ff), z(B, ff)
+        mats = [m for ly in self.layers for m in (ly.qk, ly.v, ly.o, ly.gate_up, ly.gate, ly.up, ly.down) if m is not None]
+        need = max(int(L.pyrite_cuda_workspace_size(m.ggml_type, m.cols, c)) for m in mats for c in {1, B})
+        ws = torch.empty(need + 256, dtype=torch.uint8, device=d)
+        st = torch.cuda.current_stream(d).cuda_stream
+        eps = float(s.rms_norm_eps)
+        last = len(self.layers) - 1
+        for p0 in range(0, n, B):
+            c = min(B, n - p0)
+            _check(L.pyrite_cuda_embed_rows(self.embd.ggml_type, self.embd.data.data_ptr(), s.vocab_size, h,
+                                            self.tokens[p0:].data_ptr(), c, hid.data_ptr(), h, st), "embed rows")
+            for li, ly in enumerate(self.layers):
+                _check(L.pyrite_cuda_rmsnorm_rows(hid.data_ptr(), h, ly.attn_norm.data_ptr(), h, c, eps,
+                                                  nrm.data_ptr(), h, st), "rmsnorm rows")
+                self._mm(ly.qk, nrm, h, qkv, q + 2 * kv, c, ws, 0, st)
+                self._mm(ly.v, nrm, h, qkv[:, q + kv:], q + 2 * kv, c, ws, 0, st)
+                _check(L.pyrite_cuda_qk_rope_kv_rows(
+                    qkv.data_ptr(), q + 2 * kv, ly.q_norm.data_ptr() if ly.q_norm is not None else None,
+                    ly.k_norm.data_ptr() if ly.k_norm is not None else None, s.num_attention_heads,
+                    s.num_key_value_heads, s.head_dim, eps, p0, c, self.rope.data_ptr(), self.max_ctx, qr.data_ptr(), q,
+                    self.kcache[li].data_ptr(), self.vcache[li].data_ptr(), st), "qk rope kv rows")
+                _check(L.pyrite_cuda_attention_rows(qr.data_ptr(), q, self.kcache[li].data_ptr(),
+                                                    self.vcache[li].data_ptr(), p0, c, s.num_attention_heads,
+                                                    s.num_key_value_heads, s.head_dim, self.max_ctx, att.data_ptr(), q,
+                                                    st), "attention rows")
+                self._mm(ly.o, att, q, hid, h, c, ws, ACCUMULATE, st)
+                if li == last:
+                    continue
+                _check(L.pyrite_cuda_rmsnorm_rows(hid.data_ptr(), h, ly.ffn_norm.data_ptr(), h, c, eps,
+                                                  nrm.data_ptr(), h, st), "rmsnorm rows")
+                if ly.gate_up is not None:
+                    self._mm(ly.gate_up, nrm, h, gu, 2 * ff, c, ws, 0, st)
+                else:
+                    self._mm(ly.gate, nrm, h, gu, 2 * ff, c, ws, 0, st)
+                    self._mm(ly.up, nrm, h, gu[:, ff:], 2 * ff, c, ws, 0, st)
+                _check(L.pyrite_cuda_silu_mul_rows(gu.data_ptr(), 2 * ff, ff, c, act.data_ptr(), ff, st), "silu rows")
+                self._mm(ly.down, act, ff, hid, h, c, ws, ACCUMULATE, st)
+        self.pos.fill_(n)
+        torch.cuda.synchronize(d)
+        del hid, nrm, qkv, qr, att, gu, act, ws
+
     # ------------------------------------------------------------------ public
     def reset(self, prompt: list[int]) -> None:
         if not prompt or any(not 0 <= t < self.spec.vocab_size for t in prompt):
@@ -405,8 +489,10 @@ class MixedDecoder:
         for _ in range(n):
             self.graph.replay()
 
-    def generate(self, prompt: list[int], max_new_tokens: int) -> list[int]:
-        """Greedy continuation, the reference's ``generate(..., temperature=0)``."""
+    def generate(self, prompt: list[int], max_new_tokens: int, prefill_block: int = 0) -> list[int]:
+        """Greedy continuation, the reference's ``generate(..., temperature=0)``.
+        ``prefill_block`` > 0: the prompt in blocks of that many positions
+        (:meth:`prefill`); 0: one position per step, as the reference."""
         if len(prompt) + max_new_tokens > self.max_ctx:
             raise ValueError("prompt + new tokens exceed the KV cache")
         if max_new_tokens == 0:
@@ -414,8 +500,12 @@ class MixedDecoder:
         if self.graph is None or self.prompt_len != len(prompt):
             self.reset(prompt)
             self.capture()
-        self.reset(prompt)
-        self.run_steps(len(prompt) + max_new_tokens - 1)
+        if prefill_block > 0:
+            self.prefill(prompt, prefill_block)
+            self.run_steps(max_new_tokens)
+        else:
+            self.reset(prompt)
+            self.run_steps(len(prompt) + max_new_tokens - 1)
         torch.cuda.synchronize(self.dev)
         self.check_status()
         return [int(t) for t in self.tokens[: len(prompt) + max_new_tokens].cpu()]

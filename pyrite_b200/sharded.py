@@ -211,6 +211,13 @@ class ShardedDecoder(MixedDecoder):
             self._ipc_owned = None
         self.peer_buffers = None
 
+    @property
+    def batched_prefill(self) -> bool:
+        """Tensor-parallel prompts run through the one-position step (its
+        projections' partials are summed across GPUs after each block's
+        products, which the batched path does not do)."""
+        return False
+
     def capture(self) -> None:
         dist.barrier(group=self.group)  # the ranks' first steps start together
         super().capture()
