@@ -271,32 +271,47 @@ int pyrite_cuda_silu_mul_encode(const float *gate_up, size_t f, float *act, void
 int pyrite_cuda_argmax_step(const float *logits, size_t n, void *scratch, size_t scratch_len,
                             int *tokens, int *pos, int prompt_len, int max_ctx, void *stream);
 
-/* ---- a block of prompt positions at once (batched prefill) -----------------
- * The decode-step glue for `count` consecutive positions; each position's
- * vector is a row of a row-major array (`ld*` floats between rows) -- the
- * layout of pyrite_cuda_matvec's columns, so the projections of the whole
- * block run as one multi-column (tensor-core) product.  The reference runs
- * the prompt one position at a time (executor.py:920-923); each row here gets
- * that position's arithmetic. */
+/* ---- several positions or sequences at once (prefill, multi-sequence decode)
+ * The decode-step glue for `count` rows; each row's vector is a row of a
+ * row-major array (`ld*` floats between rows) -- the layout of
+ * pyrite_cuda_matvec's columns, so the projections of all rows run as one
+ * multi-column (tensor-core) product.  The reference runs one position of one
+ * sequence per forward pass (executor.py:878-939); each row here gets that
+ * position's arithmetic.  Row j sits at position first + *pos + j * pos_step
+ * (pos: device int, may be NULL = 0, read when the kernel runs so a CUDA graph
+ * can replay the call): pos_step 1 = consecutive positions of one sequence
+ * (batched prefill), pos_step 0 = one position shared by `count` sequences,
+ * row j's KV cache cache_stride floats after row 0's (multi-sequence decode).
+ * Rows outside [0, max_ctx) are rejected (host position) or skipped (device). */
 
-/* out row j = table row ids[j] (ids: device, count entries). */
-int pyrite_cuda_embed_rows(int type_id, const void *table, size_t rows, size_t cols, const int *ids, size_t count,
-                           float *out, long long ldo, void *stream);
+/* out row j = table row ids[j * ids_stride + *pos] (ids, pos: device; pos may be NULL). */
+int pyrite_cuda_embed_rows(int type_id, const void *table, size_t rows, size_t cols, const int *ids,
+                           long long ids_stride, const int *pos, size_t count, float *out, long long ldo,
+                           void *stream);
 /* out row j = x row j * weight / sqrt(mean(x row j ^ 2) + eps), fp64 statistics. */
 int pyrite_cuda_rmsnorm_rows(const float *x, long long ldx, const float *weight, size_t n, size_t count,
                              double eps, float *out, long long ldo, void *stream);
-/* pyrite_cuda_qk_rope_kv for the positions first .. first + count - 1 (qkv row
- * j holds position first + j): q rows to q_out, k and v to cache rows first + j. */
+/* pyrite_cuda_qk_rope_kv for each row at its position: q rows to q_out, k and v
+ * to that position's row of the row's caches. */
 int pyrite_cuda_qk_rope_kv_rows(const float *qkv, long long ldqkv, const float *q_norm, const float *k_norm,
-                                int n_heads, int n_kv_heads, int head_dim, double eps, int first, int count,
-                                const void *rope_table, int max_ctx, float *q_out, long long ldq,
-                                float *k_cache, float *v_cache, void *stream);
-/* Causal GQA attention: query row j (position first + j) over cache rows
- * 0 .. first + j, scale 1/sqrt(head_dim), fp32 (executor.py:733-755); the
- * cache rows of the block are written before (pyrite_cuda_qk_rope_kv_rows). */
+                                int n_heads, int n_kv_heads, int head_dim, double eps, int first, const int *pos,
+                                int pos_step, long long cache_stride, int count, const void *rope_table,
+                                int max_ctx, float *q_out, long long ldq, float *k_cache, float *v_cache,
+                                void *stream);
+/* Causal GQA attention: query row j (position p_j) over rows 0 .. p_j of its
+ * cache, scale 1/sqrt(head_dim), fp32 (executor.py:733-755); the rows'
+ * own k / v are written before (pyrite_cuda_qk_rope_kv_rows). */
 int pyrite_cuda_attention_rows(const float *q, long long ldq, const float *k_cache, const float *v_cache,
-                               int first, int count, int n_heads, int n_kv_heads, int head_dim, int max_ctx,
-                               float *out, long long ldo, void *stream);
+                               long long cache_stride, int first, const int *pos, int pos_step, int count,
+                               int n_heads, int n_kv_heads, int head_dim, int max_ctx, float *out, long long ldo,
+                               void *stream);
+/* Greedy token of each row of [count x n] logits (one sequence per row):
+ * tokens[j * tok_stride + *pos + 1] = first index of the row's maximum unless
+ * that position still holds the prompt (sampler.py:12-15).  *pos is left as it
+ * is; pyrite_cuda_advance_pos adds 1 to it. */
+int pyrite_cuda_argmax_rows(const float *logits, long long ld, size_t n, size_t count, int *tokens,
+                            long long tok_stride, const int *pos, int prompt_len, int max_ctx, void *stream);
+int pyrite_cuda_advance_pos(int *pos, void *stream);
 /* act row j = silu(gate) * up for gate_up row j = [gate (f) | up (f)]. */
 int pyrite_cuda_silu_mul_rows(const float *gate_up, long long ldgu, size_t f, size_t count, float *act,
                               long long lda, void *stream);
@@ -376,12 +391,41 @@ int pyrite_cuda_matvec_experts(int type_id, const void *stacked, size_t stacked_
  * n_groups * n_experts * rows * row_bytes), all in one launch: selection
  * j < n_groups * n_ids multiplies expert expert_ids[j % n_ids] of stack
  * j / n_ids by activation j % n_ids into y + j * y_stride.  n_groups <= 8,
- * n_groups * n_ids <= 64. */
+ * n_groups * n_ids <= 1024. */
 int pyrite_cuda_matvec_expert_groups(int type_id, const void *stacked, size_t stacked_len, size_t n_experts,
                                      size_t n_groups, const int *expert_ids, size_t n_ids, const float *x,
                                      size_t x_stride, const void *workspace, size_t workspace_len,
                                      size_t ws_stride, float *y, size_t y_stride, size_t rows, size_t cols,
                                      unsigned flags, void *stream);
+
+/* pyrite_cuda_matvec_expert_groups for `count` sequences at once: expert_ids
+ * holds each sequence's top_k experts (count x top_k, as
+ * pyrite_cuda_moe_route_rows writes them), and selection j of a group
+ * multiplies expert expert_ids[j] by the activation of sequence j / top_k --
+ * x + (j / top_k) * x_stride and its encoding at workspace + (j / top_k) *
+ * ws_stride (pyrite_cuda_prepare_x of the count rows) -- into y + (group *
+ * count * top_k + j) * y_stride.  count * top_k * n_groups <= 1024. */
+int pyrite_cuda_matvec_expert_rows(int type_id, const void *stacked, size_t stacked_len, size_t n_experts,
+                                   size_t n_groups, const int *expert_ids, size_t count, size_t top_k,
+                                   const float *x, size_t x_stride, const void *workspace, size_t workspace_len,
+                                   size_t ws_stride, float *y, size_t y_stride, size_t rows, size_t cols,
+                                   unsigned flags, void *stream);
+/* The F32 router product (type id 0) of `count` sequences: router_logits[b *
+ * ld + e] = W[e] . x[b * ldx ...], accumulated in fp64 and rounded to fp32
+ * once, as pyrite_cuda_moe_router_route computes one sequence's. */
+int pyrite_cuda_moe_router_rows(int router_type, const void *router, size_t router_len, size_t hidden,
+                                const float *x, long long ldx, size_t count, float *router_logits, long long ld,
+                                int n_experts, void *stream);
+/* pyrite_cuda_moe_route for each row of a [count x n_experts] logits array (one
+ * sequence per row): row j's experts and weights at expert_ids / expert_weights
+ * + j * top_k (one GPU: no expert sharding). */
+int pyrite_cuda_moe_route_rows(const float *router_logits, long long ld, size_t count, int n_experts, int top_k,
+                               int norm_topk_prob, double scale, int *expert_ids, float *expert_weights,
+                               void *stream);
+/* Row b of hidden (ldh floats apart) += sum_j expert_weights[b top_k + j] *
+ * expert_out[(b top_k + j) h ...], j ascending, for b < count. */
+int pyrite_cuda_moe_combine_rows(const float *expert_out, const float *expert_weights, size_t top_k, size_t h,
+                                 size_t count, float *hidden, long long ldh, void *stream);
 
 /* act_j = silu(gate_j) * up_j for the n_sel experts (gate, up, act: n_sel x ff),
  * each encoded at workspace + j * pyrite_cuda_workspace_size(0, ff, 1). */

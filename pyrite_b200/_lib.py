@@ -65,16 +65,24 @@ SIGNATURES: dict[str, tuple] = {
     "pyrite_cuda_ipc_buffer_create": (ctypes.c_int, (_SZ, _VP, _VP)),
     "pyrite_cuda_ipc_buffer_open": (ctypes.c_int, (_VP, _VP)),
     "pyrite_cuda_ipc_buffer_close": (ctypes.c_int, (_VP, ctypes.c_int)),
-    "pyrite_cuda_embed_rows": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _SZ, _VP, _SZ, _VP, ctypes.c_longlong, _VP)),
+    "pyrite_cuda_embed_rows": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _SZ, _VP, ctypes.c_longlong, _VP, _SZ, _VP, ctypes.c_longlong, _VP)),
     "pyrite_cuda_rmsnorm_rows": (ctypes.c_int, (_VP, ctypes.c_longlong, _VP, _SZ, _SZ, ctypes.c_double, _VP, ctypes.c_longlong, _VP)),
-    "pyrite_cuda_qk_rope_kv_rows": (ctypes.c_int, (_VP, ctypes.c_longlong, _VP, _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                                                   ctypes.c_double, ctypes.c_int, ctypes.c_int, _VP, ctypes.c_int, _VP,
-                                                   ctypes.c_longlong, _VP, _VP, _VP)),
-    "pyrite_cuda_attention_rows": (ctypes.c_int, (_VP, ctypes.c_longlong, _VP, _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                                                  ctypes.c_int, ctypes.c_int, ctypes.c_int, _VP, ctypes.c_longlong, _VP)),
+    "pyrite_cuda_qk_rope_kv_rows": (ctypes.c_int, (_VP, ctypes.c_longlong, _VP, _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_int, _VP, ctypes.c_int,
+                                                   ctypes.c_longlong, ctypes.c_int, _VP, ctypes.c_int, _VP, ctypes.c_longlong, _VP, _VP, _VP)),
+    "pyrite_cuda_attention_rows": (ctypes.c_int, (_VP, ctypes.c_longlong, _VP, _VP, ctypes.c_longlong, ctypes.c_int, _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                  _VP, ctypes.c_longlong, _VP)),
+    "pyrite_cuda_argmax_rows": (ctypes.c_int, (_VP, ctypes.c_longlong, _SZ, _SZ, _VP, ctypes.c_longlong, _VP, ctypes.c_int, ctypes.c_int, _VP)),
+    "pyrite_cuda_advance_pos": (ctypes.c_int, (_VP, _VP)),
     "pyrite_cuda_silu_mul_rows": (ctypes.c_int, (_VP, ctypes.c_longlong, _SZ, _SZ, _VP, ctypes.c_longlong, _VP)),
     "pyrite_cuda_argmax_local": (ctypes.c_int, (_VP, _SZ, ctypes.c_longlong, _VP, _SZ, _VP, _VP)),
     "pyrite_cuda_argmax_pick": (ctypes.c_int, (_VP, _SZ, _VP, _VP, ctypes.c_int, ctypes.c_int, _VP)),
+    "pyrite_cuda_matvec_expert_rows": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _SZ, _SZ, _VP, _SZ, _SZ, _VP, _SZ, _VP, _SZ,
+                                                      _SZ, _VP, _SZ, _SZ, _SZ, ctypes.c_uint, _VP)),
+    "pyrite_cuda_moe_router_rows": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _SZ, _VP, ctypes.c_longlong, _SZ, _VP,
+                                                   ctypes.c_longlong, ctypes.c_int, _VP)),
+    "pyrite_cuda_moe_route_rows": (ctypes.c_int, (_VP, ctypes.c_longlong, _SZ, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_double, _VP, _VP,
+                                                  _VP)),
+    "pyrite_cuda_moe_combine_rows": (ctypes.c_int, (_VP, _VP, _SZ, _SZ, _SZ, _VP, ctypes.c_longlong, _VP)),
     "pyrite_cuda_allreduce_sum": (ctypes.c_int, (_VP, _VP, _SZ, _VP, _SZ, ctypes.c_int, ctypes.c_int, _VP, _VP)),
     "pyrite_cuda_moe_norm_router_route": (ctypes.c_int, (ctypes.c_int, _VP, _SZ, _SZ, _VP, _VP, ctypes.c_double, _VP,
                                                          _VP, _SZ, _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int,

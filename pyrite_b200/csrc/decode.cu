@@ -53,14 +53,16 @@ __global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ 
   pdl_launch_dependents();
 }
 
-// Row j of out (ld values apart) = table row ids[j] (the embedding lookup of
-// several positions; one CTA per row).
+// Row j of out (ld values apart) = table row ids[j * ids_stride + *pos] (the
+// embedding lookup of several positions or sequences; pos may be NULL: 0; one
+// CTA per row).
 template <int TY>
 __global__ void __launch_bounds__(256) embed_rows_kernel(const uint8_t* __restrict__ table, size_t row_bytes, int rows,
-                                                         int cols, const int* __restrict__ ids,
-                                                         float* __restrict__ out, long long ld) {
+                                                         int cols, const int* __restrict__ ids, long long ids_stride,
+                                                         const int* __restrict__ pos, float* __restrict__ out,
+                                                         long long ld) {
   pdl_wait();
-  const int row = ids[blockIdx.x];
+  const int row = ids[(size_t)blockIdx.x * ids_stride + (pos ? *pos : 0)];
   float* o = out + (size_t)blockIdx.x * ld;
   if (row >= 0 && row < rows) {  // ids are validated on the host; never read outside the table
     const uint8_t* r = table + (size_t)row * row_bytes;
@@ -414,6 +416,19 @@ __global__ void __launch_bounds__(32) argmax_final_kernel(const float* __restric
 // position's vectors a row of a row-major [count x n] array (the layout of the
 // multi-column products: column j of the tensor-core product is row j here).
 
+// Position of row j: first + *pos (pos may be NULL) + j * step -- consecutive
+// positions of one sequence (prefill: step 1) or one position shared by
+// several sequences (multi-sequence decode: step 0, each with its own cache
+// cache_stride floats apart).  Rows outside [0, max_ctx) are skipped.
+struct RowPos {
+  int first;
+  const int* pos;
+  int step;
+  long long cache_stride;
+  int max_ctx;
+  __device__ __forceinline__ int at(int j) const { return first + (pos ? *pos : 0) + j * step; }
+};
+
 // out[j] = x[j] * w / sqrt(mean(x[j]^2) + eps), fp64 statistics like
 // rmsnorm_encode_kernel (executor.py:621-624); one CTA per row.
 __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restrict__ x, long long ldx,
@@ -430,20 +445,24 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restri
   pdl_launch_dependents();
 }
 
-// qk_rope_kv_kernel for position first + j of row j of qkv (blockIdx.y = j):
-// q (normed, rotated) to row j of qout, k and v to cache row first + j.
+// qk_rope_kv_kernel for row j of qkv (blockIdx.y = j) at position rp.at(j): q
+// (normed, rotated) to row j of qout, k and v to row rp.at(j) of row j's
+// caches (rp.cache_stride floats apart; 0: one cache).
 __global__ void __launch_bounds__(256) qk_rope_kv_rows_kernel(const float* __restrict__ qkv, long long ldqkv,
                                                               const float* __restrict__ qnw,
                                                               const float* __restrict__ knw, int nq, int nkv,
-                                                              double eps, int first, const double2* __restrict__ rope,
+                                                              double eps, RowPos rp, const double2* __restrict__ rope,
                                                               float* __restrict__ qout, long long ldq,
-                                                              float* __restrict__ kcache, float* __restrict__ vcache) {
+                                                              float* __restrict__ kcache_base,
+                                                              float* __restrict__ vcache_base) {
   pdl_wait();
   constexpr int HD = 128;
   const int lane = threadIdx.x & 31;
   const int head = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int j = blockIdx.y, pos = first + j;
-  if (head < nq + 2 * nkv) {
+  const int j = blockIdx.y, pos = rp.at(j);
+  float* kcache = kcache_base + (size_t)j * rp.cache_stride;
+  float* vcache = vcache_base + (size_t)j * rp.cache_stride;
+  if (head < nq + 2 * nkv && pos >= 0 && pos < rp.max_ctx) {
     const int kv_dim = nkv * HD;
     const double2* rr = rope + (size_t)pos * (HD / 2);
     const float* src = qkv + (size_t)j * ldqkv + (size_t)head * HD;
@@ -465,26 +484,33 @@ __global__ void __launch_bounds__(256) qk_rope_kv_rows_kernel(const float* __res
 // dimensions 8 (t % 16) .. 8 (t % 16) + 7.
 constexpr int kAttnQB = 16, kAttnKT = 32, kAttnKStride = 129;  // padded K rows: no bank conflicts
 __global__ void __launch_bounds__(256) attention_rows_kernel(const float* __restrict__ q, long long ldq,
-                                                             const float* __restrict__ kcache,
-                                                             const float* __restrict__ vcache, int first, int count,
-                                                             int nq, int nkv, float* __restrict__ out, long long ldo) {
+                                                             const float* __restrict__ kcache_base,
+                                                             const float* __restrict__ vcache_base, RowPos rp,
+                                                             int count, int nq, int nkv, float* __restrict__ out,
+                                                             long long ldo) {
   constexpr int HD = 128;
   __shared__ float qs[kAttnQB][HD];
   __shared__ float ks[kAttnKT * kAttnKStride];
   __shared__ __align__(16) float vs[kAttnKT][HD];
   __shared__ float ps[kAttnQB][kAttnKT];
   pdl_wait();
-  const int tid = threadIdx.x, head = blockIdx.x, j0 = blockIdx.y * kAttnQB;
+  // a CTA: 16 consecutive positions of one sequence (rp.step 1), or the one
+  // query of one sequence (rp.step 0: each row has its own cache)
+  const int qb = rp.step ? kAttnQB : 1;
+  const int tid = threadIdx.x, head = blockIdx.x, j0 = blockIdx.y * qb;
   const int kvh = head / (nq / nkv), kv_dim = nkv * HD;
+  const float* kcache = kcache_base + (size_t)j0 * rp.cache_stride;
+  const float* vcache = vcache_base + (size_t)j0 * rp.cache_stride;
   const int qi = tid >> 4, sub = tid & 15;
-  const int nqb = min(kAttnQB, count - j0);
+  const int nqb = min(qb, count - j0);
   for (int e = tid; e < kAttnQB * HD; e += blockDim.x) {
     const int i = e / HD, d = e % HD;
     qs[i][d] = i < nqb ? q[(size_t)(j0 + i) * ldq + (size_t)head * HD + d] : 0.f;
   }
-  const int qpos = first + j0 + qi;              // this thread's query position
-  const bool qon = qi < nqb;
-  const int kend = first + j0 + nqb;             // keys 0 .. kend - 1 are needed by some query
+  const int qpos = rp.at(j0 + min(qi, nqb - 1));  // this thread's query position
+  const bool qon = qi < nqb && qpos >= 0 && qpos < rp.max_ctx;
+  // keys 0 .. kend - 1 are needed by some query (positions grow with the row)
+  const int kend = min(rp.at(j0 + nqb - 1) + 1, rp.max_ctx);
   const float scale = (float)(1.0 / sqrt((double)HD));
   float m = -FLT_MAX, l = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   for (int t0 = 0; t0 < kend; t0 += kAttnKT) {
@@ -553,6 +579,40 @@ __global__ void __launch_bounds__(256) silu_mul_rows_kernel(const float* __restr
     const float x = g[i];
     a[i] = (x > -60.0f ? x / (1.0f + expf(-x)) : 0.0f) * g[f + i];
   }
+  pdl_launch_dependents();
+}
+
+// Greedy token of row j of a [count x n] logits array (one sequence per row):
+// the first index of the row's largest logit to tokens[j * tok_stride + *pos +
+// 1] unless that position still holds the prompt (sampler.py:12-15); *pos is
+// not advanced here (pyrite_cuda_advance_pos, once for all rows).
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restrict__ x, long long ld, int n,
+                                                           int* __restrict__ tokens, long long tok_stride,
+                                                           const int* __restrict__ pos, int prompt_len, int max_ctx) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  pdl_wait();
+  const float* r = x + (size_t)blockIdx.x * ld;
+  float v = -FLT_MAX;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) better(v, idx, r[i], i);
+  warp_best(v, idx);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) { sv[warp] = v; si[warp] = idx; }
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < (int)(blockDim.x >> 5) ? sv[lane] : -FLT_MAX;
+    idx = lane < (int)(blockDim.x >> 5) ? si[lane] : 0x7fffffff;
+    warp_best(v, idx);
+    const int p = *pos;
+    if (lane == 0 && p + 1 < max_ctx && p + 1 >= prompt_len) tokens[(size_t)blockIdx.x * tok_stride + p + 1] = idx;
+  }
+  pdl_launch_dependents();
+}
+
+__global__ void advance_pos_kernel(int* pos) {
+  pdl_wait();
+  if (threadIdx.x == 0) *pos += 1;
   pdl_launch_dependents();
 }
 
@@ -703,12 +763,13 @@ int pyrite_cuda_argmax_step(const float* logits, size_t n, void* scratch, size_t
                        pos, prompt_len, max_ctx));
 }
 
-int pyrite_cuda_embed_rows(int type_id, const void* table, size_t rows, size_t cols, const int* ids, size_t count,
-                           float* out, long long ldo, void* stream) {
+int pyrite_cuda_embed_rows(int type_id, const void* table, size_t rows, size_t cols, const int* ids,
+                           long long ids_stride, const int* pos, size_t count, float* out, long long ldo,
+                           void* stream) {
   const TypeGeo* t = find_type(type_id);
   if (!t) return PYRITE_E_TYPE;
   if (!table || !ids || !out || rows == 0 || cols == 0 || cols % (size_t)t->bs || count == 0 || count > 65535 ||
-      ldo < (long long)cols)
+      ldo < (long long)cols || ids_stride < 0)
     return PYRITE_E_SHAPE;
   const size_t rb = cols / t->bs * t->bpb;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -716,7 +777,8 @@ int pyrite_cuda_embed_rows(int type_id, const void* table, size_t rows, size_t c
 #define PYR_CASE(TY)                                                                                            \
   case TY:                                                                                                      \
     return rc(launch_pdl(embed_rows_kernel<TY>, dim3((unsigned)count), dim3(256), 0, s,                         \
-                         static_cast<const uint8_t*>(table), rb, (int)rows, (int)cols, ids, out, ldo));
+                         static_cast<const uint8_t*>(table), rb, (int)rows, (int)cols, ids, ids_stride, pos, out, \
+                         ldo));
     PYR_FOR_EACH_TYPE(PYR_CASE)
 #undef PYR_CASE
     default:
@@ -733,32 +795,61 @@ int pyrite_cuda_rmsnorm_rows(const float* x, long long ldx, const float* weight,
                        ldx, weight, (int)n, eps, out, ldo));
 }
 
+namespace {
+// Host checks of the row positions: with a device position only the kernel
+// can check (it skips rows outside the cache); without one, all of them here.
+bool rows_in_cache(int first, const int* pos, int step, int count, int max_ctx) {
+  if (count <= 0 || count > 65535 || max_ctx <= 0 || (step != 0 && step != 1)) return false;
+  if (pos) return true;
+  return first >= 0 && (long long)first + (long long)(count - 1) * step < max_ctx;
+}
+}  // namespace
+
 int pyrite_cuda_qk_rope_kv_rows(const float* qkv, long long ldqkv, const float* q_norm, const float* k_norm,
-                                int n_heads, int n_kv_heads, int head_dim, double eps, int first, int count,
-                                const void* rope_table, int max_ctx, float* q_out, long long ldq, float* k_cache,
-                                float* v_cache, void* stream) {
+                                int n_heads, int n_kv_heads, int head_dim, double eps, int first, const int* pos,
+                                int pos_step, long long cache_stride, int count, const void* rope_table, int max_ctx,
+                                float* q_out, long long ldq, float* k_cache, float* v_cache, void* stream) {
   if (head_dim != 128 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || !qkv || !rope_table || !q_out ||
-      !k_cache || !v_cache || first < 0 || count <= 0 || count > 65535 || first + count > max_ctx ||
+      !k_cache || !v_cache || !rows_in_cache(first, pos, pos_step, count, max_ctx) || cache_stride < 0 ||
+      (pos_step == 0 && count > 1 && cache_stride < (long long)max_ctx * n_kv_heads * 128) ||
       ldqkv < (long long)(n_heads + 2 * n_kv_heads) * 128 || ldq < (long long)n_heads * 128)
     return PYRITE_E_SHAPE;
   const int heads = n_heads + 2 * n_kv_heads;
+  RowPos rp{first, pos, pos_step, cache_stride, max_ctx};
   return rc(launch_pdl(qk_rope_kv_rows_kernel, dim3((unsigned)((heads + 7) / 8), (unsigned)count), dim3(256), 0,
-                       static_cast<cudaStream_t>(stream), qkv, ldqkv, q_norm, k_norm, n_heads, n_kv_heads, eps, first,
+                       static_cast<cudaStream_t>(stream), qkv, ldqkv, q_norm, k_norm, n_heads, n_kv_heads, eps, rp,
                        static_cast<const double2*>(rope_table), q_out, ldq, k_cache, v_cache));
 }
 
-int pyrite_cuda_attention_rows(const float* q, long long ldq, const float* k_cache, const float* v_cache, int first,
-                               int count, int n_heads, int n_kv_heads, int head_dim, int max_ctx, float* out,
-                               long long ldo, void* stream) {
+int pyrite_cuda_attention_rows(const float* q, long long ldq, const float* k_cache, const float* v_cache,
+                               long long cache_stride, int first, const int* pos, int pos_step, int count, int n_heads,
+                               int n_kv_heads, int head_dim, int max_ctx, float* out, long long ldo, void* stream) {
   if (head_dim != 128 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || !q || !k_cache || !v_cache ||
-      !out || first < 0 || count <= 0 || first + count > max_ctx || ldq < (long long)n_heads * 128 ||
-      ldo < (long long)n_heads * 128 || ((uintptr_t)k_cache | (uintptr_t)v_cache) & 15)
+      !out || !rows_in_cache(first, pos, pos_step, count, max_ctx) || cache_stride < 0 ||
+      (pos_step == 0 && count > 1 && cache_stride < (long long)max_ctx * n_kv_heads * 128) ||
+      ldq < (long long)n_heads * 128 || ldo < (long long)n_heads * 128 ||
+      (((uintptr_t)k_cache | (uintptr_t)v_cache) & 15) || (cache_stride & 3))
     return PYRITE_E_SHAPE;
-  const unsigned qblocks = (unsigned)((count + kAttnQB - 1) / kAttnQB);
-  if (qblocks > 65535) return PYRITE_E_SHAPE;
+  const int qb = pos_step ? kAttnQB : 1;
+  const unsigned qblocks = (unsigned)((count + qb - 1) / qb);
+  RowPos rp{first, pos, pos_step, cache_stride, max_ctx};
   return rc(launch_pdl(attention_rows_kernel, dim3((unsigned)n_heads, qblocks), dim3(256), 0,
-                       static_cast<cudaStream_t>(stream), q, ldq, k_cache, v_cache, first, count, n_heads, n_kv_heads,
+                       static_cast<cudaStream_t>(stream), q, ldq, k_cache, v_cache, rp, count, n_heads, n_kv_heads,
                        out, ldo));
+}
+
+int pyrite_cuda_argmax_rows(const float* logits, long long ld, size_t n, size_t count, int* tokens,
+                            long long tok_stride, const int* pos, int prompt_len, int max_ctx, void* stream) {
+  if (!logits || !tokens || !pos || n == 0 || n > 0x7fffffffu || count == 0 || count > 65535 || ld < (long long)n ||
+      tok_stride < max_ctx)
+    return PYRITE_E_SHAPE;
+  return rc(launch_pdl(argmax_rows_kernel, dim3((unsigned)count), dim3(1024), 0, static_cast<cudaStream_t>(stream),
+                       logits, ld, (int)n, tokens, tok_stride, pos, prompt_len, max_ctx));
+}
+
+int pyrite_cuda_advance_pos(int* pos, void* stream) {
+  if (!pos) return PYRITE_E_BUFFER;
+  return rc(launch_pdl(advance_pos_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), pos));
 }
 
 int pyrite_cuda_silu_mul_rows(const float* gate_up, long long ldgu, size_t f, size_t count, float* act, long long lda,

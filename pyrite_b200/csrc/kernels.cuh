@@ -102,6 +102,7 @@ struct ExpertArgs {
   int n_experts, n_sel;
   long long expert_bytes, ws_stride, y_stride;
   int n_ids = 0;  // 0: n_sel (one group)
+  int x_div = 1;  // id index i takes activation i / x_div (top-k selections of one sequence share its x)
 };
 // The activation computed in every CTA's prologue instead of a prepared
 // workspace: mode 1 RMSNorm of src with weight norm, mode 2 silu(src[:cols]) *

@@ -127,6 +127,37 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict_
   pdl_launch_dependents();
 }
 
+// The F32 router product of several sequences: logits[b][e] = sum_c W[e][c] x[b][c]
+// accumulated in fp64 and rounded to fp32 once, as the one-sequence routing
+// launch computes it (one CTA per (expert, sequence)).
+__global__ void __launch_bounds__(256) moe_router_rows_kernel(const float* __restrict__ W, int h,
+                                                              const float* __restrict__ x, long long ldx,
+                                                              float* __restrict__ logits, long long ld) {
+  __shared__ double dshm[32];
+  pdl_wait();
+  const int e = blockIdx.x, b = blockIdx.y;
+  const float* rf = W + (size_t)e * (size_t)h;
+  const float* xb = x + (size_t)b * ldx;
+  double acc = 0.0;
+  for (int c = threadIdx.x; c < h; c += blockDim.x) acc += (double)__ldg(rf + c) * (double)xb[c];
+  const double total = block_sum(acc, dshm);
+  if (threadIdx.x == 0) logits[(size_t)b * ld + e] = (float)total;
+  pdl_launch_dependents();
+}
+
+// moe_route_kernel for row blockIdx.x of a [count x n] logits array: its top_k
+// experts and weights to row blockIdx.x of ids / weights (top_k apart).
+__global__ void __launch_bounds__(256) moe_route_rows_kernel(const float* __restrict__ logits, long long ld,
+                                                             RouteArgs a) {
+  pdl_wait();
+  RouteArgs r = a;
+  r.ids += (size_t)blockIdx.x * a.k;
+  r.weights += (size_t)blockIdx.x * a.k;
+  if (r.global_ids) r.global_ids += (size_t)blockIdx.x * a.k;
+  route_block(logits + (size_t)blockIdx.x * ld, r);
+  pdl_launch_dependents();
+}
+
 // The F32 router matvec and the routing in one launch.  CTA r computes logit
 // r: every thread a strided share of the row in fp64 (the reference's native
 // products accumulate in fp64), one fixed-order block sum, rounded to fp32
@@ -215,6 +246,24 @@ __global__ void __launch_bounds__(256) moe_silu_mul_encode_kernel(const float* _
   pdl_launch_dependents();
 }
 
+// Row b of hidden (ldh apart) += sum_{j < k} w[b k + j] * out[b k + j], j
+// ascending (executor.py:786-792) for each sequence b = blockIdx.y.
+__global__ void __launch_bounds__(256) moe_combine_rows_kernel(const float* __restrict__ out,
+                                                               const float* __restrict__ w, int k, int h,
+                                                               float* __restrict__ hidden, long long ldh) {
+  pdl_wait();
+  const int b = blockIdx.y;
+  const float* ob = out + (size_t)b * k * h;
+  const float* wb = w + (size_t)b * k;
+  float* hb = hidden + (size_t)b * ldh;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < h; i += gridDim.x * blockDim.x) {
+    float acc = hb[i];
+    for (int j = 0; j < k; ++j) acc += wb[j] * ob[(size_t)j * h + i];
+    hb[i] = acc;
+  }
+  pdl_launch_dependents();
+}
+
 // hidden[i] += sum_{j < n_sel} w_j * out[j][i], j ascending (executor.py:786-792).
 __global__ void __launch_bounds__(256) moe_combine_kernel(const float* __restrict__ out, const float* __restrict__ w,
                                                           int n_sel, int h, float* __restrict__ hidden) {
@@ -249,6 +298,41 @@ int pyrite_cuda_moe_route(const float* router_logits, int n_experts, int top_k, 
   RouteArgs a{n_experts, top_k, norm_topk_prob ? 1 : 0, scale, shard_count, shard_index, expert_ids, expert_weights,
               global_ids};
   return rc(launch_pdl(moe_route_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), router_logits, a));
+}
+
+int pyrite_cuda_moe_router_rows(int router_type, const void* router, size_t router_len, size_t hidden,
+                                const float* x, long long ldx, size_t count, float* router_logits, long long ld,
+                                int n_experts, void* stream) {
+  if (router_type != 0) return PYRITE_E_TYPE;  // F32 routers, as the reference keeps them
+  if (!router || !x || !router_logits || n_experts <= 0 || n_experts > 65535 || hidden == 0 ||
+      hidden > 0x7fffffffu || count == 0 || count > 65535 || ldx < (long long)hidden || ld < n_experts)
+    return PYRITE_E_SHAPE;
+  if (router_len != (size_t)n_experts * hidden * 4 || ((uintptr_t)router & 3)) return PYRITE_E_BUFFER;
+  return rc(launch_pdl(moe_router_rows_kernel, dim3((unsigned)n_experts, (unsigned)count), dim3(256), 0,
+                       static_cast<cudaStream_t>(stream), static_cast<const float*>(router), (int)hidden, x, ldx,
+                       router_logits, ld));
+}
+
+int pyrite_cuda_moe_route_rows(const float* router_logits, long long ld, size_t count, int n_experts, int top_k,
+                               int norm_topk_prob, double scale, int* expert_ids, float* expert_weights,
+                               void* stream) {
+  if (!router_logits || !expert_ids || !expert_weights || n_experts <= 0 || n_experts > 4096 || top_k <= 0 ||
+      top_k > 32 || top_k > n_experts || !(scale > 0.0) || count == 0 || count > 65535 || ld < n_experts)
+    return PYRITE_E_SHAPE;
+  RouteArgs a{n_experts, top_k, norm_topk_prob ? 1 : 0, scale, 1, 0, expert_ids, expert_weights, nullptr};
+  return rc(launch_pdl(moe_route_rows_kernel, dim3((unsigned)count), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                       router_logits, ld, a));
+}
+
+int pyrite_cuda_moe_combine_rows(const float* expert_out, const float* expert_weights, size_t top_k, size_t h,
+                                 size_t count, float* hidden, long long ldh, void* stream) {
+  if (!expert_out || !expert_weights || !hidden || top_k == 0 || top_k > 64 || h == 0 || h > 0x7fffffffu ||
+      count == 0 || count > 65535 || ldh < (long long)h)
+    return PYRITE_E_SHAPE;
+  int gx = (int)((h + 255) / 256);
+  if (gx > 64) gx = 64;
+  return rc(launch_pdl(moe_combine_rows_kernel, dim3(gx, (unsigned)count), dim3(256), 0,
+                       static_cast<cudaStream_t>(stream), expert_out, expert_weights, (int)top_k, (int)h, hidden, ldh));
 }
 
 int pyrite_cuda_moe_router_route(int router_type, const void* router, size_t router_len, size_t hidden,
@@ -293,12 +377,41 @@ int pyrite_cuda_matvec_experts(int type_id, const void* stacked, size_t stacked_
                                           workspace, workspace_len, ws_stride, y, y_stride, rows, cols, flags, stream);
 }
 
+namespace {
+// pyrite_cuda_matvec_expert_groups; id index i takes activation i / x_div.
+int expert_groups(int type_id, const void* stacked, size_t stacked_len, size_t n_experts, size_t n_groups,
+                  const int* expert_ids, size_t n_ids, size_t x_div, const float* x, size_t x_stride,
+                  const void* workspace, size_t workspace_len, size_t ws_stride, float* y, size_t y_stride,
+                  size_t rows, size_t cols, unsigned flags, void* stream);
+}  // namespace
+
 int pyrite_cuda_matvec_expert_groups(int type_id, const void* stacked, size_t stacked_len, size_t n_experts,
                                      size_t n_groups, const int* expert_ids, size_t n_ids, const float* x,
                                      size_t x_stride, const void* workspace, size_t workspace_len, size_t ws_stride,
                                      float* y, size_t y_stride, size_t rows, size_t cols, unsigned flags,
                                      void* stream) {
-  if (n_groups == 0 || n_groups > 8) return PYRITE_E_BUFFER;
+  return expert_groups(type_id, stacked, stacked_len, n_experts, n_groups, expert_ids, n_ids, 1, x, x_stride,
+                       workspace, workspace_len, ws_stride, y, y_stride, rows, cols, flags, stream);
+}
+
+int pyrite_cuda_matvec_expert_rows(int type_id, const void* stacked, size_t stacked_len, size_t n_experts,
+                                   size_t n_groups, const int* expert_ids, size_t count, size_t top_k, const float* x,
+                                   size_t x_stride, const void* workspace, size_t workspace_len, size_t ws_stride,
+                                   float* y, size_t y_stride, size_t rows, size_t cols, unsigned flags,
+                                   void* stream) {
+  if (count == 0 || top_k == 0 || top_k > 64 || count > 65535) return PYRITE_E_BUFFER;
+  return expert_groups(type_id, stacked, stacked_len, n_experts, n_groups, expert_ids, count * top_k, top_k, x,
+                       x_stride, workspace, workspace_len, ws_stride, y, y_stride, rows, cols, flags, stream);
+}
+
+}  // extern "C"
+
+namespace {
+int expert_groups(int type_id, const void* stacked, size_t stacked_len, size_t n_experts, size_t n_groups,
+                  const int* expert_ids, size_t n_ids, size_t x_div, const float* x, size_t x_stride,
+                  const void* workspace, size_t workspace_len, size_t ws_stride, float* y, size_t y_stride,
+                  size_t rows, size_t cols, unsigned flags, void* stream) {
+  if (n_groups == 0 || n_groups > 8 || x_div == 0) return PYRITE_E_BUFFER;
   const size_t n_sel = n_ids * n_groups;
   const TypeGeo* t = find_type(type_id);
   if (!t) return PYRITE_E_TYPE;
@@ -307,16 +420,17 @@ int pyrite_cuda_matvec_expert_groups(int type_id, const void* stacked, size_t st
   const size_t rb = cols / t->bs * t->bpb;
   const size_t expert_bytes = rb * rows;
   if (!stacked || !expert_ids || !x || !y || !workspace || n_experts == 0 || n_experts > 0x7fffffffu || n_ids == 0 ||
-      n_sel > 64 || stacked_len != expert_bytes * n_experts * n_groups)
+      n_sel > 1024 || stacked_len != expert_bytes * n_experts * n_groups)
     return PYRITE_E_BUFFER;
   if (y_stride < rows) return PYRITE_E_BUFFER;
   const size_t per = pyrite_cuda_workspace_size(0, cols, 1);
+  const size_t n_x = (n_ids - 1) / x_div + 1;  // activations (and their encodings) read
   if (((uintptr_t)workspace & 255) || (ws_stride && (ws_stride < per || ws_stride % 256)) ||
-      workspace_len < (ws_stride ? ws_stride * (n_ids - 1) + per : per))
+      workspace_len < (ws_stride ? ws_stride * (n_x - 1) + per : per))
     return PYRITE_E_BUFFER;
   const uint8_t* w = static_cast<const uint8_t*>(stacked);
   ExpertArgs ex{expert_ids, (int)n_experts, (int)n_sel, (long long)expert_bytes, (long long)ws_stride,
-                (long long)y_stride, (int)n_ids};
+                (long long)y_stride, (int)n_ids, (int)x_div};
   const bool acc = (flags & PYRITE_F_ACCUMULATE) != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int r;
@@ -331,10 +445,13 @@ int pyrite_cuda_matvec_expert_groups(int type_id, const void* stacked, size_t st
   }
   return r > 0 ? PYRITE_E_CUDA : r;
 }
+}  // namespace
+
+extern "C" {
 
 int pyrite_cuda_moe_silu_mul_encode(const float* gate, const float* up, size_t ff, size_t n_sel, float* act,
                                     void* workspace, size_t workspace_len, void* stream) {
-  if (!gate || !up || !act || !workspace || ff == 0 || ff % 32 || ff > 0x7fffffffu || n_sel == 0 || n_sel > 64)
+  if (!gate || !up || !act || !workspace || ff == 0 || ff % 32 || ff > 0x7fffffffu || n_sel == 0 || n_sel > 1024)
     return PYRITE_E_SHAPE;
   const size_t per = pyrite_cuda_workspace_size(0, ff, 1);
   if (((uintptr_t)workspace & 255) || workspace_len < per * n_sel) return PYRITE_E_BUFFER;

@@ -18,7 +18,7 @@ namespace pyr {
 // ids[j] (expert_bytes apart), x + j * x_stride and y + j * y_stride.
 struct GenericExperts {  // as ExpertArgs: slice j = expert ids[j % n_ids] of group j / n_ids
   const int* ids = nullptr;
-  int n_experts = 0, n_ids = 1;
+  int n_experts = 0, n_ids = 1, x_div = 1;
   long long expert_bytes = 0, x_stride = 0, y_stride = 0;
 };
 
@@ -39,7 +39,7 @@ mv_generic_kernel(const uint8_t* __restrict__ w, size_t row_bytes, int rows, int
     }
     e += (j / ex.n_ids) * ex.n_experts;
     w += (size_t)e * (size_t)ex.expert_bytes;
-    x += (size_t)idn * (size_t)ex.x_stride;
+    x += (size_t)(idn / ex.x_div) * (size_t)ex.x_stride;
     y += (size_t)j * (size_t)ex.y_stride;
   }
   const int lane = threadIdx.x & 31;
@@ -147,6 +147,7 @@ int launch_mv_generic(int type_id, const MatvecArgs<T>& a, cudaStream_t stream, 
     ex.ids = experts->ids;
     ex.n_experts = experts->n_experts;
     ex.n_ids = experts->n_ids > 0 ? experts->n_ids : experts->n_sel;
+    ex.x_div = experts->x_div > 0 ? experts->x_div : 1;
     ex.expert_bytes = experts->expert_bytes;
     ex.x_stride = x_stride;
     ex.y_stride = experts->y_stride;

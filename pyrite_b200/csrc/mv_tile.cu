@@ -571,6 +571,7 @@ struct TileArgs {
   const int* experts;
   int n_experts, n_sel, n_ids;
   long long expert_bytes, ws_stride, y_stride;
+  int x_div;  // id index i takes prepared x number i / x_div
   // x prologue (xmode != 0): every CTA encodes its own copy of x into shared
   // memory from fp32 input instead of reading a prepared workspace --
   // 1: x = xsrc * xnorm / rms(xsrc) (fp64 statistics), 2: x = silu(xsrc[0:cols])
@@ -733,7 +734,7 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
   if (!early && tid == 0)
     for (int k = 0; k < min(my, S - 1); ++k) issue(k);
 
-  const uint8_t* xws = a.ws + (size_t)(a.experts ? sel % a.n_ids : 0) * (size_t)a.ws_stride;
+  const uint8_t* xws = a.ws + (size_t)(a.experts ? (sel % a.n_ids) / a.x_div : 0) * (size_t)a.ws_stride;
   if (a.xmode) {  // this CTA's own encoding of x (the input was written by the preceding kernel)
     __shared__ double xshm[32];
     uint8_t* enc = smem + a.xenc_off;
@@ -830,7 +831,7 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kerne
     // (x's encoding is located again from the arguments, so no pointer to it
     // stays live through the streaming loop)
     const uint8_t* xe = a.xmode ? smem + a.xenc_off
-                                : a.ws + (size_t)(a.experts ? sel % a.n_ids : 0) * (size_t)a.ws_stride;
+                                : a.ws + (size_t)(a.experts ? (sel % a.n_ids) / a.x_div : 0) * (size_t)a.ws_stride;
     wide_pass<TY>(wb, a.row_bytes, a.cols, reinterpret_cast<const float*>(xe + 2LL * a.cols), xe + x2_offset(a.cols),
                   yb, cta, ncta, rows_per_stage, a.rows, my, reinterpret_cast<int*>(smem));
     __syncthreads();
@@ -972,7 +973,7 @@ int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, in
   const size_t xenc = xp ? ((lane_workspace_bytes(cols) + 255) & ~(size_t)255) : 0;
   const TilePlan p = plan_tile(row_bytes, rows, cols, vals, xenc);
   TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs_log2, p.m, p.stage_bytes, static_weights ? 1 : 0,
-              accumulate ? 1 : 0, post ? *post : PostArgs{}, nullptr, 0, 0, 0, 0, 0, 0,
+              accumulate ? 1 : 0, post ? *post : PostArgs{}, nullptr, 0, 0, 0, 0, 0, 0, 1,
               xp ? xp->mode : 0, xp ? xp->src : nullptr, xp ? xp->norm : nullptr, xp ? xp->eps : 0.0,
               xp ? xp->out : nullptr, p.xenc_off};
   if (ex) {
@@ -980,6 +981,7 @@ int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, in
     ta.n_experts = ex->n_experts;
     ta.n_sel = ex->n_sel;
     ta.n_ids = ex->n_ids > 0 ? ex->n_ids : ex->n_sel;
+    ta.x_div = ex->x_div > 0 ? ex->x_div : 1;
     ta.expert_bytes = ex->expert_bytes;
     ta.ws_stride = ex->ws_stride;
     ta.y_stride = ex->y_stride;

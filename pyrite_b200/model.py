@@ -423,7 +423,8 @@ class MixedDecoder:
         for p0 in range(0, n, B):
             c = min(B, n - p0)
             _check(L.pyrite_cuda_embed_rows(self.embd.ggml_type, self.embd.data.data_ptr(), s.vocab_size, h,
-                                            self.tokens[p0:].data_ptr(), c, hid.data_ptr(), h, st), "embed rows")
+                                            self.tokens[p0:].data_ptr(), 1, None, c, hid.data_ptr(), h, st),
+                   "embed rows")
             for li, ly in enumerate(self.layers):
                 _check(L.pyrite_cuda_rmsnorm_rows(hid.data_ptr(), h, ly.attn_norm.data_ptr(), h, c, eps,
                                                   nrm.data_ptr(), h, st), "rmsnorm rows")
@@ -432,12 +433,12 @@ class MixedDecoder:
                 _check(L.pyrite_cuda_qk_rope_kv_rows(
                     qkv.data_ptr(), q + 2 * kv, ly.q_norm.data_ptr() if ly.q_norm is not None else None,
                     ly.k_norm.data_ptr() if ly.k_norm is not None else None, s.num_attention_heads,
-                    s.num_key_value_heads, s.head_dim, eps, p0, c, self.rope.data_ptr(), self.max_ctx, qr.data_ptr(), q,
-                    self.kcache[li].data_ptr(), self.vcache[li].data_ptr(), st), "qk rope kv rows")
+                    s.num_key_value_heads, s.head_dim, eps, p0, None, 1, 0, c, self.rope.data_ptr(), self.max_ctx,
+                    qr.data_ptr(), q, self.kcache[li].data_ptr(), self.vcache[li].data_ptr(), st), "qk rope kv rows")
                 _check(L.pyrite_cuda_attention_rows(qr.data_ptr(), q, self.kcache[li].data_ptr(),
-                                                    self.vcache[li].data_ptr(), p0, c, s.num_attention_heads,
-                                                    s.num_key_value_heads, s.head_dim, self.max_ctx, att.data_ptr(), q,
-                                                    st), "attention rows")
+                                                    self.vcache[li].data_ptr(), 0, p0, None, 1, c,
+                                                    s.num_attention_heads, s.num_key_value_heads, s.head_dim,
+                                                    self.max_ctx, att.data_ptr(), q, st), "attention rows")
                 self._mm(ly.o, att, q, hid, h, c, ws, ACCUMULATE, st)
                 if li == last:
                     continue

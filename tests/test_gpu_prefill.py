@@ -137,8 +137,8 @@ def test_qk_rope_kv_rows_and_causal_attention(cuda_device, nq, nkv, first, count
     rope = torch.from_numpy(rope_table(max_ctx, theta)).cuda()
     qr = torch.empty(count, nq * HD, device="cuda")
     assert lib.pyrite_cuda_qk_rope_kv_rows(qkv.data_ptr(), (nq + 2 * nkv) * HD, qn.data_ptr(), kn.data_ptr(), nq, nkv,
-                                           HD, eps, first, count, rope.data_ptr(), max_ctx, qr.data_ptr(), nq * HD,
-                                           kc.data_ptr(), vc.data_ptr(), st) == 0
+                                           HD, eps, first, None, 1, 0, count, rope.data_ptr(), max_ctx, qr.data_ptr(),
+                                           nq * HD, kc.data_ptr(), vc.data_ptr(), st) == 0
     qref = torch.empty(nq * HD, device="cuda")
     for j in range(count):
         p = torch.tensor([first + j], dtype=torch.int32, device="cuda")
@@ -149,8 +149,8 @@ def test_qk_rope_kv_rows_and_causal_attention(cuda_device, nq, nkv, first, count
         assert torch.equal(qr[j], qref)
     assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
     out = torch.empty(count, nq * HD, device="cuda")
-    assert lib.pyrite_cuda_attention_rows(qr.data_ptr(), nq * HD, kc.data_ptr(), vc.data_ptr(), first, count, nq, nkv,
-                                          HD, max_ctx, out.data_ptr(), nq * HD, st) == 0
+    assert lib.pyrite_cuda_attention_rows(qr.data_ptr(), nq * HD, kc.data_ptr(), vc.data_ptr(), 0, first, None, 1, count,
+                                          nq, nkv, HD, max_ctx, out.data_ptr(), nq * HD, st) == 0
     torch.cuda.synchronize()
     K, V, Q, O = (t.double().cpu().numpy() for t in (kc, vc, qr, out))
     grp = nq // nkv
