@@ -628,6 +628,11 @@ def model_leg(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
     if pg:  # the NVLink sum's peer mappings, after every rank's last step
         pg.barrier()
         dec.close()
+    batch16 = None
+    if which == "c4" and world == 1:  # configs[3] also decodes 16 sequences at once
+        del dec
+        torch.cuda.empty_cache()
+        batch16 = batch_leg(dev, spec, prefill, new)
     out = {"config": cfg, "decode_tok_s": round(1000.0 / ms_tok, 1), "ms_per_token": round(ms_tok, 4),
            "prefill_tok_s": round((prefill - 1) * 1000.0 / pre_ms, 1),
            "prefill": ("blocks of 64 positions, projections on the tensor cores (MixedDecoder.prefill)" if batched
@@ -638,7 +643,44 @@ def model_leg(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
            "hbm_frac_of_measured": round(active / (ms_tok * 1e-3) / 1e9 / (measured_peak()[0] * world), 4),
            "weights": "layers 0-1 generated from seeds (N(0,0.02) quantized), deeper layers: own HBM copies of them",
            "host_build_seconds": round(built, 1)}
+    if batch16 is not None:
+        out["batch16"] = batch16
+    else:
+        del dec
+    return out
+
+
+def batch_leg(dev, spec, prefill: int, new: int, batch: int = 16) -> dict:
+    """configs[3] at batch 16: 16 sequences (seeded prompts of `prefill` ids)
+    decoded together (pyrite_b200.batch.BatchDecoder: one multi-column product
+    per projection for all sequences, per-row routing, every (sequence,
+    expert) selection in one launch); the prompts run one position per step for
+    all sequences at once.  CUDA events around the decode steps."""
+    import torch
+
+    from pyrite_b200.batch import BatchDecoder
+    dec = BatchDecoder.synthetic(spec, device=dev, max_ctx=prefill + new, batch=batch, replicate=True)
+    rng = np.random.default_rng(SEED + batch)
+    prompts = [list(map(int, rng.integers(0, spec.vocab_size, prefill))) for _ in range(batch)]
+    dec.breset(prompts)
+    dec.bcapture()
+    dec.breset(prompts)
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize(dev)
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record(stream)
+    dec.brun_steps(prefill - 1)
+    e1.record(stream)
+    dec.brun_steps(new)
+    e2.record(stream)
+    torch.cuda.synchronize(dev)
+    dec.check_status()
+    ms_tok = e1.elapsed_time(e2) / new
+    out = {"batch": batch, "decode_tok_s": round(batch * 1000.0 / ms_tok, 1), "ms_per_step": round(ms_tok, 4),
+           "prefill_tok_s": round(batch * (prefill - 1) * 1000.0 / e0.elapsed_time(e1), 1),
+           "note": "16 seeded prompts of equal length; tok/s counts every sequence's tokens"}
     del dec
+    torch.cuda.empty_cache()
     return out
 
 

@@ -38,8 +38,8 @@ from .model import ACCUMULATE, MixedDecoder, _Mat
 class BatchDecoder(MixedDecoder):
     """``batch`` sequences of one checkpoint, decoded greedily together."""
 
-    def __init__(self, spec, tensors, device="cuda", max_ctx: int = 512, batch: int = 16):
-        super().__init__(spec, tensors, device=device, max_ctx=max_ctx)
+    def __init__(self, spec, tensors, device="cuda", max_ctx: int = 512, batch: int = 16, replicate: bool = False):
+        super().__init__(spec, tensors, device=device, max_ctx=max_ctx, replicate=replicate)
         if not 1 <= batch <= 128:
             raise ValueError("batch must be 1..128")
         s, L, d = self.spec, self.lib, self.dev
@@ -72,11 +72,17 @@ class BatchDecoder(MixedDecoder):
         self.bprompt_len = 0
 
     @classmethod
-    def synthetic(cls, spec, device="cuda", max_ctx: int = 512, batch: int = 16) -> "BatchDecoder":
+    def synthetic(cls, spec, device="cuda", max_ctx: int = 512, batch: int = 16,
+                  replicate: bool = False) -> "BatchDecoder":
+        """The seeded synthetic checkpoint of ``spec``; ``replicate``: layers 0
+        and 1 generated, deeper layers their own device copies of those bytes."""
+        from dataclasses import replace
+
         from .synthetic import MoESpec, dense_tensors, moe_tensors
+        gen_spec = replace(spec, num_hidden_layers=min(2, spec.num_hidden_layers)) if replicate else spec
         gen = moe_tensors if isinstance(spec, MoESpec) else dense_tensors
-        tensors = {name: (dims, t, payload) for name, dims, t, payload in gen(spec)}
-        return cls(spec, tensors, device=device, max_ctx=max_ctx, batch=batch)
+        tensors = {name: (dims, t, payload) for name, dims, t, payload in gen(gen_spec)}
+        return cls(spec, tensors, device=device, max_ctx=max_ctx, batch=batch, replicate=replicate)
 
     @staticmethod
     def _aligned(buf: torch.Tensor) -> tuple[int, int]:
