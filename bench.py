@@ -388,27 +388,32 @@ def run_ours(args) -> None:
 def strong_leg(dev, W, X, Y, wl, stream, pg, world: int, rank: int, steps: int, warmup: int) -> dict:
     """The same step with every matrix's rows split over the GPUs (rank k
     multiplies rows [k r / N, (k + 1) r / N), the row range of the reference's
-    executor call, executor.py:481-509) and the full outputs assembled on every
-    GPU by an NCCL all_gather per matrix: total work fixed as N grows.  Time:
-    CUDA events around `steps` replays of one graph, max over ranks.  The
-    gathered rows must equal the one-GPU rows bit for bit (any row partition
-    gives the same bits)."""
+    executor call, executor.py:481-509) and the outputs assembled on every GPU
+    by one NCCL all_gather of all matrices' row slices: total work fixed as N
+    grows.  Time: CUDA events around `steps` replays of one graph, max over
+    ranks.  The gathered rows must equal the one-GPU rows bit for bit (any row
+    partition gives the same bits)."""
     import torch
 
     from pyrite_b200.kernels import cuda as K
-    parts = {}
+    offs, total, parts = {}, 0, {}
+    for _, t, r, c in wl:
+        offs[(t, r, c)] = total
+        total += r // world
+    local = torch.empty(total, device=dev)            # this rank's rows of every matrix
+    gathered = torch.empty(world * total, device=dev)  # rank-major: every rank's rows
     for _, t, r, c in wl:
         rr, rb = r // world, row_bytes(t, c)
-        parts[(t, r, c)] = (W[(t, r, c)][rank * rr * rb:(rank + 1) * rr * rb], torch.empty(rr, device=dev),
-                            torch.empty(r, device=dev), rr)
+        o = offs[(t, r, c)]
+        parts[(t, r, c)] = (W[(t, r, c)][rank * rr * rb:(rank + 1) * rr * rb], local[o:o + rr], rr)
     WS = {c: torch.empty(K.workspace_size(0, c) + 256, dtype=torch.uint8, device=dev) for c in X}
 
     def step():
         px = {c: K.prepare_x(X[c], workspace=WS[c]) for c in X}
         for _, t, r, c in wl:
-            w, yl, ya, rr = parts[(t, r, c)]
+            w, yl, rr = parts[(t, r, c)]
             K.matvec_prepared(t, w, px[c], rr, c, out=yl, static_weights=True)
-            pg.all_gather_into_tensor(ya, yl)
+        pg.all_gather_into_tensor(gathered, local)
 
     with torch.cuda.stream(stream):
         step()
@@ -430,14 +435,16 @@ def strong_leg(dev, W, X, Y, wl, stream, pg, world: int, rank: int, steps: int, 
     torch.cuda.synchronize()
     t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
     pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    same = torch.tensor([int(all(torch.equal(parts[k][2], Y[k]) for k in parts))], device=dev)
+    g = gathered.view(world, total)
+    same = int(all(torch.equal(g[:, offs[k]:offs[k] + k[1] // world].reshape(-1), Y[k]) for k in offs))
+    same = torch.tensor([same], device=dev)
     pg.all_reduce(same, op=pg.ReduceOp.MIN)
     ms = float(t.item())
     step_bytes = sum(algo_bytes(t_, r, c) for _, t_, r, c in wl)
     del graph
     return {"value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 5),
             "n_gpus": world, "scaling": "strong", "steps": steps,
-            "parallelism": f"rows of every matrix split over {world} GPUs, NCCL all_gather of each output",
+            "parallelism": f"rows of every matrix split over {world} GPUs, one NCCL all_gather of all row slices",
             "rows_bit_identical_to_one_gpu": bool(same.item())}
 
 
