@@ -432,8 +432,8 @@ struct UnitQ6K {
 };
 
 // IQ4_XS: d | scales_h | scales_l[4] | qs[128]  (native.c:364-379).  Unit j
-// is sub-block j.  Codes index the non-linear book through a 16-entry byte
-// table (two 8-entry permutes and a select on bit 3); looked-up bytes come out
+// is sub-block j.  Codes index the non-linear book through two 8-entry byte
+// permutes whose results sum to the book value (below); looked-up bytes come out
 // in the order [lo0, hi0, lo1, hi1], so the x digits are interleaved the same
 // way once, when they are loaded.  8-byte aligned blocks.
 struct UnitIQ4XS {
@@ -456,21 +456,29 @@ struct UnitIQ4XS {
     const uint2 hdr = lds64(blk);  // d | scales_h | scales_l[4]
     const uint2 q01 = lds64(blk + 8 + 16 * j), q23 = lds64(blk + 16 + 16 * j);
     const uint32_t qw[4] = {q01.x, q01.y, q23.x, q23.y};
-    // the book as int8: -127 -104 -83 -65 -49 -35 -22 -10 | 1 13 25 38 53 69 89 113
-    const uint32_t T0 = 0xBFAD9881u, T1 = 0xF6EADDCFu, T2 = 0x26190D01u, T3 = 0x71594535u;
+    // The book as int8: -127 -104 -83 -65 -49 -35 -22 -10 | 1 13 25 38 53 69 89 113.
+    // A code used directly as a prmt selector into the lower half (all
+    // negative) gives book[code] for codes 0-7 and -1 (the replicated sign)
+    // for codes 8-15; the code with bit 3 flipped, into the upper half plus
+    // one (all positive), gives 0 for codes 0-7 and book[code] + 1 for 8-15.
+    // The two byte vectors sum to book[code], and dp4a is linear, so each
+    // goes to dp4a as it is: two permutes per four codes and no select.
+    constexpr uint32_t N0 = 0xBFAD9881u, N1 = 0xF6EADDCFu;  // book[0..7]
+    constexpr uint32_t P0 = 0x271A0E02u, P1 = 0x725A4636u;  // book[8..15] + 1
     int a = 0, b = 0, a1 = 0, b1 = 0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      // the selectors of all 8 nibbles at once (prmt reads the low 16 bits):
-      // bits 0-2 index a half of the book, bit 3 picks the half
-      const uint32_t sel = qw[k] & 0x77777777u, pick = ((qw[k] >> 1) & 0x44444444u) | 0x32103210u;
-      const uint32_t v0 = __byte_perm(__byte_perm(T0, T1, sel), __byte_perm(T2, T3, sel), pick);
-      const uint32_t sel1 = sel >> 16, pick1 = pick >> 16;
-      const uint32_t v1 = __byte_perm(__byte_perm(T0, T1, sel1), __byte_perm(T2, T3, sel1), pick1);
-      a = __dp4a((int)v0, (int)u.a[2 * k], a);
-      b = __dp4a((int)v0, (int)u.b[2 * k], b);
-      a1 = __dp4a((int)v1, (int)u.a[2 * k + 1], a1);
-      b1 = __dp4a((int)v1, (int)u.b[2 * k + 1], b1);
+      const uint32_t q = qw[k], f = q ^ 0x88888888u;  // prmt reads a selector's low 16 bits
+      const uint32_t n0 = prmt_sx(N0, N1, q), p0 = prmt_sx(P0, P1, f);
+      const uint32_t n1 = prmt_sx(N0, N1, q >> 16), p1 = prmt_sx(P0, P1, f >> 16);
+      a = __dp4a((int)n0, (int)u.a[2 * k], a);
+      b = __dp4a((int)n0, (int)u.b[2 * k], b);
+      a1 = __dp4a((int)n1, (int)u.a[2 * k + 1], a1);
+      b1 = __dp4a((int)n1, (int)u.b[2 * k + 1], b1);
+      a = __dp4a((int)p0, (int)u.a[2 * k], a);
+      b = __dp4a((int)p0, (int)u.b[2 * k], b);
+      a1 = __dp4a((int)p1, (int)u.a[2 * k + 1], a1);
+      b1 = __dp4a((int)p1, (int)u.b[2 * k + 1], b1);
     }
     a += a1;
     b += b1;
@@ -585,7 +593,12 @@ struct TileArgs {
 };
 
 // CTAs per SM each format's register budget allows (launch bounds).
-template <int TY> constexpr int tile_min_blocks() { return (TY == Q6_K || TY == kQ6KRealign) ? 2 : 3; }
+// CTAs per SM the register budget is sized for (65,536 / (256 * this)): Q6_K
+// and every lane holding two or more units need more than 80 registers, and
+// their stages (32 KB for the 4096 x 14336 shapes) fit two CTAs per SM anyway.
+template <int TY, int UL> constexpr int tile_min_blocks() {
+  return (TY == Q6_K || TY == kQ6KRealign || UL >= 2) ? 2 : 3;
+}
 
 // The part of 32 weights (unit u of block b) that the streaming loop multiplies
 // by the encoded x: d*sc*q, without the offsets it applies to the exact fp32
@@ -669,7 +682,7 @@ __device__ __forceinline__ void wide_pass(const uint8_t* wb, size_t row_bytes, i
 }
 
 template <int TY, int UL, int M>
-__global__ void __launch_bounds__(kThreads, tile_min_blocks<TY>()) mv_tile_kernel(TileArgs a, int* status) {
+__global__ void __launch_bounds__(kThreads, tile_min_blocks<TY, UL>()) mv_tile_kernel(TileArgs a, int* status) {
   using U = typename UnitOf<TY>::T;
   constexpr int BPB = Geo<TY>::bpb, S = kStages;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -907,7 +920,7 @@ int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
   const int rows_per_stage = M << ta.rs_log2;
   const int nstages = (ta.rows + rows_per_stage - 1) / rows_per_stage;
   int per_sm = (int)((227 * 1024) / (smem + 1024));
-  const int minb = tile_min_blocks<TY>();
+  const int minb = tile_min_blocks<TY, UL>();
   if (per_sm > minb) per_sm = minb;
   if (per_sm < 1) per_sm = 1;
   int grid = nsm * per_sm;

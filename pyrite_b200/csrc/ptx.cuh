@@ -36,6 +36,16 @@ __device__ __forceinline__ void sts32f(uint32_t a, float v) {
   asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
 }
 
+// prmt.b32 in its generic mode: each selector nibble's bits 0-2 pick one of the
+// eight bytes {b, a} (a = bytes 0-3), and its bit 3, when set, replicates the
+// sign bit of that byte over the result byte instead of copying it.  The low 16
+// bits of `sel` are read.
+__device__ __forceinline__ uint32_t prmt_sx(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
 // ---- mbarriers ----------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
