@@ -497,6 +497,7 @@ template <> struct UnitOf<Q6_K> { using T = UnitQ6K<false>; };
 template <> struct UnitOf<kQ6KRealign> { using T = UnitQ6K<true>; };
 template <> struct UnitOf<IQ4_XS> { using T = UnitIQ4XS; };
 
+// a tile CTA has up to kThreads threads (rs row slots of lps lanes, tile plan)
 constexpr int kThreads = 256, kWarps = 8, kMaxRowsPerStage = 64, kStages = 3;
 constexpr size_t kMaxTileSmem = 150 * 1024;  // dynamic shared memory a tile CTA may take
 
@@ -509,7 +510,7 @@ __device__ void run_post(const PostArgs& p, const float* y, int n, float best_v,
   __shared__ float bv[32];
   __shared__ int bi[32];
   __shared__ int last;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
   if (p.op == kPostArgmax) {  // this CTA's best row -> its partial slot
     warp_best(best_v, best_i);
     if (lane == 0) {
@@ -518,8 +519,8 @@ __device__ void run_post(const PostArgs& p, const float* y, int n, float best_v,
     }
     __syncthreads();
     if (warp == 0) {
-      best_v = lane < kWarps ? bv[lane] : -FLT_MAX;
-      best_i = lane < kWarps ? bi[lane] : 0x7fffffff;
+      best_v = lane < nw ? bv[lane] : -FLT_MAX;
+      best_i = lane < nw ? bi[lane] : 0x7fffffff;
       warp_best(best_v, best_i);
       if (lane == 0) {
         p.pv[blockIdx.x] = best_v;
@@ -538,11 +539,11 @@ __device__ void run_post(const PostArgs& p, const float* y, int n, float best_v,
   if (p.op == kPostRmsnormEncode) {
     block_rmsnorm_encode(y, p.w, n, p.eps, p.out, p.ws, shm);
   } else if (p.op == kPostSiluMulEncode) {
-    warps_silu_mul_encode(y, n / 2, p.out, p.ws, warp, kWarps);
+    warps_silu_mul_encode(y, n / 2, p.out, p.ws, warp, nw);
   } else if (p.op == kPostArgmax) {
     float v = -FLT_MAX;
     int idx = 0x7fffffff;
-    for (int c = tid; c < (int)gridDim.x; c += kThreads) better(v, idx, __ldcg(p.pv + c), __ldcg(p.pi + c));
+    for (int c = tid; c < (int)gridDim.x; c += (int)blockDim.x) better(v, idx, __ldcg(p.pv + c), __ldcg(p.pi + c));
     warp_best(v, idx);
     if (lane == 0) {
       bv[warp] = v;
@@ -550,7 +551,7 @@ __device__ void run_post(const PostArgs& p, const float* y, int n, float best_v,
     }
     __syncthreads();
     if (tid == 0) {
-      for (int w = 1; w < kWarps; ++w) better(v, idx, bv[w], bi[w]);
+      for (int w = 1; w < nw; ++w) better(v, idx, bv[w], bi[w]);
       const int q = *p.pos;
       if (q + 1 < p.max_ctx && q + 1 >= p.prompt_len) p.tokens[q + 1] = idx;
       *p.pos = q + 1;
@@ -565,7 +566,7 @@ struct TileArgs {
   int rows, cols;
   const uint8_t* ws;  // prepared x
   float* y;
-  int rs_log2;      // row slots rs = 1 << rs_log2 (lanes per slot = 256 / rs, a multiple of 32)
+  int rs, lps;      // rs row slots of lps lanes (a multiple of 32); the CTA has rs * lps threads
   int m;            // rows per slot per stage
   int stage_bytes;  // shared bytes per stage (rs*m rows + alignment slack)
   int static_weights;
@@ -646,7 +647,7 @@ __device__ __forceinline__ void wide_pass(const uint8_t* wb, size_t row_bytes, i
                                           int* list) {
   constexpr int DT = TY == kQ6KRealign ? (int)Q6_K : TY;  // the format the realigning kernel reads
   constexpr int BS = Geo<DT>::bs, BPB = Geo<DT>::bpb, UPB = BS / 32;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nblk = cols / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5, nblk = cols / 32;
   if (warp == 0) {
     int n = 0;
     for (int b0 = 0; b0 < nblk; b0 += 32) {
@@ -660,7 +661,7 @@ __device__ __forceinline__ void wide_pass(const uint8_t* wb, size_t row_bytes, i
   }
   __syncthreads();
   const int n = list[0];
-  for (int idx = warp; idx < my * rps; idx += kWarps) {
+  for (int idx = warp; idx < my * rps; idx += nw) {
     const int row = (cta + (idx / rps) * ncta) * rps + idx % rps;
     if (row >= rows) continue;  // warp-uniform
     const uint8_t* rp = wb + (size_t)row * row_bytes;
@@ -689,9 +690,8 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY, UL>()) mv_tile_k
   float* red = reinterpret_cast<float*>(smem + (size_t)S * a.stage_bytes);  // [2][kWarps][M]
   uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * kWarps * M);        // [S] full barriers
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int lps_log2 = 8 - a.rs_log2, lps = 1 << lps_log2;
-  const int slot = tid >> lps_log2, ls = tid & (lps - 1);
-  const int rows_per_stage = M << a.rs_log2;
+  const int lps = a.lps, slot = tid / lps, ls = tid - slot * lps;
+  const int rows_per_stage = M * a.rs;
   const int nstages = (a.rows + rows_per_stage - 1) / rows_per_stage;
   const int units = a.cols / U::VALS;
   // routed experts: CTA group `sel` takes stacked matrix a.experts[sel]
@@ -860,17 +860,20 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY, UL>()) mv_tile_k
   if (a.post.op != kPostNone) run_post(a.post, a.y, a.rows, best_v, best_i);
 }
 
-struct TilePlan { int rs_log2, m, stage_bytes, ul; size_t smem; int xenc_off; };
+struct TilePlan { int rs, lps, m, stage_bytes, ul; size_t smem; int xenc_off; };
 
 TilePlan plan_tile(size_t row_bytes, int rows, int cols, int vals, size_t xenc_bytes) {
   TilePlan p{};
   const int units = cols / vals;
-  int pow2 = 32;
-  while (pow2 < units && pow2 < kThreads) pow2 *= 2;
-  const int rs = kThreads / pow2;  // row slots: 1..8, each 32..256 lanes
-  p.rs_log2 = rs == 8 ? 3 : rs == 4 ? 2 : rs == 2 ? 1 : 0;
-  const int lps = kThreads / rs;
-  p.ul = (units + lps - 1) / lps;
+  // a row's units over lps lanes, ul units per lane; lps is the smallest
+  // multiple of 32 that holds them, so no warp of a slot is idle and at most
+  // 31 lanes are (14336 columns: 224 or 448 units -> 224 lanes, 7 warps);
+  // rs slots of rows side by side fill up to kThreads threads
+  p.ul = (units + kThreads - 1) / kThreads;
+  p.lps = 32 * (((units + p.ul - 1) / p.ul + 31) / 32);
+  p.rs = kThreads / p.lps;
+  if (p.rs > 8) p.rs = 8;
+  const int rs = p.rs;
   // rows per slot per stage (1, 2, 4 or 8): stages of up to 32 KB amortise the
   // per-stage barrier, copy issue and row reduction; 3 slots keep 2 in flight.
   // A matrix too small for a full wave of such stages keeps 20 KB stages, so
@@ -917,7 +920,7 @@ int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
     smem_set[dev].store(true, std::memory_order_release);
   }
   if (smem > (size_t)kMaxSmem) return 1;
-  const int rows_per_stage = M << ta.rs_log2;
+  const int rows_per_stage = M * ta.rs;
   const int nstages = (ta.rows + rows_per_stage - 1) / rows_per_stage;
   int per_sm = (int)((227 * 1024) / (smem + 1024));
   const int minb = tile_min_blocks<TY, UL>();
@@ -932,7 +935,8 @@ int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
   } else if (grid > nstages) {
     grid = nstages;
   }
-  return launch_pdl(mv_tile_kernel<TY, UL, M>, dim3(grid), dim3(kThreads), smem, stream, ta, device_status_word());
+  return launch_pdl(mv_tile_kernel<TY, UL, M>, dim3(grid), dim3(ta.rs * ta.lps), smem, stream, ta,
+                    device_status_word());
 }
 
 template <int TY>
@@ -985,7 +989,7 @@ int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, in
   const int vals = (type_id == Q6_K || type_id == Q4_K || type_id == Q5_K) ? 64 : 32;
   const size_t xenc = xp ? ((lane_workspace_bytes(cols) + 255) & ~(size_t)255) : 0;
   const TilePlan p = plan_tile(row_bytes, rows, cols, vals, xenc);
-  TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs_log2, p.m, p.stage_bytes, static_weights ? 1 : 0,
+  TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs, p.lps, p.m, p.stage_bytes, static_weights ? 1 : 0,
               accumulate ? 1 : 0, post ? *post : PostArgs{}, nullptr, 0, 0, 0, 0, 0, 0, 1,
               xp ? xp->mode : 0, xp ? xp->src : nullptr, xp ? xp->norm : nullptr, xp ? xp->eps : 0.0,
               xp ? xp->out : nullptr, p.xenc_off};
