@@ -22,7 +22,8 @@
 //    of a row, so it loads its x digits once, into registers, for the whole
 //    kernel.  Only weights move per row.
 //  * Weights are staged through a ring of S shared-memory stages; a stage is
-//    RS*M consecutive rows, i.e. one contiguous byte range of up to ~32 KB,
+//    RS*M consecutive rows, i.e. one contiguous byte range: 3 stages of up to
+//    ~32 KB, or 2 of up to ~48 KB where that doubles the rows per stage,
 //    fetched by ONE TMA bulk copy (cp.async.bulk) that completes on the
 //    slot's mbarrier.  (Measured on B200: bulk copies below ~4 KB cannot
 //    saturate HBM, 16 KB copies stream at ~7 TB/s.)  Lanes then decode their
@@ -498,7 +499,7 @@ template <> struct UnitOf<kQ6KRealign> { using T = UnitQ6K<true>; };
 template <> struct UnitOf<IQ4_XS> { using T = UnitIQ4XS; };
 
 // a tile CTA has up to kThreads threads (rs row slots of lps lanes, tile plan)
-constexpr int kThreads = 256, kWarps = 8, kMaxRowsPerStage = 64, kStages = 3;
+constexpr int kThreads = 256, kWarps = 8, kMaxRowsPerStage = 64, kMaxStages = 3;
 constexpr size_t kMaxTileSmem = 150 * 1024;  // dynamic shared memory a tile CTA may take
 
 // The last CTA to finish (a ticket counter, no waiting) runs one operation on
@@ -569,6 +570,7 @@ struct TileArgs {
   int rs, lps;      // rs row slots of lps lanes (a multiple of 32); the CTA has rs * lps threads
   int m;            // rows per slot per stage
   int stage_bytes;  // shared bytes per stage (rs*m rows + alignment slack)
+  int slots;        // stages in the ring (2 or 3)
   int static_weights;
   int accumulate;   // y += W x (a residual stream) instead of y = W x
   PostArgs post;    // operation run on the whole y by the last CTA to finish
@@ -685,7 +687,8 @@ __device__ __forceinline__ void wide_pass(const uint8_t* wb, size_t row_bytes, i
 template <int TY, int UL, int M>
 __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY, UL>()) mv_tile_kernel(TileArgs a, int* status) {
   using U = typename UnitOf<TY>::T;
-  constexpr int BPB = Geo<TY>::bpb, S = kStages;
+  constexpr int BPB = Geo<TY>::bpb;
+  const int S = a.slots;
   extern __shared__ __align__(128) uint8_t smem[];
   float* red = reinterpret_cast<float*>(smem + (size_t)S * a.stage_bytes);  // [2][kWarps][M]
   uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * kWarps * M);        // [S] full barriers
@@ -706,16 +709,17 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY, UL>()) mv_tile_k
   const size_t stage_stride = (size_t)rows_per_stage * a.row_bytes;
 
   auto stage_rows = [&](int st) { return min(rows_per_stage, a.rows - st * rows_per_stage); };
-  // the CTA's k-th stage -> ring slot k % S, one bulk copy of its contiguous bytes
-  auto issue = [&](int k) {  // thread 0
+  // the CTA's k-th stage -> ring slot `rs_i` (= k % S, known to the caller
+  // without a division), one bulk copy of its contiguous bytes
+  auto issue = [&](int k, int rs_i) {  // thread 0
     const int st = cta + k * ncta;
     if (st >= nstages) return;
     const uintptr_t src = (uintptr_t)wb + (uintptr_t)st * stage_stride;
     const uintptr_t al = src & ~(uintptr_t)15;
     const uint32_t len = (uint32_t)(((src - al) + (uintptr_t)stage_rows(st) * a.row_bytes + 15) & ~(uintptr_t)15);
-    const uint32_t bar = smem_addr(&bars[k % S]);
+    const uint32_t bar = smem_addr(&bars[rs_i]);
     mbar_expect_tx(bar, len);
-    bulk_g2s(ring + (uint32_t)((k % S) * a.stage_bytes), reinterpret_cast<const void*>(al), len, bar);
+    bulk_g2s(ring + (uint32_t)(rs_i * a.stage_bytes), reinterpret_cast<const void*>(al), len, bar);
   };
 
   const int my = cta < nstages ? (nstages - 1 - cta) / ncta + 1 : 0;
@@ -728,7 +732,7 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY, UL>()) mv_tile_k
   // the preceding kernel drains; x and y are touched only after pdl_wait().
   const bool early = a.static_weights && !a.experts;
   if (early && tid == 0)
-    for (int k = 0; k < min(my, S - 1); ++k) issue(k);
+    for (int k = 0; k < min(my, S - 1); ++k) issue(k, k);
   pdl_wait();
   pdl_launch_dependents();
   if (a.experts) {  // written by the routing kernel this one waited for
@@ -745,7 +749,7 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY, UL>()) mv_tile_k
   const int wmod4 = (int)((uintptr_t)wb & 3);
   float* const yb = a.y + (size_t)sel * (size_t)a.y_stride;
   if (!early && tid == 0)
-    for (int k = 0; k < min(my, S - 1); ++k) issue(k);
+    for (int k = 0; k < min(my, S - 1); ++k) issue(k, k);
 
   const uint8_t* xws = a.ws + (size_t)(a.experts ? (sel % a.n_ids) / a.x_div : 0) * (size_t)a.ws_stride;
   if (a.xmode) {  // this CTA's own encoding of x (the input was written by the preceding kernel)
@@ -794,25 +798,29 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY, UL>()) mv_tile_k
   __shared__ int gave_up;
   if (tid == 0) gave_up = 0;
   __syncthreads();
+  int ring_i = 0;         // ring slot of stage k (k % S) ...
+  uint32_t ring_ph = 0u;  // ... and the phase parity of its barrier ((k / S) & 1)
   for (; k < my; ++k) {
     // stage k landed; the barrier also retires iteration k-1, whose slot the
     // refill below reuses.  A thread whose bounded wait gives up raises the
     // shared flag before the barrier, so every thread leaves the loop at the
     // same iteration.
-    if (!mbar_wait_bounded(smem_addr(&bars[k % S]), (uint32_t)(k / S) & 1u)) gave_up = 1;
+    if (!mbar_wait_bounded(smem_addr(&bars[ring_i]), ring_ph)) gave_up = 1;
     __syncthreads();
     if (gave_up) {
       if (tid == 0) atomicOr(status, (int)kStatusWaitTimeout);
       break;
     }
-    if (k > 0) finalize(k - 1);
+    // refill stage k-1's slot (every warp finished it before the barrier) first,
+    // then finalize stage k-1's rows from the reduction buffer
     if (tid == 0 && k + S - 1 < my) {
       fence_proxy_async();  // generic reads of the slot precede its async refill
-      issue(k + S - 1);
+      issue(k + S - 1, ring_i == 0 ? S - 1 : ring_i - 1);
     }
+    if (k > 0) finalize(k - 1);
     const int st = cta + k * ncta;
     const int nr = stage_rows(st);
-    const uint32_t base = ring + (uint32_t)((k % S) * a.stage_bytes) +
+    const uint32_t base = ring + (uint32_t)(ring_i * a.stage_bytes) +
                           (uint32_t)(((uintptr_t)wb + (uintptr_t)st * stage_stride) & 15) +
                           (uint32_t)(slot * M) * (uint32_t)a.row_bytes;
     float acc[M];
@@ -829,6 +837,10 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY, UL>()) mv_tile_k
     float* r = red + (size_t)(k & 1) * kWarps * M;
     const float v = reduce_rows<M>(acc, lane);
     if ((lane & (32 / M - 1)) == 0) r[warp * M + lane / (32 / M)] = v;
+    if (++ring_i == S) {
+      ring_i = 0;
+      ring_ph ^= 1u;
+    }
   }
   __syncthreads();
   if (k == my && my > 0) finalize(my - 1);
@@ -860,7 +872,7 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY, UL>()) mv_tile_k
   if (a.post.op != kPostNone) run_post(a.post, a.y, a.rows, best_v, best_i);
 }
 
-struct TilePlan { int rs, lps, m, stage_bytes, ul; size_t smem; int xenc_off; };
+struct TilePlan { int rs, lps, m, stage_bytes, slots, ul; size_t smem; int xenc_off; };
 
 TilePlan plan_tile(size_t row_bytes, int rows, int cols, int vals, size_t xenc_bytes) {
   TilePlan p{};
@@ -876,17 +888,35 @@ TilePlan plan_tile(size_t row_bytes, int rows, int cols, int vals, size_t xenc_b
   const int rs = p.rs;
   // rows per slot per stage (1, 2, 4 or 8): stages of up to 32 KB amortise the
   // per-stage barrier, copy issue and row reduction; 3 slots keep 2 in flight.
-  // A matrix too small for a full wave of such stages keeps 20 KB stages, so
-  // more CTAs share it.
+  // Where 48 KB doubles the rows of a stage and the matrix still has a full
+  // wave of such stages, 2 slots of the larger stage (the same bytes in
+  // flight per SM, half the per-stage work per byte; measured 5-11% faster on
+  // the rows x 4096 shapes, and slower where the stage stays the same size).
+  // A matrix too small for a full wave of stages keeps 20 KB stages, so more
+  // CTAs share it.
+  // M is capped by the rows a stage may hold and by the instantiated (UL, M):
+  // up to 8 for one unit per lane, 4 for two, 2 for more
   const size_t per = (size_t)rs * row_bytes;
-  auto m_for = [&](size_t cap) { return per * 8 <= cap ? 8 : per * 4 <= cap ? 4 : per * 2 <= cap ? 2 : 1; };
+  int max_m = p.ul == 1 ? 8 : p.ul == 2 ? 4 : 2;
+  if (rs * max_m > kMaxRowsPerStage) max_m = kMaxRowsPerStage / rs;
+  auto m_for = [&](size_t cap) {
+    const int m = per * 8 <= cap ? 8 : per * 4 <= cap ? 4 : per * 2 <= cap ? 2 : 1;
+    return m < max_m ? m : max_m;
+  };
+  const long long wave = 148LL * 3;
+  p.slots = 3;
   p.m = m_for(32 * 1024);
-  if ((long long)rows / ((long long)rs * p.m) < 148LL * 3) p.m = m_for(20 * 1024);
-  if (rs * p.m > kMaxRowsPerStage) p.m = kMaxRowsPerStage / rs;
+  const int m48 = m_for(48 * 1024);
+  if (m48 > p.m && (long long)rows / ((long long)rs * m48) >= wave) {
+    p.m = m48;
+    p.slots = 2;
+  } else if ((long long)rows / ((long long)rs * p.m) < wave) {
+    p.m = m_for(20 * 1024);
+  }
   for (;;) {
     const size_t sb = ((size_t)rs * p.m * row_bytes + 16 + 32 + 127) & ~(size_t)127;
     p.stage_bytes = (int)sb;
-    p.smem = (size_t)kStages * sb + 2 * kWarps * p.m * sizeof(float) + (size_t)kStages * 8;
+    p.smem = (size_t)p.slots * sb + 2 * kWarps * p.m * sizeof(float) + (size_t)kMaxStages * 8;
     if (xenc_bytes) {
       p.xenc_off = (int)((p.smem + 255) & ~(size_t)255);
       p.smem = (size_t)p.xenc_off + xenc_bytes;
@@ -894,6 +924,7 @@ TilePlan plan_tile(size_t row_bytes, int rows, int cols, int vals, size_t xenc_b
     // a prologue's copy of x shares the CTA's shared memory: smaller stages
     if (p.smem <= kMaxTileSmem || p.m == 1) return p;
     p.m /= 2;
+    p.slots = 3;
   }
 }
 
@@ -989,7 +1020,7 @@ int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, in
   const int vals = (type_id == Q6_K || type_id == Q4_K || type_id == Q5_K) ? 64 : 32;
   const size_t xenc = xp ? ((lane_workspace_bytes(cols) + 255) & ~(size_t)255) : 0;
   const TilePlan p = plan_tile(row_bytes, rows, cols, vals, xenc);
-  TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs, p.lps, p.m, p.stage_bytes, static_weights ? 1 : 0,
+  TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs, p.lps, p.m, p.stage_bytes, p.slots, static_weights ? 1 : 0,
               accumulate ? 1 : 0, post ? *post : PostArgs{}, nullptr, 0, 0, 0, 0, 0, 0, 1,
               xp ? xp->mode : 0, xp ? xp->src : nullptr, xp ? xp->norm : nullptr, xp ? xp->eps : 0.0,
               xp ? xp->out : nullptr, p.xenc_off};
