@@ -17,8 +17,8 @@
 //    channel), where two digits would lose the small values' precision; a
 //    CTA adds those terms to its rows after streaming them (wide_pass), and
 //    only when x has a wide block, so the streaming loop is the same either way.
-//  * A CTA (256 threads) owns whole rows.  Its lanes are split into RS row
-//    slots; lane l of a slot always handles the same units (32-value pieces)
+//  * A CTA (up to 256 threads) owns whole rows.  Its lanes are split into RS
+//    row slots of 16 or a multiple of 32 lanes; lane l of a slot always handles the same units (32-value pieces)
 //    of a row, so it loads its x digits once, into registers, for the whole
 //    kernel.  Only weights move per row.
 //  * Weights are staged through a ring of S shared-memory stages; a stage is
@@ -28,8 +28,8 @@
 //    slot's mbarrier.  (Measured on B200: bulk copies below ~4 KB cannot
 //    saturate HBM, 16 KB copies stream at ~7 TB/s.)  Lanes then decode their
 //    units from shared memory, whatever the block alignment.
-//  * K-quant headers are decoded cooperatively: the 8 lanes of a block decode
-//    one (scale, min) pair each and trade d*sc, dmin*m by shuffle.
+//  * Each lane decodes the (scale, min) pairs of its own units, so a unit's
+//    header and epilogue are paid once per 64 values (K-quants).
 //  * Row sums: a butterfly that reduces M rows at once, then a fixed-order
 //    sum of the slot's warps in shared memory (deterministic; any row
 //    partition gives bit-identical rows).
@@ -142,18 +142,20 @@ __device__ __forceinline__ int dot16u(const uint32_t (&c)[4], const Dig16& d) {
   return (a0 + a1) * 254 + (b0 + b1);
 }
 
-// Row sums of M per-lane partials with one butterfly: at each level a lane
-// keeps half of its rows and trades the other half with its partner, so M
-// rows cost 5 + M - 1 shuffles instead of 5 M.  Returns the full sum of row
-// lane / (32 / M).
-template <int M>
+// Row sums of M per-lane partials with one butterfly over LANES lanes (32: a
+// whole warp; 16: each half of a warp separately): at each level a lane keeps
+// half of its rows and trades the other half with its partner, so M rows cost
+// log2(LANES) + M - 1 shuffles instead of M log2(LANES).  Returns the full sum
+// of row (lane % LANES) / (LANES / M) of the lane's LANES-lane group.
+template <int M, int LANES>
 __device__ __forceinline__ float reduce_rows(const float (&acc)[M], int lane) {
+  constexpr int LEVELS = LANES == 32 ? 5 : 4;
   float v[M];
 #pragma unroll
   for (int i = 0; i < M; ++i) v[i] = acc[i];
 #pragma unroll
-  for (int lvl = 0; lvl < 5; ++lvl) {
-    const int stride = 16 >> lvl;
+  for (int lvl = 0; lvl < LEVELS; ++lvl) {
+    const int stride = (LANES / 2) >> lvl;
     const int n = (M >> lvl) > 1 ? (M >> lvl) : 1;  // rows still held
     if (n > 1) {
       const int half = n / 2;
@@ -498,8 +500,10 @@ template <> struct UnitOf<Q6_K> { using T = UnitQ6K<false>; };
 template <> struct UnitOf<kQ6KRealign> { using T = UnitQ6K<true>; };
 template <> struct UnitOf<IQ4_XS> { using T = UnitIQ4XS; };
 
-// a tile CTA has up to kThreads threads (rs row slots of lps lanes, tile plan)
-constexpr int kThreads = 256, kWarps = 8, kMaxRowsPerStage = 64, kMaxStages = 3;
+// a tile CTA has up to kThreads threads (rs row slots of lps lanes, tile plan);
+// a slot's row partials come from its warps, or from its half warp when a
+// slot has 16 lanes (kMaxParts partials per row block)
+constexpr int kThreads = 256, kWarps = 8, kMaxParts = 16, kMaxRowsPerStage = 64, kMaxStages = 3;
 constexpr size_t kMaxTileSmem = 150 * 1024;  // dynamic shared memory a tile CTA may take
 
 // The last CTA to finish (a ticket counter, no waiting) runs one operation on
@@ -567,7 +571,7 @@ struct TileArgs {
   int rows, cols;
   const uint8_t* ws;  // prepared x
   float* y;
-  int rs, lps;      // rs row slots of lps lanes (a multiple of 32); the CTA has rs * lps threads
+  int rs, lps;      // rs row slots of lps lanes (16 or a multiple of 32); the CTA has rs * lps threads
   int m;            // rows per slot per stage
   int stage_bytes;  // shared bytes per stage (rs*m rows + alignment slack)
   int slots;        // stages in the ring (2 or 3)
@@ -596,11 +600,12 @@ struct TileArgs {
 };
 
 // CTAs per SM each format's register budget allows (launch bounds).
-// CTAs per SM the register budget is sized for (65,536 / (256 * this)): Q6_K
-// and every lane holding two or more units need more than 80 registers, and
-// their stages (32 KB for the 4096 x 14336 shapes) fit two CTAs per SM anyway.
+// CTAs per SM the register budget is sized for (65,536 / (256 * this)): Q6_K,
+// Q4_K and every lane holding two or more units need more than 80 registers,
+// and their stages (32 KB for the 4096 x 14336 shapes) fit two CTAs per SM
+// anyway (Q4_K: -3% on 4096 x 14336 with 128 registers, no change elsewhere).
 template <int TY, int UL> constexpr int tile_min_blocks() {
-  return (TY == Q6_K || TY == kQ6KRealign || UL >= 2) ? 2 : 3;
+  return (TY == Q6_K || TY == kQ6KRealign || TY == Q4_K || UL >= 2) ? 2 : 3;
 }
 
 // The part of 32 weights (unit u of block b) that the streaming loop multiplies
@@ -684,14 +689,17 @@ __device__ __forceinline__ void wide_pass(const uint8_t* wb, size_t row_bytes, i
   }
 }
 
-template <int TY, int UL, int M>
+// HALF: 16-lane row slots, two per warp (rows of at most 16 units; one unit
+// per lane), a separate instantiation so the common kernels keep their
+// registers.
+template <int TY, int UL, int M, bool HALF>
 __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY, UL>()) mv_tile_kernel(TileArgs a, int* status) {
   using U = typename UnitOf<TY>::T;
   constexpr int BPB = Geo<TY>::bpb;
   const int S = a.slots;
   extern __shared__ __align__(128) uint8_t smem[];
-  float* red = reinterpret_cast<float*>(smem + (size_t)S * a.stage_bytes);  // [2][kWarps][M]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * kWarps * M);        // [S] full barriers
+  float* red = reinterpret_cast<float*>(smem + (size_t)S * a.stage_bytes);  // [2][kMaxParts][M]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * kMaxParts * M);      // [S] full barriers
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lps = a.lps, slot = tid / lps, ls = tid - slot * lps;
   const int rows_per_stage = M * a.rs;
@@ -780,13 +788,13 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY, UL>()) mv_tile_k
 
   float best_v = -FLT_MAX;  // POST_ARGMAX: this thread's best finalized row
   int best_i = 0x7fffffff;
-  auto finalize = [&](int k) {  // fixed-order sum of the slot warps' partials
+  auto finalize = [&](int k) {  // fixed-order sum of the slot's partials (its warps, or its half warp)
     const int st = cta + k * ncta;
     if (tid < stage_rows(st)) {
-      const int s_slot = tid / M, i = tid % M, wps = lps >> 5;
-      const float* r = red + (size_t)(k & 1) * kWarps * M;
+      const int s_slot = tid / M, i = tid % M, parts = HALF ? 1 : lps >> 5;
+      const float* r = red + (size_t)(k & 1) * kMaxParts * M;
       float v = 0.f;
-      for (int w = 0; w < wps; ++w) v += r[(s_slot * wps + w) * M + i];
+      for (int w = 0; w < parts; ++w) v += r[(s_slot * parts + w) * M + i];
       float* yp = yb + (size_t)st * rows_per_stage + tid;
       v = a.accumulate ? *yp + v : v;
       *yp = v;
@@ -834,9 +842,14 @@ __global__ void __launch_bounds__(kThreads, tile_min_blocks<TY, UL>()) mv_tile_k
       for (int kk = 0; kk < UL; ++kk) v += uon[kk] * U::dot(rowa + (uint32_t)uoff[kk], uj[kk], xu[kk], lane);
       acc[i] = on * v;
     }
-    float* r = red + (size_t)(k & 1) * kWarps * M;
-    const float v = reduce_rows<M>(acc, lane);
-    if ((lane & (32 / M - 1)) == 0) r[warp * M + lane / (32 / M)] = v;
+    float* r = red + (size_t)(k & 1) * kMaxParts * M;
+    if constexpr (!HALF) {  // partial of warp `warp` (part `warp` of slot warp / (lps / 32))
+      const float v = reduce_rows<M, 32>(acc, lane);
+      if ((lane & (32 / M - 1)) == 0) r[warp * M + lane / (32 / M)] = v;
+    } else {  // two 16-lane slots per warp: the partial of slot 2 warp + lane / 16
+      const float v = reduce_rows<M, 16>(acc, lane);
+      if ((lane & (16 / M - 1)) == 0) r[(2 * warp + (lane >> 4)) * M + (lane & 15) / (16 / M)] = v;
+    }
     if (++ring_i == S) {
       ring_i = 0;
       ring_ph ^= 1u;
@@ -878,13 +891,14 @@ TilePlan plan_tile(size_t row_bytes, int rows, int cols, int vals, size_t xenc_b
   TilePlan p{};
   const int units = cols / vals;
   // a row's units over lps lanes, ul units per lane; lps is the smallest
-  // multiple of 32 that holds them, so no warp of a slot is idle and at most
+  // multiple of 32 that holds them (or 16), so no warp of a slot is idle and at most
   // 31 lanes are (14336 columns: 224 or 448 units -> 224 lanes, 7 warps);
   // rs slots of rows side by side fill up to kThreads threads
+  // Rows of at most 16 units (64-value units: 1024 columns and less, e.g. the
+  // 768-column MoE expert down products) take 16-lane slots, two per warp.
   p.ul = (units + kThreads - 1) / kThreads;
-  p.lps = 32 * (((units + p.ul - 1) / p.ul + 31) / 32);
+  p.lps = units <= 16 ? 16 : 32 * (((units + p.ul - 1) / p.ul + 31) / 32);
   p.rs = kThreads / p.lps;
-  if (p.rs > 8) p.rs = 8;
   const int rs = p.rs;
   // rows per slot per stage (1, 2, 4 or 8): stages of up to 32 KB amortise the
   // per-stage barrier, copy issue and row reduction; 3 slots keep 2 in flight.
@@ -916,7 +930,7 @@ TilePlan plan_tile(size_t row_bytes, int rows, int cols, int vals, size_t xenc_b
   for (;;) {
     const size_t sb = ((size_t)rs * p.m * row_bytes + 16 + 32 + 127) & ~(size_t)127;
     p.stage_bytes = (int)sb;
-    p.smem = (size_t)p.slots * sb + 2 * kWarps * p.m * sizeof(float) + (size_t)kMaxStages * 8;
+    p.smem = (size_t)p.slots * sb + 2 * kMaxParts * p.m * sizeof(float) + (size_t)kMaxStages * 8;
     if (xenc_bytes) {
       p.xenc_off = (int)((p.smem + 255) & ~(size_t)255);
       p.smem = (size_t)p.xenc_off + xenc_bytes;
@@ -928,7 +942,7 @@ TilePlan plan_tile(size_t row_bytes, int rows, int cols, int vals, size_t xenc_b
   }
 }
 
-template <int TY, int UL, int M>
+template <int TY, int UL, int M, bool HALF>
 int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -945,7 +959,7 @@ int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
   }
   constexpr int kMaxSmem = (int)kMaxTileSmem;
   if (!smem_set[dev].load(std::memory_order_acquire)) {
-    if (cudaFuncSetAttribute(mv_tile_kernel<TY, UL, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+    if (cudaFuncSetAttribute(mv_tile_kernel<TY, UL, M, HALF>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
         cudaSuccess)
       return -100 - (int)cudaGetLastError();
     smem_set[dev].store(true, std::memory_order_release);
@@ -966,14 +980,21 @@ int launch_tile_t(const TileArgs& ta, size_t smem, cudaStream_t stream) {
   } else if (grid > nstages) {
     grid = nstages;
   }
-  return launch_pdl(mv_tile_kernel<TY, UL, M>, dim3(grid), dim3(ta.rs * ta.lps), smem, stream, ta,
+  return launch_pdl(mv_tile_kernel<TY, UL, M, HALF>, dim3(grid), dim3(ta.rs * ta.lps), smem, stream, ta,
                     device_status_word());
 }
 
 template <int TY>
 int launch_tile_type(const TileArgs& ta, int ul, size_t smem, cudaStream_t stream) {
 #define PYR_UM(UL_, M_) \
-  if (ul == UL_ && ta.m == M_) return launch_tile_t<TY, UL_, M_>(ta, smem, stream);
+  if (ul == UL_ && ta.m == M_) return launch_tile_t<TY, UL_, M_, false>(ta, smem, stream);
+  if (ta.lps == 16) {  // 16-lane slots: one unit per lane, at most 4 rows per slot (16 slots)
+    if (ul != 1) return 1;
+    if (ta.m == 1) return launch_tile_t<TY, 1, 1, true>(ta, smem, stream);
+    if (ta.m == 2) return launch_tile_t<TY, 1, 2, true>(ta, smem, stream);
+    if (ta.m == 4) return launch_tile_t<TY, 1, 4, true>(ta, smem, stream);
+    return 1;
+  }
   PYR_UM(1, 1) PYR_UM(1, 2) PYR_UM(1, 4) PYR_UM(1, 8) PYR_UM(2, 1) PYR_UM(2, 2) PYR_UM(2, 4)
   PYR_UM(3, 1) PYR_UM(3, 2) PYR_UM(4, 1) PYR_UM(4, 2)
 #undef PYR_UM

@@ -112,7 +112,9 @@ def test_device_matvec_golden_payloads(cuda_device, golden_decoders, ggml_type):
 # rows x cols cases that walk every tail of the streamed kernel: partial row
 # groups, partial chunks (cols not a multiple of the chunk), single rows,
 # more groups than warps.
-RAGGED = [(1, 256), (3, 768), (5, 1280), (37, 2304), (130, 4096), (513, 1024), (2, 14336)]
+# includes rows of at most 16 units (16-lane slots: 256..1024 columns of the
+# 64-value K-quant units, the 2048 x 768 MoE expert down shape)
+RAGGED = [(1, 256), (3, 768), (5, 1280), (37, 2304), (130, 4096), (513, 1024), (2, 14336), (2048, 768), (700, 512)]
 
 
 @pytest.mark.parametrize("rows,cols", RAGGED)
