@@ -494,23 +494,32 @@ __global__ void __launch_bounds__(256) attention_rows_kernel(const float* __rest
   __shared__ __align__(16) float vs[kAttnKT][HD];
   __shared__ float ps[kAttnQB][kAttnKT];
   pdl_wait();
-  // a CTA: 16 consecutive positions of one sequence (rp.step 1), or the one
-  // query of one sequence (rp.step 0: each row has its own cache)
-  const int qb = rp.step ? kAttnQB : 1;
-  const int tid = threadIdx.x, head = blockIdx.x, j0 = blockIdx.y * qb;
-  const int kvh = head / (nq / nkv), kv_dim = nkv * HD;
+  // A CTA's 16 query slots: 16 consecutive positions of one sequence and one
+  // head (rp.step 1: blockIdx = (head, block of rows)), or up to 16 query
+  // heads of one KV head at the one position of one sequence (rp.step 0, each
+  // row its own cache: blockIdx = (KV head x head block, row)); either way the
+  // slots share every K/V tile the CTA loads.  A query's arithmetic does not
+  // depend on its slot.
+  const int group = nq / nkv, nhb = (group + kAttnQB - 1) / kAttnQB;
+  const bool heads = rp.step == 0;
+  const int tid = threadIdx.x, kv_dim = nkv * HD;
+  const int j0 = heads ? blockIdx.y : blockIdx.y * kAttnQB;
+  const int kvh = heads ? blockIdx.x / nhb : blockIdx.x / group;
+  const int h0 = heads ? kvh * group + (blockIdx.x % nhb) * kAttnQB : blockIdx.x;  // slot 0's head
   const float* kcache = kcache_base + (size_t)j0 * rp.cache_stride;
   const float* vcache = vcache_base + (size_t)j0 * rp.cache_stride;
   const int qi = tid >> 4, sub = tid & 15;
-  const int nqb = min(qb, count - j0);
+  const int nqb = heads ? min(kAttnQB, kvh * group + group - h0) : min(kAttnQB, count - j0);
   for (int e = tid; e < kAttnQB * HD; e += blockDim.x) {
     const int i = e / HD, d = e % HD;
-    qs[i][d] = i < nqb ? q[(size_t)(j0 + i) * ldq + (size_t)head * HD + d] : 0.f;
+    const size_t src = heads ? (size_t)j0 * ldq + (size_t)(h0 + i) * HD : (size_t)(j0 + i) * ldq + (size_t)h0 * HD;
+    qs[i][d] = i < nqb ? q[src + d] : 0.f;
   }
-  const int qpos = rp.at(j0 + min(qi, nqb - 1));  // this thread's query position
+  const int qrow = heads ? j0 : j0 + min(qi, nqb - 1);  // this thread's query row
+  const int qpos = rp.at(qrow);                         // and its position
   const bool qon = qi < nqb && qpos >= 0 && qpos < rp.max_ctx;
   // keys 0 .. kend - 1 are needed by some query (positions grow with the row)
-  const int kend = min(rp.at(j0 + nqb - 1) + 1, rp.max_ctx);
+  const int kend = min(rp.at(heads ? j0 : j0 + nqb - 1) + 1, rp.max_ctx);
   const float scale = (float)(1.0 / sqrt((double)HD));
   float m = -FLT_MAX, l = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   for (int t0 = 0; t0 < kend; t0 += kAttnKT) {
@@ -561,7 +570,7 @@ __global__ void __launch_bounds__(256) attention_rows_kernel(const float* __rest
     }
   }
   if (qon) {
-    float* orow = out + (size_t)(j0 + qi) * ldo + (size_t)head * HD + 8 * sub;
+    float* orow = out + (size_t)(heads ? j0 : j0 + qi) * ldo + (size_t)(heads ? h0 + qi : h0) * HD + 8 * sub;
     const float inv = 1.f / l;
 #pragma unroll
     for (int e = 0; e < 8; ++e) orow[e] = o[e] * inv;
@@ -830,10 +839,13 @@ int pyrite_cuda_attention_rows(const float* q, long long ldq, const float* k_cac
       ldq < (long long)n_heads * 128 || ldo < (long long)n_heads * 128 ||
       (((uintptr_t)k_cache | (uintptr_t)v_cache) & 15) || (cache_stride & 3))
     return PYRITE_E_SHAPE;
-  const int qb = pos_step ? kAttnQB : 1;
-  const unsigned qblocks = (unsigned)((count + qb - 1) / qb);
+  // pos_step 1: (head, block of 16 rows); pos_step 0: (KV head x block of 16
+  // of its query heads, row)
+  const int group = n_heads / n_kv_heads, nhb = (group + kAttnQB - 1) / kAttnQB;
+  const dim3 grid = pos_step ? dim3((unsigned)n_heads, (unsigned)((count + kAttnQB - 1) / kAttnQB))
+                             : dim3((unsigned)(n_kv_heads * nhb), (unsigned)count);
   RowPos rp{first, pos, pos_step, cache_stride, max_ctx};
-  return rc(launch_pdl(attention_rows_kernel, dim3((unsigned)n_heads, qblocks), dim3(256), 0,
+  return rc(launch_pdl(attention_rows_kernel, grid, dim3(256), 0,
                        static_cast<cudaStream_t>(stream), q, ldq, k_cache, v_cache, rp, count, n_heads, n_kv_heads,
                        out, ldo));
 }

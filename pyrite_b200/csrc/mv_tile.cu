@@ -643,11 +643,18 @@ __device__ __forceinline__ void code_part(const uint8_t* b, int u, float (&v)[32
 // The third digits of the wide blocks of x (negative scales), for the rows a
 // CTA owns (stages cta, cta + ncta, ... of rps rows).  Warp 0 lists the wide
 // blocks in increasing order in `list` (shared memory: list[0] = count, then
-// the block indices); then a warp per row, its lanes over the listed blocks
-// in turn, each decoding the d*sc*q part of its 32 weights (code_part, fp32)
-// and dotting it with the block's third digits; a fixed-order warp sum, added
-// to y.  Runs after the rows are final, only when x has a wide block, so the
-// streaming loop keeps its registers and instruction mix.
+// the block indices).  Then each row takes a group of G lanes (G: the next
+// power of two >= the count n, at most 32; a warp serves 32 / G rows at
+// once): lane g of a group takes listed blocks g, g + G, ... (one block per
+// lane when n <= 32), decodes the d*sc*q part of its 32 weights (code_part,
+// fp32) and dots it with the block's third digits; a butterfly over the group
+// sums the lanes, and the sum is added to y.  The result does not depend on
+// G: a 32-lane butterfly whose lanes past n hold +0 differs from the G-lane
+// one only in turning a -0 into +0, which the "+ 0" before the butterfly
+// does for G < 32.  (One warp per row left all but n lanes idle: with 683
+// rows per CTA this pass cost as much as the streaming loop.)  Runs after
+// the rows are final, only when x has a wide block, so the streaming loop
+// keeps its registers and instruction mix.
 template <int TY>
 __device__ __forceinline__ void wide_pass(const uint8_t* wb, size_t row_bytes, int cols, const float* scale,
                                           const uint8_t* q2, float* yb, int cta, int ncta, int rps, int rows, int my,
@@ -668,24 +675,31 @@ __device__ __forceinline__ void wide_pass(const uint8_t* wb, size_t row_bytes, i
   }
   __syncthreads();
   const int n = list[0];
-  for (int idx = warp; idx < my * rps; idx += nw) {
-    const int row = (cta + (idx / rps) * ncta) * rps + idx % rps;
-    if (row >= rows) continue;  // warp-uniform
-    const uint8_t* rp = wb + (size_t)row * row_bytes;
+  int G = 1;
+  while (G < n && G < 32) G *= 2;
+  const int per_warp = 32 / G, g = lane & (G - 1);  // rows per warp pass; this lane's place in its group
+  const int total = my * rps;
+  for (int base = warp * per_warp; base < total; base += nw * per_warp) {  // warp-uniform trip count
+    const int idx = base + lane / G;
+    const int row = idx < total ? (cta + (idx / rps) * ncta) * rps + idx % rps : rows;
+    const bool on = row < rows;
     float part = 0.f;
-    for (int j = lane; j < n; j += 32) {
-      const int b = list[1 + j];
-      float w[32];
-      code_part<DT>(rp + (size_t)(b / UPB) * BPB, b % UPB, w);
-      const int8_t* d2 = reinterpret_cast<const int8_t*>(q2 + 32 * b);
-      float t = 0.f;
+    if (on) {
+      const uint8_t* rp = wb + (size_t)row * row_bytes;
+      for (int j = g; j < n; j += G) {
+        const int b = list[1 + j];
+        float w[32];
+        code_part<DT>(rp + (size_t)(b / UPB) * BPB, b % UPB, w);
+        const int8_t* d2 = reinterpret_cast<const int8_t*>(q2 + 32 * b);
+        float t = 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) t = fmaf(w[i], (float)d2[i], t);
-      part = fmaf(-scale[b], t, part);  // a negative scale: its magnitude is s_b / 254
+        for (int i = 0; i < 32; ++i) t = fmaf(w[i], (float)d2[i], t);
+        part = fmaf(-scale[b], t, part);  // a negative scale: its magnitude is s_b / 254
+      }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-    if (lane == 0) yb[row] += part * kInv254;
+    if (G < 32) part = part + 0.0f;  // -0 -> +0, as the lanes past n of a 32-lane sum do
+    for (int o = G / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (on && g == 0) yb[row] += part * kInv254;
   }
 }
 
