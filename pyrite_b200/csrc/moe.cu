@@ -33,54 +33,49 @@ struct RouteArgs {
   int* global_ids;
 };
 
-// The routing of one token by one CTA (256 threads): n <= 4096 router logits
-// (read through L2: other CTAs may just have written them), k <= 32.
-// Experts sharded by id over `shards` GPUs: this one (shard `index`) holds
-// experts e % shards == index at local slot e / shards; a selected expert it
-// does not hold gets id -1 and weight 0 (the expert matvecs skip it).
+// The routing of one token by the first warp of a CTA (the other threads
+// return at once; no block barrier inside): n <= 4096 router logits (read
+// through L2: other CTAs may just have written them), k <= 32.  Lane l takes
+// experts l, l + 32, ...; maxima, sums and the k argmax rounds are warp
+// butterflies (the same bits on every lane).  Experts sharded by id over
+// `shards` GPUs: this one (shard `index`) holds experts e % shards == index
+// at local slot e / shards; a selected expert it does not hold gets id -1
+// and weight 0 (the expert matvecs skip it).  (The block-wide form took two
+// block barriers per argmax round: ~17 us per layer for the configs[3]
+// router, cold.)
 __device__ void route_block(const float* __restrict__ logits, const RouteArgs& a) {
   __shared__ double p[4096];
-  __shared__ double dred[32];
-  __shared__ int wi[32];
-  __shared__ double chosen_p[32];
-  __shared__ int chosen_i[32];
-  const int n = a.n, k = a.k, norm = a.norm, shards = a.shards, index = a.index;
-  const double scale = a.scale;
-  int* const ids = a.ids;
-  float* const weights = a.weights;
-  int* const global_ids = a.global_ids;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31;
+  if (tid >= 32) return;
+  const int n = a.n, k = a.k;
   // softmax in fp64 (tensor_ops.py:513-521): exp(v - max) / sum
   double m = -DBL_MAX;
-  for (int e = tid; e < n; e += blockDim.x) m = fmax(m, (double)__ldcg(logits + e));
+  for (int e = lane; e < n; e += 32) m = fmax(m, (double)__ldcg(logits + e));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (lane == 0) dred[warp] = m;
-  __syncthreads();
-  m = dred[0];
-  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = fmax(m, dred[w]);
-  __syncthreads();
   double s = 0.0;
-  for (int e = tid; e < n; e += blockDim.x) {
+  for (int e = lane; e < n; e += 32) {
     const double x = exp((double)__ldcg(logits + e) - m);
     p[e] = x;
     s += x;
   }
-  const double total = block_sum(s, dred);
-  for (int e = tid; e < n; e += blockDim.x) p[e] /= total;
-  __syncthreads();
-  // k rounds of (max p, lowest e); a chosen expert drops out with p = -1
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  for (int e = lane; e < n; e += 32) p[e] /= s;
+  // k rounds of (max p, lowest e); a chosen expert drops out with p = -1.
+  // Round r's choice stays in lane r (cp, ci).
+  double cp = 0.0;
+  int ci = 0;
   for (int r = 0; r < k; ++r) {
     int bi = 0x7fffffff;
     double bp = -2.0;
-    for (int e = tid; e < n; e += blockDim.x)
+    for (int e = lane; e < n; e += 32)
       if (p[e] > bp || (p[e] == bp && e < bi)) {
         bp = p[e];
         bi = e;
       }
-    // reduce (bp, bi) over the block: compare in fp64
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
+    for (int o = 16; o > 0; o >>= 1) {  // compare in fp64, lowest index on ties
       const double op = __shfl_xor_sync(0xffffffffu, bp, o);
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (op > bp || (op == bp && oi < bi)) {
@@ -88,40 +83,27 @@ __device__ void route_block(const float* __restrict__ logits, const RouteArgs& a
         bi = oi;
       }
     }
-    if (lane == 0) {
-      dred[warp] = bp;
-      wi[warp] = bi;
+    if (lane == r) {
+      cp = bp;
+      ci = bi;
     }
-    __syncthreads();
-    if (tid == 0) {
-      for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
-        if (dred[w] > bp || (dred[w] == bp && wi[w] < bi)) {
-          bp = dred[w];
-          bi = wi[w];
-        }
-      chosen_p[r] = bp;
-      chosen_i[r] = bi;
-      p[bi] = -1.0;
-    }
-    __syncthreads();
+    if (lane == (bi & 31)) p[bi] = -1.0;  // the lane that owns expert bi
+    __syncwarp();
   }
-  if (tid == 0) {
-    double tot = 0.0;
-    for (int r = 0; r < k; ++r) tot += chosen_p[r];
-    for (int r = 0; r < k; ++r) {
-      double w = chosen_p[r];
-      if (norm && tot > 0.0) w = w / tot;
-      if (scale != 1.0) w = w * scale;
-      const int e = chosen_i[r];
-      const bool mine = e % shards == index;
-      ids[r] = mine ? e / shards : -1;
-      weights[r] = mine ? (float)w : 0.0f;
-      if (global_ids) global_ids[r] = e;
-    }
+  double tot = 0.0;  // in round order, as the weights are renormalised
+  for (int r = 0; r < k; ++r) tot += __shfl_sync(0xffffffffu, cp, r);
+  if (lane < k) {
+    double w = cp;
+    if (a.norm && tot > 0.0) w = w / tot;
+    if (a.scale != 1.0) w = w * a.scale;
+    const bool mine = ci % a.shards == a.index;
+    a.ids[lane] = mine ? ci / a.shards : -1;
+    a.weights[lane] = mine ? (float)w : 0.0f;
+    if (a.global_ids) a.global_ids[lane] = ci;
   }
 }
 
-__global__ void __launch_bounds__(256) moe_route_kernel(const float* __restrict__ logits, RouteArgs a) {
+__global__ void __launch_bounds__(32) moe_route_kernel(const float* __restrict__ logits, RouteArgs a) {
   pdl_wait();
   route_block(logits, a);
   pdl_launch_dependents();
@@ -147,7 +129,7 @@ __global__ void __launch_bounds__(256) moe_router_rows_kernel(const float* __res
 
 // moe_route_kernel for row blockIdx.x of a [count x n] logits array: its top_k
 // experts and weights to row blockIdx.x of ids / weights (top_k apart).
-__global__ void __launch_bounds__(256) moe_route_rows_kernel(const float* __restrict__ logits, long long ld,
+__global__ void __launch_bounds__(32) moe_route_rows_kernel(const float* __restrict__ logits, long long ld,
                                                              RouteArgs a) {
   pdl_wait();
   RouteArgs r = a;
@@ -297,7 +279,7 @@ int pyrite_cuda_moe_route(const float* router_logits, int n_experts, int top_k, 
     return PYRITE_E_SHAPE;
   RouteArgs a{n_experts, top_k, norm_topk_prob ? 1 : 0, scale, shard_count, shard_index, expert_ids, expert_weights,
               global_ids};
-  return rc(launch_pdl(moe_route_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), router_logits, a));
+  return rc(launch_pdl(moe_route_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), router_logits, a));
 }
 
 int pyrite_cuda_moe_router_rows(int router_type, const void* router, size_t router_len, size_t hidden,
@@ -320,7 +302,7 @@ int pyrite_cuda_moe_route_rows(const float* router_logits, long long ld, size_t 
       top_k > 32 || top_k > n_experts || !(scale > 0.0) || count == 0 || count > 65535 || ld < n_experts)
     return PYRITE_E_SHAPE;
   RouteArgs a{n_experts, top_k, norm_topk_prob ? 1 : 0, scale, 1, 0, expert_ids, expert_weights, nullptr};
-  return rc(launch_pdl(moe_route_rows_kernel, dim3((unsigned)count), dim3(256), 0, static_cast<cudaStream_t>(stream),
+  return rc(launch_pdl(moe_route_rows_kernel, dim3((unsigned)count), dim3(32), 0, static_cast<cudaStream_t>(stream),
                        router_logits, ld, a));
 }
 
