@@ -328,6 +328,7 @@ def run_ours(args) -> None:
            if (rank == 0 and not args.no_cpu) else None)
     decode = decode_leg(dev) if (rank == 0 and not args.no_decode) else None
     batched = batched_leg(dev, W, X, wl, stream) if (rank == 0 and not args.no_batched) else None
+    types = types_leg(dev, stream) if (rank == 0 and not args.no_types) else None
     del W, X, Y
     torch.cuda.empty_cache()
     models = None
@@ -374,6 +375,7 @@ def run_ours(args) -> None:
             "e2e": e2e,
             "decode": decode,
             "batched": batched,
+            "types": types,
             "models": models,
             "gpu_launches": args.steps * (len(wl) + len({c for _, _, _, c in wl})),
             "clocks": clocks.summary(),
@@ -460,6 +462,7 @@ def batched_leg(dev, W, X, wl, stream, ncols_list=(8, 64)) -> dict:
     from pyrite_b200.kernels import cuda as K
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").is_file() else {}
     tflops_peak = float(peaks.get("bf16_tflops", 1590.0))
+    tflops_kind = "measured bf16_tflops (burst)" if "bf16_tflops" in peaks else "fallback bf16 1590 TFLOP/s (burst)"
     rows_out, tot_flops, tot_us = [], 0.0, 0.0
     for ncols in ncols_list:
         for name, t, r, c in wl:
@@ -504,12 +507,83 @@ def batched_leg(dev, W, X, wl, stream, ncols_list=(8, 64)) -> dict:
             "roofline": {"bound": "tensor", "kernel": f"mm_tc_kernel<{dom['type']}>@{dom['rows']}x{dom['cols']}"
                                                       f"x{dom['ncols']}",
                          "achieved": dom_tf, "peak": tflops_peak, "unit": "TFLOP/s",
-                         "frac": round(dom_tf / tflops_peak, 4), "peak_kind": "measured bf16_tflops (burst)",
+                         "frac": round(dom_tf / tflops_peak, 4), "peak_kind": tflops_kind,
                          "flops": "2 rows cols ncols per launch (algorithmic; the split-bf16 scheme issues 4x)"}}
 
 
+# ---------------------------------------------------------------- the other decodable types
+OTHER_TYPES = {"Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "Q8_1": 9, "IQ4_NL": 20, "Q2_K": 10, "Q3_K": 11,
+               "F16": 1, "BF16": 30, "F32": 0}
+
+
+def other_payload(t: int, rows: int, cols: int, seed: int) -> bytes:
+    """Seeded N(0, 0.02) weights in format t: the package's quantizer where it
+    has one, a plain cast for the float formats, and seeded random blocks with
+    finite scales (tests/payloads.py) for Q4_1 / Q5_0 / Q5_1 / Q8_1, which have
+    no encoder here (the bytes streamed per row are the same either way)."""
+    from pyrite_b200.quantize import quantize, quantize_types
+    w = gaussian_weights(rows, cols, seed)
+    if t in quantize_types():
+        return quantize(t, w)
+    if t == 0:
+        return w.tobytes()
+    if t == 1:
+        return w.astype(np.float16).tobytes()
+    if t == 30:
+        return (w.view(np.uint32) >> 16).astype(np.uint16).tobytes()
+    from tests.payloads import random_payload
+    return random_payload(t, rows, cols, seed=seed)
+
+
+def types_leg(dev, stream, shapes=((14336, 4096), (4096, 14336))) -> dict:
+    """Batch-1 throughput of every other decodable type on the large configs[1]
+    shapes, timed like the step's per-kernel lines (each matrix rotating over
+    > 512 MB of copies inside one CUDA graph, events on its stream).  Q4_0,
+    Q4_1, Q5_0, Q5_1, Q8_1 and IQ4_NL run the tile kernel; Q2_K, Q3_K and the
+    float formats the warp-per-row kernel."""
+    import torch
+
+    from pyrite_b200.kernels import cuda as K
+    out = []
+    for (r, c) in shapes:
+        x = torch.from_numpy(np.random.default_rng(SEED + c).normal(0.0, 1.0, c).astype(np.float32)).to(dev)
+        y = torch.empty(r, dtype=torch.float32, device=dev)
+        ws = torch.empty(K.workspace_size(0, c) + 256, dtype=torch.uint8, device=dev)
+        for name, t in OTHER_TYPES.items():
+            src = torch.frombuffer(bytearray(other_payload(t, r, c, SEED + 7 * t + r)), dtype=torch.uint8).to(dev)
+            copies = max(3, -(-512 * 2**20 // src.numel()))
+            bufs = [src.clone() for _ in range(copies)]
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                px = K.prepare_x(x, workspace=ws)
+                K.matvec_prepared(t, bufs[0], px, r, c, out=y, static_weights=True)
+                torch.cuda.synchronize()
+                with torch.cuda.graph(g, stream=stream):
+                    for _ in range(2):
+                        for b in bufs:
+                            K.matvec_prepared(t, b, px, r, c, out=y, static_weights=True)
+                g.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (2 * copies)
+            out.append({"type": name, "rows": r, "cols": c, "us": round(us, 3),
+                        "GBps": round(algo_bytes(t, r, c) / (us * 1e-6) / 1e9, 1),
+                        "kernel": "mv_tile_kernel" if t in (2, 3, 6, 7, 9, 20) else "mv_generic_kernel"})
+            del g, bufs, src
+            torch.cuda.empty_cache()
+    if K.status() != 0:
+        raise SystemExit("device status word set during the types leg")
+    return {"config": "batch 1, every other decodable type at 14336x4096 and 4096x14336, cold HBM per launch",
+            "kernels": out}
+
+
 # ---------------------------------------------------------------- greedy parity of the model legs
-GOLDEN_2L = {"c3": "c3_2l.json", "c4": "moe_c4_2l.json", "c5": "moe_c5_2l.json"}
+# 2-layer full-width checkpoints, 120-token prompt + 8 greedy tokens (a 128-position window)
+GOLDEN_2L = {"c3": "c3_2l_w128.json", "c4": "moe_c4_2l_w128.json", "c5": "moe_c5_2l_w128.json"}
 
 
 def golden_parity(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> dict:
@@ -527,9 +601,9 @@ def golden_parity(dev, which: str, world: int = 1, rank: int = 0, pg=None) -> di
     spec = cls(**{k: v for k, v in g["spec"].items() if k in {f.name for f in fields(cls)}})
     if world > 1:
         from pyrite_b200.sharded import ShardedDecoder
-        dec = ShardedDecoder.synthetic(spec, rank, world, device=dev, max_ctx=64)
+        dec = ShardedDecoder.synthetic(spec, rank, world, device=dev, max_ctx=256)
     else:
-        dec = MixedDecoder.synthetic(spec, device=dev, max_ctx=64)
+        dec = MixedDecoder.synthetic(spec, device=dev, max_ctx=256)
     prompt, want = g["prompt"], g["generated"]
     got = dec.generate(prompt, len(want))[len(prompt):]
     dec.graph = None  # graphs holding NCCL calls go before the process group does
@@ -863,6 +937,7 @@ def main() -> None:
     ap.add_argument("--no-decode", action="store_true", help="skip the configs[0] decode tok/s leg")
     ap.add_argument("--no-batched", action="store_true", help="skip the 8- and 64-column tensor-core leg")
     ap.add_argument("--no-models", action="store_true", help="skip the configs[2] / configs[3] decode legs")
+    ap.add_argument("--no-types", action="store_true", help="skip the batch-1 leg of the other decodable types")
     ap.add_argument("--only", help="profile one matrix of the workload, e.g. Q4_K:14336x4096")
     args = ap.parse_args()
     if args.only:

@@ -182,7 +182,11 @@ int pyrite_cuda_matvec_prepared(int type_id, const void *weights, size_t weights
  * pyrite_cuda_matvec with ncols = 1; cols above PYRITE_NOALLOC_MAX_COLS is
  * rejected with PYRITE_E_SHAPE before any GPU work.  The first call on each
  * device looks up the array's device address (cudaGetSymbolAddress) with that
- * device current -- make that first call before any stream capture.  The one
+ * device current -- make that first call before any stream capture.  The
+ * address is kept for the life of the process: after cudaDeviceReset (or
+ * anything else that destroys and re-creates the device's primary context)
+ * it is stale, and this entry point must not be called again in that
+ * process.  The one
  * array is shared by every call on a device and keeps the last call's bytes:
  * calls that may overlap on the GPU (different streams without ordering)
  * race on it; calls on one stream are ordered and safe. */

@@ -54,12 +54,16 @@ int geometry(int type_id, size_t rows, size_t cols, size_t* row_bytes, const Typ
 
 int cuda_code(cudaError_t e) { return e == cudaSuccess ? 0 : PYRITE_E_CUDA; }
 
-// Library-owned staging for the host-buffer entry points: one stream and one
-// growable device buffer per device, serialised by a mutex.  Nothing is kept
-// between calls except this reusable scratch.
+// Library-owned staging for the host-buffer entry points: a compute stream, a
+// copy stream, a ring of events and one growable device buffer per device,
+// serialised by a mutex.  Nothing is kept between calls except this reusable
+// scratch.
+constexpr int kStageEvents = 8;
 struct HostStage {
   std::mutex mu;
-  cudaStream_t stream = nullptr;
+  cudaStream_t stream = nullptr;  // kernels and the result copy
+  cudaStream_t copy = nullptr;    // host-to-device copies of the payload
+  cudaEvent_t ev[kStageEvents] = {};
   void* buf = nullptr;
   size_t cap = 0;
 };
@@ -68,6 +72,11 @@ HostStage g_stage[64];
 int stage_reserve(HostStage& st, size_t bytes) {
   if (!st.stream && cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking) != cudaSuccess)
     return PYRITE_E_CUDA;
+  if (!st.copy) {
+    if (cudaStreamCreateWithFlags(&st.copy, cudaStreamNonBlocking) != cudaSuccess) return PYRITE_E_CUDA;
+    for (cudaEvent_t& e : st.ev)
+      if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return PYRITE_E_CUDA;
+  }
   if (bytes <= st.cap) return 0;
   if (st.buf) cudaFree(st.buf);
   st.buf = nullptr;
@@ -123,11 +132,24 @@ int pyrite_matvec(int type_id, const uint8_t* data, size_t data_len, const doubl
   uint8_t* dw = static_cast<uint8_t*>(st.buf);
   double* dx = reinterpret_cast<double*>(dw + xoff);
   double* dy = reinterpret_cast<double*>(dw + yoff);
-  if ((rc = cuda_code(cudaMemcpyAsync(dw, data, data_len, cudaMemcpyHostToDevice, st.stream)))) return rc;
-  if ((rc = cuda_code(cudaMemcpyAsync(dx, x, cols * sizeof(double), cudaMemcpyHostToDevice, st.stream))))
-    return rc;
-  MatvecArgs<double> a{dw, rb, (int)rows, (int)cols, dx, 0, dy, 0};
-  if ((rc = launch_mv_generic<double, 1>(type_id, a, st.stream))) return rc > 0 ? PYRITE_E_CUDA : rc;
+  // The payload crosses PCIe in row chunks of ~8 MB on the copy stream; each
+  // chunk's rows are computed on the compute stream as soon as it has landed,
+  // so the products overlap the copies of the chunks after them.  Rows are
+  // independent, so the results are the same bits as one launch over all rows.
+  // (An event of the ring is recorded again only after the compute stream's
+  // wait on its previous recording was enqueued, which is all a wait needs.)
+  if ((rc = cuda_code(cudaMemcpyAsync(dx, x, cols * sizeof(double), cudaMemcpyHostToDevice, st.copy)))) return rc;
+  const size_t chunk_rows = rb >= ((size_t)8 << 20) ? 1 : ((size_t)8 << 20) / rb;
+  int k = 0;
+  for (size_t r0 = 0; r0 < rows; r0 += chunk_rows, k = (k + 1) % kStageEvents) {
+    const size_t n = rows - r0 < chunk_rows ? rows - r0 : chunk_rows;
+    if ((rc = cuda_code(cudaMemcpyAsync(dw + r0 * rb, data + r0 * rb, n * rb, cudaMemcpyHostToDevice, st.copy))))
+      return rc;
+    if ((rc = cuda_code(cudaEventRecord(st.ev[k], st.copy)))) return rc;
+    if ((rc = cuda_code(cudaStreamWaitEvent(st.stream, st.ev[k], 0)))) return rc;
+    MatvecArgs<double> a{dw + r0 * rb, rb, (int)n, (int)cols, dx, 0, dy + r0, 0};
+    if ((rc = launch_mv_generic<double, 1>(type_id, a, st.stream))) return rc > 0 ? PYRITE_E_CUDA : rc;
+  }
   if ((rc = cuda_code(cudaMemcpyAsync(out, dy, rows * sizeof(double), cudaMemcpyDeviceToHost, st.stream))))
     return rc;
   return cuda_code(cudaStreamSynchronize(st.stream));

@@ -288,14 +288,16 @@ __device__ __forceinline__ void words8(const Dig16& lo, const Dig16& hi, bool pl
   w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = c.x; w[5] = c.y; w[6] = c.z; w[7] = c.w;
 }
 
-// Q8_0: d | int8 qs[32]  (native.c:330-336).  One unit per block.  34-byte
-// blocks sit 0 or 2 bytes past a word boundary; with the lane's digits
+// Q8_0: d | int8 qs[32]  (native.c:330-336); Q8_1: d | s | int8 qs[32]
+// (native.c:338-344, s unused by the decode).  One unit per block.  34-byte
+// Q8_0 blocks sit 0 or 2 bytes past a word boundary; with the lane's digits
 // shifted to match, the 9 aligned words feed dp4a directly.
-struct UnitQ80 {
-  static constexpr int UPB = 1, VALS = 32;
+template <int TY>
+struct UnitQ8 {
+  static constexpr int UPB = 1, VALS = 32, QS = TY == Q8_1 ? 4 : 2, BPB = Geo<TY>::bpb;
   struct XU { uint32_t a[9], b[9]; float s; };
   __device__ static void load_x(const XView& x, int unit, XU& u, int wmod4, bool& wide) {
-    const int mis = (wmod4 + 34 * unit + 2) & 3;  // offset of qs past a word boundary
+    const int mis = (wmod4 + BPB * unit + QS) & 3;  // offset of qs past a word boundary
     const Dig16 lo = dig16(x, 32 * unit), hi = dig16(x, 32 * unit + 16);
     uint32_t w[8];
     words8(lo, hi, false, w);
@@ -307,7 +309,7 @@ struct UnitQ80 {
     u.s = fabsf(s);
   }
   __device__ static float dot(uint32_t blk, int, const XU& u, int) {
-    const uint32_t base = (blk + 2) & ~3u;
+    const uint32_t base = (blk + QS) & ~3u;
     int a0 = 0, a1 = 0, b0 = 0, b1 = 0;
 #pragma unroll
     for (int k = 0; k < 9; k += 2) {
@@ -491,11 +493,116 @@ struct UnitIQ4XS {
   }
 };
 
+// The 32-value blocks with 16 bytes of nibble codes (native.c:281-328, 351-358):
+//   Q4_0   d | qs[16]              value d*(q - 8)
+//   Q4_1   d | m | qs[16]          value d*q + m
+//   Q5_0   d | qh[4] | qs[16]      value d*(q5 - 16), q5 = q | bit i of qh << 4
+//   Q5_1   d | m | qh[4] | qs[16]  value d*q5 + m
+//   IQ4_NL d | qs[16]              value d*book[q]
+// Byte i of qs holds value i (low nibble) and value 16+i (high nibble).  One
+// unit per block.  The offsets (-8, -16, m) multiply the exact fp32 sum of the
+// block's x, so the digit planes see only d*q.  18- and 22-byte blocks sit 0
+// or 2 bytes past a word boundary: the five aligned words around qs are
+// funnel-shifted by the block's own misalignment (read from its address).
+// IQ4_NL looks its codes up as IQ4_XS does (two sign-replicating byte
+// permutes summed through dp4a), with the digits interleaved to match.
+template <int TY>
+struct UnitLegacy {
+  static constexpr int UPB = 1, VALS = 32;
+  static constexpr int QS = TY == Q4_1 ? 4 : TY == Q5_0 ? 6 : TY == Q5_1 ? 8 : 2;  // offset of qs
+  static constexpr bool A4 = Geo<TY>::bpb % 4 == 0;  // blocks keep the row's word alignment
+  static constexpr bool NL = TY == IQ4_NL, Q5 = TY == Q5_0 || TY == Q5_1, MIN = TY == Q4_1 || TY == Q5_1;
+  struct XU { uint32_t a[8], b[8]; float s, m; };
+  __device__ static void load_x(const XView& x, int unit, XU& u, int, bool& wide) {
+    const Dig16 lo = dig16(x, 32 * unit), hi = dig16(x, 32 * unit + 16);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if constexpr (NL) {
+        u.a[2 * k] = __byte_perm(w4(lo.a, k), w4(hi.a, k), 0x5140);
+        u.a[2 * k + 1] = __byte_perm(w4(lo.a, k), w4(hi.a, k), 0x7362);
+        u.b[2 * k] = __byte_perm(w4(lo.b, k), w4(hi.b, k), 0x5140);
+        u.b[2 * k + 1] = __byte_perm(w4(lo.b, k), w4(hi.b, k), 0x7362);
+      } else {
+        u.a[k] = w4(lo.a, k); u.a[4 + k] = w4(hi.a, k);
+        u.b[k] = w4(lo.b, k); u.b[4 + k] = w4(hi.b, k);
+      }
+    }
+    const float s = *(x.scale + unit);
+    wide |= s < 0.f;
+    u.s = fabsf(s);
+    u.m = *(x.sum16 + 2 * unit) + *(x.sum16 + 2 * unit + 1);
+  }
+  // bits 4j..4j+3 of v, one per byte (bit 0 of bytes 0..3)
+  __device__ static uint32_t spread4(uint32_t v) { return ((v & 15u) * 0x00204081u) & 0x01010101u; }
+  __device__ static float dot(uint32_t blk, int, const XU& u, int) {
+    uint32_t q[4];
+    if constexpr (A4) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) q[k] = lds32(blk + QS + 4 * k);
+    } else {
+      const uint32_t base = (blk + QS) & ~3u, sh = ((blk + QS) & 3u) * 8u;
+      uint32_t w[5];
+#pragma unroll
+      for (int k = 0; k < 5; ++k) w[k] = lds32(base + 4 * k);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) q[k] = __funnelshift_r(w[k], w[k + 1], sh);
+    }
+    int a = 0, b = 0, a1 = 0, b1 = 0;
+    if constexpr (NL) {
+      constexpr uint32_t N0 = 0xBFAD9881u, N1 = 0xF6EADDCFu;  // book[0..7] (see UnitIQ4XS)
+      constexpr uint32_t P0 = 0x271A0E02u, P1 = 0x725A4636u;  // book[8..15] + 1
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t f = q[k] ^ 0x88888888u;
+        const uint32_t n0 = prmt_sx(N0, N1, q[k]), p0 = prmt_sx(P0, P1, f);
+        const uint32_t n1 = prmt_sx(N0, N1, q[k] >> 16), p1 = prmt_sx(P0, P1, f >> 16);
+        a = __dp4a((int)n0, (int)u.a[2 * k], a);
+        b = __dp4a((int)n0, (int)u.b[2 * k], b);
+        a1 = __dp4a((int)n1, (int)u.a[2 * k + 1], a1);
+        b1 = __dp4a((int)n1, (int)u.b[2 * k + 1], b1);
+        a = __dp4a((int)p0, (int)u.a[2 * k], a);
+        b = __dp4a((int)p0, (int)u.b[2 * k], b);
+        a1 = __dp4a((int)p1, (int)u.a[2 * k + 1], a1);
+        b1 = __dp4a((int)p1, (int)u.b[2 * k + 1], b1);
+      }
+    } else {
+      uint32_t qh = 0;
+      if constexpr (Q5) {  // qh sits just before qs (2-byte aligned for Q5_0)
+        const uint32_t ha = blk + QS - 4, hb = ha & ~3u;
+        qh = (ha & 3u) ? __funnelshift_r(lds32(hb), lds32(hb + 4), (ha & 3u) * 8u) : lds32(hb);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint32_t lo = q[k] & 0x0F0F0F0Fu, hi = (q[k] >> 4) & 0x0F0F0F0Fu;
+        if constexpr (Q5) {
+          lo |= spread4(qh >> (4 * k)) << 4;
+          hi |= spread4(qh >> (16 + 4 * k)) << 4;
+        }
+        a = __dp4a((int)lo, (int)u.a[k], a);
+        b = __dp4a((int)lo, (int)u.b[k], b);
+        a1 = __dp4a((int)hi, (int)u.a[4 + k], a1);
+        b1 = __dp4a((int)hi, (int)u.b[4 + k], b1);
+      }
+    }
+    const float d = half_f(lds16(blk));
+    const float t = u.s * (float)((a + a1) * 254 + (b + b1));
+    if constexpr (MIN) return d * t + half_f(lds16(blk + 2)) * u.m;
+    else if constexpr (TY == Q4_0) return d * (t - 8.0f * u.m);
+    else if constexpr (TY == Q5_0) return d * (t - 16.0f * u.m);
+    else return d * t;
+  }
+};
 
 template <int TY> struct UnitOf;
 template <> struct UnitOf<Q4_K> { using T = UnitK45<Q4_K>; };
 template <> struct UnitOf<Q5_K> { using T = UnitK45<Q5_K>; };
-template <> struct UnitOf<Q8_0> { using T = UnitQ80; };
+template <> struct UnitOf<Q8_0> { using T = UnitQ8<Q8_0>; };
+template <> struct UnitOf<Q8_1> { using T = UnitQ8<Q8_1>; };
+template <> struct UnitOf<Q4_0> { using T = UnitLegacy<Q4_0>; };
+template <> struct UnitOf<Q4_1> { using T = UnitLegacy<Q4_1>; };
+template <> struct UnitOf<Q5_0> { using T = UnitLegacy<Q5_0>; };
+template <> struct UnitOf<Q5_1> { using T = UnitLegacy<Q5_1>; };
+template <> struct UnitOf<IQ4_NL> { using T = UnitLegacy<IQ4_NL>; };
 template <> struct UnitOf<Q6_K> { using T = UnitQ6K<false>; };
 template <> struct UnitOf<kQ6KRealign> { using T = UnitQ6K<true>; };
 template <> struct UnitOf<IQ4_XS> { using T = UnitIQ4XS; };
@@ -611,10 +718,22 @@ template <int TY, int UL> constexpr int tile_min_blocks() {
 // The part of 32 weights (unit u of block b) that the streaming loop multiplies
 // by the encoded x: d*sc*q, without the offsets it applies to the exact fp32
 // sums of x (Q4_K / Q5_K: dmin*m, native.c:173-197 and 410-437; Q6_K: the
-// -32 of d*sc*(q - 32), native.c:199-225).  Q8_0 and IQ4_XS have no offset.
+// -32 of d*sc*(q - 32), native.c:199-225; Q4_0 / Q5_0: the -8 / -16, Q4_1 /
+// Q5_1: m, native.c:281-328).  Q8_0, Q8_1, IQ4_NL and IQ4_XS have no offset.
 template <int TY>
 __device__ __forceinline__ void code_part(const uint8_t* b, int u, float (&v)[32]) {
-  if constexpr (TY == Q4_K || TY == Q5_K) {
+  if constexpr (TY == Q4_0 || TY == Q4_1 || TY == Q5_0 || TY == Q5_1) {
+    constexpr int QS = UnitLegacy<TY>::QS;
+    const float d = half_val<float>(ld_u16(b));
+    const uint32_t qh = (TY == Q5_0 || TY == Q5_1) ? ld_u32(b + QS - 4) : 0u;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int lo = (b[QS + i] & 15) | (int)(((qh >> i) & 1u) << 4);
+      const int hi = (b[QS + i] >> 4) | (int)(((qh >> (16 + i)) & 1u) << 4);
+      v[i] = d * (float)lo;
+      v[16 + i] = d * (float)hi;
+    }
+  } else if constexpr (TY == Q4_K || TY == Q5_K) {
     int sc, mn;
     k4_scale_min(b + 4, u, sc, mn);
     const float d1 = half_val<float>(ld_u16(b)) * (float)sc;
@@ -1033,9 +1152,13 @@ bool lane_supported(int type_id, const uint8_t* w, size_t row_bytes, int cols) {
     case Q4_K: case Q5_K: return (base & 15) == 0 && (row_bytes & 15) == 0;
     // the shifted-digit decoders need 2-byte aligned blocks; Q8_0 rows keep the
     // word alignment, Q6_K rows may alternate (a realigning instantiation)
-    case Q8_0: return (base & 1) == 0 && (row_bytes & 3) == 0;
+    case Q8_0: case Q8_1: return (base & 1) == 0 && (row_bytes & 3) == 0;
     case Q6_K: return (base & 1) == 0;
     case IQ4_XS: return (base & 7) == 0;
+    // 32-value blocks: rows of a multiple of 256 columns are 16-byte multiples;
+    // 18 / 22-byte blocks need 2-byte, 20 / 24-byte blocks 4-byte alignment
+    case Q4_0: case Q5_0: case IQ4_NL: return (base & 1) == 0;
+    case Q4_1: case Q5_1: return (base & 3) == 0;
     default: return false;
   }
 }
@@ -1078,6 +1201,12 @@ int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, in
       return (row_bytes & 3) ? launch_tile_type<kQ6KRealign>(ta, p.ul, p.smem, stream)
                              : launch_tile_type<Q6_K>(ta, p.ul, p.smem, stream);
     case IQ4_XS: return launch_tile_type<IQ4_XS>(ta, p.ul, p.smem, stream);
+    case Q8_1: return launch_tile_type<Q8_1>(ta, p.ul, p.smem, stream);
+    case Q4_0: return launch_tile_type<Q4_0>(ta, p.ul, p.smem, stream);
+    case Q4_1: return launch_tile_type<Q4_1>(ta, p.ul, p.smem, stream);
+    case Q5_0: return launch_tile_type<Q5_0>(ta, p.ul, p.smem, stream);
+    case Q5_1: return launch_tile_type<Q5_1>(ta, p.ul, p.smem, stream);
+    case IQ4_NL: return launch_tile_type<IQ4_NL>(ta, p.ul, p.smem, stream);
     default: return 1;
   }
 }

@@ -36,6 +36,7 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--vocab", type=int, default=None)
     ap.add_argument("--new", type=int, default=8)
+    ap.add_argument("--prompt", type=int, default=16)
     ap.add_argument("--out", default="c1_decode.json")
     args = ap.parse_args()
 
@@ -65,7 +66,7 @@ def main() -> None:
     builder.write(path)
     print(f"wrote {path} ({path.stat().st_size} bytes) in {time.time() - t0:.1f}s", flush=True)
 
-    ids = prompt_ids(spec)
+    ids = prompt_ids(spec, n=args.prompt)
     cfg = RuntimeConfig(ram_budget_mb=32768, max_context_tokens=512, max_kv_tokens=512)
     top: list[list[list[float]]] = []
     with open_executor(path, config=cfg, sampler_seed=0) as ex:

@@ -125,3 +125,9 @@ def test_llama_q4_k_m_tiny_decode_matches_reference(cuda_device):
 def test_c3_llama_8b_q4_k_m_two_layers_matches_reference(cuda_device):
     """configs[2] at full width (hidden 4096, ffn 14336, vocab 128256), 2 layers."""
     _check_mixed("c3_2l.json", cuda_device)
+
+
+def test_c3_llama_8b_two_layers_over_a_128_position_window(cuda_device):
+    """The same checkpoint, 120-token prompt and 8 greedy tokens: greedy ids and
+    the top logits of all 127 passes against the reference executor."""
+    _check_mixed("c3_2l_w128.json", cuda_device)

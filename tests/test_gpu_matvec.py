@@ -128,7 +128,7 @@ def test_device_matvec_ragged_shapes(cuda_device, ggml_type, rows, cols):
 
 
 @pytest.mark.parametrize("offset", [2, 4, 8, 6, 14])
-@pytest.mark.parametrize("ggml_type", [8, 12, 13, 14, 23, 2, 10, 11])
+@pytest.mark.parametrize("ggml_type", [8, 12, 13, 14, 23, 2, 10, 11, 3, 6, 7, 9, 20])
 def test_device_matvec_unaligned_payloads(cuda_device, ggml_type, offset):
     rows, cols = 19, 2048
     payload = random_payload(ggml_type, rows, cols, seed=offset)
@@ -167,7 +167,7 @@ def test_device_row_ranges_are_independent(cuda_device):
         assert torch.equal(full, parts)
 
 
-@pytest.mark.parametrize("ggml_type", [8, 12, 13, 14, 23, 2, 30])
+@pytest.mark.parametrize("ggml_type", [8, 12, 13, 14, 23, 2, 30, 3, 6, 7, 9, 20])
 def test_prepared_x_path_matches_one_shot_matvec(cuda_device, ggml_type):
     """One encoding of x shared by several matrices gives the one-shot results."""
     torch = _torch()

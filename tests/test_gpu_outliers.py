@@ -91,6 +91,39 @@ def test_matvec_and_prepared_with_outlier_channels(cuda_device, ggml_type, rows,
     check(ggml_type, payload, x, y2.cpu().numpy(), rows, cols, oc, "pyrite_cuda_matvec_prepared")
 
 
+LEGACY = [2, 3, 6, 7, 9, 20]  # Q4_0, Q4_1, Q5_0, Q5_1, Q8_1, IQ4_NL: 32-value blocks on the tile kernel
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,cols", [(256, 4096), (128, 14336), (96, 768)])
+@pytest.mark.parametrize("ggml_type", LEGACY)
+def test_legacy_blocks_with_outlier_channels(cuda_device, ggml_type, rows, cols):
+    """The 32-value block formats on the batch-1 tile kernel, whose wide-block
+    pass multiplies the third digits by d*q without the block's offset (-8,
+    -16 or m, applied to the exact fp32 sums of x).  Q4_0 and IQ4_NL weights
+    come from the package's quantizers with the outlier columns zeroed; the
+    formats without an encoder use seeded random blocks (non-zero weights on the
+    outlier columns, whose digits the encoding carries exactly)."""
+    import torch
+
+    from pyrite_b200.kernels import cuda as K
+    from pyrite_b200.quantize import quantize_types
+    from tests.payloads import random_payload
+    x, oc = outlier_x(cols, seed=5 * cols + ggml_type)
+    if ggml_type in quantize_types():
+        payload = payload_zero_on(ggml_type, rows, cols, oc, seed=rows * 3 + cols)
+    else:
+        payload = random_payload(ggml_type, rows, cols, seed=rows * 3 + cols)
+    w = torch.frombuffer(bytearray(payload), dtype=torch.uint8).cuda()
+    xd = torch.from_numpy(x).cuda()
+    y = K.matvec(ggml_type, w, xd, rows, cols)
+    y2 = K.matvec_prepared(ggml_type, w, K.prepare_x(xd), rows, cols)
+    torch.cuda.synchronize()
+    assert K.status() == 0
+    check(ggml_type, payload, x, y.cpu().numpy(), rows, cols, oc, "pyrite_cuda_matvec")
+    check(ggml_type, payload, x, y2.cpu().numpy(), rows, cols, oc, "pyrite_cuda_matvec_prepared")
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("rows,cols", [(256, 4096), (128, 14336), (64, 1024)])
 @pytest.mark.parametrize("ggml_type", TYPES)

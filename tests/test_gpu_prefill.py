@@ -30,7 +30,7 @@ def _dense_spec(g):
     return DenseSpec(**{k: v for k, v in g["spec"].items() if k in {f.name for f in fields(DenseSpec)}})
 
 
-@pytest.mark.parametrize("golden", ["c1_small.json", "llama_tiny.json", "c3_2l.json"])
+@pytest.mark.parametrize("golden", ["c1_small.json", "llama_tiny.json", "c3_2l.json", "c3_2l_w128.json"])
 @pytest.mark.parametrize("block", [64, 5, 1])
 def test_prefilled_decode_matches_reference_greedy_ids(cuda_device, golden, block):
     import torch
