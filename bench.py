@@ -539,7 +539,7 @@ def types_leg(dev, stream, shapes=((14336, 4096), (4096, 14336))) -> dict:
     """Batch-1 throughput of every other decodable type on the large configs[1]
     shapes, timed like the step's per-kernel lines (each matrix rotating over
     > 512 MB of copies inside one CUDA graph, events on its stream).  Q4_0,
-    Q4_1, Q5_0, Q5_1, Q8_1 and IQ4_NL run the tile kernel; Q2_K, Q3_K and the
+    Q4_1, Q5_0, Q5_1, Q8_1, IQ4_NL, Q2_K and Q3_K run the tile kernel; the
     float formats the warp-per-row kernel."""
     import torch
 
@@ -572,7 +572,7 @@ def types_leg(dev, stream, shapes=((14336, 4096), (4096, 14336))) -> dict:
             us = e0.elapsed_time(e1) * 1e3 / (2 * copies)
             out.append({"type": name, "rows": r, "cols": c, "us": round(us, 3),
                         "GBps": round(algo_bytes(t, r, c) / (us * 1e-6) / 1e9, 1),
-                        "kernel": "mv_tile_kernel" if t in (2, 3, 6, 7, 9, 20) else "mv_generic_kernel"})
+                        "kernel": "mv_tile_kernel" if t in (2, 3, 6, 7, 9, 10, 11, 20) else "mv_generic_kernel"})
             del g, bufs, src
             torch.cuda.empty_cache()
     if K.status() != 0:

@@ -1,8 +1,9 @@
 // mv_tile.cu -- batch-1 fused dequantize x matvec for the main GGML formats.
 //
 // y = W x, the product of the reference's pyrite_matvec
-// (pyrite/kernels/native.c:518-555), fp32 out, for Q8_0, Q4_K, Q5_K, Q6_K and
-// IQ4_XS.  The path is HBM-bound (~2 flop per weight byte); everything here
+// (pyrite/kernels/native.c:518-555), fp32 out, for every GGML block format:
+// Q8_0, Q4_K, Q5_K, Q6_K, IQ4_XS and Q2_K, Q3_K, Q4_0, Q4_1, Q5_0, Q5_1, Q8_1,
+// IQ4_NL.  The path is HBM-bound (~2 flop per weight byte); everything here
 // serves one goal: stream every weight byte once, at full bandwidth, while
 // keeping the per-byte instruction count low.
 //
@@ -593,6 +594,99 @@ struct UnitLegacy {
   }
 };
 
+// Sum over one 16-value sub-block: 254 * dot(codes, x0) + dot(codes, x1), the
+// four code words c against digit words k0..k0+3 of one 32-value run.
+__device__ __forceinline__ int dot16w(const uint32_t (&c)[8], int k0, const Dig32& d) {
+  int a0 = __dp4a((int)c[k0], (int)d.a[k0], 0), a1 = __dp4a((int)c[k0 + 1], (int)d.a[k0 + 1], 0);
+  int b0 = __dp4a((int)c[k0], (int)d.b[k0], 0), b1 = __dp4a((int)c[k0 + 1], (int)d.b[k0 + 1], 0);
+  a0 = __dp4a((int)c[k0 + 2], (int)d.a[k0 + 2], a0);
+  a1 = __dp4a((int)c[k0 + 3], (int)d.a[k0 + 3], a1);
+  b0 = __dp4a((int)c[k0 + 2], (int)d.b[k0 + 2], b0);
+  b1 = __dp4a((int)c[k0 + 3], (int)d.b[k0 + 3], b1);
+  return (a0 + a1) * 254 + (b0 + b1);
+}
+
+// Q2_K: scales[16] | qs[64] | d | dmin  (native.c:381-408) and Q3_K: hmask[32]
+// | qs[64] | scales[12] | d  (native.c:129-171).  Value 128h+32g+l takes the
+// 2-bit code (qs[32h+l] >> 2g) & 3; Q3_K adds bit 4h+g of hmask[l] as bit 2
+// and subtracts 4.  A unit is 64 values (h, p), g = 2p and 2p+1: both read the
+// same 32 qs (and hmask) bytes, at shifts 4p and 4p+2, so each byte is loaded
+// once, and the unit's four 16-value sub-blocks have their scales in four
+// consecutive bytes.  The offsets (Q2_K: dmin*m; Q3_K: -4) multiply the exact
+// fp32 sums of x.  Q2_K blocks (84 bytes) keep the row's word alignment; Q3_K
+// blocks (110 bytes) sit 0 or 2 bytes past a word boundary and their words are
+// funnel-shifted by that misalignment, read from the block's address.
+template <int TY>
+struct UnitK23 {
+  static constexpr int UPB = 4, VALS = 64;
+  struct XU { Dig32 lo, hi; float slo, shi; float m[4]; };
+  __device__ static void load_x(const XView& x, int unit, XU& u, int, bool& wide) {
+    const int ca = 256 * (unit >> 2) + 64 * (unit & 3), cb = ca + 32;
+    dig32(x, ca, u.lo);
+    dig32(x, cb, u.hi);
+    const float sa = *(x.scale + (ca >> 5)), sb = *(x.scale + (cb >> 5));
+    wide |= (sa < 0.f) | (sb < 0.f);
+    u.slo = fabsf(sa);
+    u.shi = fabsf(sb);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) u.m[i] = *(x.sum16 + (ca >> 4) + i);
+  }
+  __device__ static float dot(uint32_t blk, int j, const XU& u, int) {
+    const int h = j >> 1, p = j & 1;
+    uint32_t q[8], c0[8], c1[8];
+    if constexpr (TY == Q2_K) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) q[k] = lds32(blk + 16 + 32 * h + 4 * k);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        c0[k] = (q[k] >> (4 * p)) & 0x03030303u;
+        c1[k] = (q[k] >> (4 * p + 2)) & 0x03030303u;
+      }
+      const uint32_t sc = lds32(blk + 8 * h + 4 * p);  // scale | min << 4, one byte per sub-block
+      const uint32_t dd = lds32(blk + 80);             // d | dmin
+      const float r = u.slo * ((float)(sc & 15u) * (float)dot16w(c0, 0, u.lo) +
+                               (float)((sc >> 8) & 15u) * (float)dot16w(c0, 4, u.lo)) +
+                      u.shi * ((float)((sc >> 16) & 15u) * (float)dot16w(c1, 0, u.hi) +
+                               (float)((sc >> 24) & 15u) * (float)dot16w(c1, 4, u.hi));
+      const float mins = (float)((sc >> 4) & 15u) * u.m[0] + (float)((sc >> 12) & 15u) * u.m[1] +
+                         (float)((sc >> 20) & 15u) * u.m[2] + (float)(sc >> 28) * u.m[3];
+      return half_f(dd & 0xffffu) * r - half_f(dd >> 16) * mins;
+    } else {
+      const uint32_t sh = (blk & 3u) * 8u;  // 0 or 16: every field keeps the block's misalignment
+      const uint32_t qb = (blk + 32 + 32 * h) & ~3u, hb = blk & ~3u, sb = (blk + 96) & ~3u;
+      uint32_t hm[8];
+      uint32_t wq = lds32(qb), wh = lds32(hb);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t nq = lds32(qb + 4 * k + 4), nh = lds32(hb + 4 * k + 4);
+        q[k] = __funnelshift_r(wq, nq, sh);
+        hm[k] = __funnelshift_r(wh, nh, sh);
+        wq = nq;
+        wh = nh;
+      }
+      const int hs = 4 * h + 2 * p;  // hmask bit of g = 2p (g = 2p+1: the next bit)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        c0[k] = ((q[k] >> (4 * p)) & 0x03030303u) | (((hm[k] >> hs) & 0x01010101u) << 2);
+        c1[k] = ((q[k] >> (4 * p + 2)) & 0x03030303u) | (((hm[k] >> (hs + 1)) & 0x01010101u) << 2);
+      }
+      // the unit's scales k = 8h+4p .. 8h+4p+3: low 4 bits from bytes 4p..4p+3
+      // (low nibbles for h = 0, high for h = 1), high 2 bits from bytes 8..11
+      // at shift 2(2h+p); 6-bit values biased by 32
+      const uint32_t s0 = lds32(sb), s1 = lds32(sb + 4), s2 = lds32(sb + 8), s3 = lds32(sb + 12);
+      const uint32_t lw = p ? __funnelshift_r(s1, s2, sh) : __funnelshift_r(s0, s1, sh);
+      const uint32_t hw = __funnelshift_r(s2, s3, sh);
+      const uint32_t sc = ((lw >> (4 * h)) & 0x0F0F0F0Fu) | (((hw >> (2 * (2 * h + p))) & 0x03030303u) << 4);
+      const float f0 = (float)((int)(sc & 63u) - 32), f1 = (float)((int)((sc >> 8) & 63u) - 32);
+      const float f2 = (float)((int)((sc >> 16) & 63u) - 32), f3 = (float)((int)(sc >> 24) - 32);
+      const float r = u.slo * (f0 * (float)dot16w(c0, 0, u.lo) + f1 * (float)dot16w(c0, 4, u.lo)) +
+                      u.shi * (f2 * (float)dot16w(c1, 0, u.hi) + f3 * (float)dot16w(c1, 4, u.hi));
+      const float offs = f0 * u.m[0] + f1 * u.m[1] + f2 * u.m[2] + f3 * u.m[3];
+      return half_f(lds16(blk + 108)) * (r - 4.0f * offs);
+    }
+  }
+};
+
 template <int TY> struct UnitOf;
 template <> struct UnitOf<Q4_K> { using T = UnitK45<Q4_K>; };
 template <> struct UnitOf<Q5_K> { using T = UnitK45<Q5_K>; };
@@ -603,6 +697,8 @@ template <> struct UnitOf<Q4_1> { using T = UnitLegacy<Q4_1>; };
 template <> struct UnitOf<Q5_0> { using T = UnitLegacy<Q5_0>; };
 template <> struct UnitOf<Q5_1> { using T = UnitLegacy<Q5_1>; };
 template <> struct UnitOf<IQ4_NL> { using T = UnitLegacy<IQ4_NL>; };
+template <> struct UnitOf<Q2_K> { using T = UnitK23<Q2_K>; };
+template <> struct UnitOf<Q3_K> { using T = UnitK23<Q3_K>; };
 template <> struct UnitOf<Q6_K> { using T = UnitQ6K<false>; };
 template <> struct UnitOf<kQ6KRealign> { using T = UnitQ6K<true>; };
 template <> struct UnitOf<IQ4_XS> { using T = UnitIQ4XS; };
@@ -712,17 +808,42 @@ struct TileArgs {
 // and their stages (32 KB for the 4096 x 14336 shapes) fit two CTAs per SM
 // anyway (Q4_K: -3% on 4096 x 14336 with 128 registers, no change elsewhere).
 template <int TY, int UL> constexpr int tile_min_blocks() {
-  return (TY == Q6_K || TY == kQ6KRealign || TY == Q4_K || UL >= 2) ? 2 : 3;
+  return (TY == Q6_K || TY == kQ6KRealign || TY == Q4_K || TY == Q2_K || TY == Q3_K || UL >= 2) ? 2 : 3;
 }
 
 // The part of 32 weights (unit u of block b) that the streaming loop multiplies
 // by the encoded x: d*sc*q, without the offsets it applies to the exact fp32
 // sums of x (Q4_K / Q5_K: dmin*m, native.c:173-197 and 410-437; Q6_K: the
 // -32 of d*sc*(q - 32), native.c:199-225; Q4_0 / Q5_0: the -8 / -16, Q4_1 /
-// Q5_1: m, native.c:281-328).  Q8_0, Q8_1, IQ4_NL and IQ4_XS have no offset.
+// Q5_1: m, native.c:281-328; Q2_K: dmin*m, native.c:381-408; Q3_K: the -4 of
+// d*sc*(q - 4), native.c:129-171).  Q8_0, Q8_1, IQ4_NL and IQ4_XS have no offset.
 template <int TY>
 __device__ __forceinline__ void code_part(const uint8_t* b, int u, float (&v)[32]) {
-  if constexpr (TY == Q4_0 || TY == Q4_1 || TY == Q5_0 || TY == Q5_1) {
+  if constexpr (TY == Q2_K) {
+    const float d = half_val<float>(ld_u16(b + 80));
+    const int h = u >> 2, g = u & 3;
+#pragma unroll
+    for (int l = 0; l < 32; ++l) {
+      const int sc = b[8 * h + 2 * g + (l >> 4)] & 15;
+      v[l] = d * (float)sc * (float)((b[16 + 32 * h + l] >> (2 * g)) & 3);
+    }
+  } else if constexpr (TY == Q3_K) {
+    const float d = half_val<float>(ld_u16(b + 108));
+    const int h = u >> 2, g = u & 3;
+    float dl[2];
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int k = 8 * h + 2 * g + s;
+      const int low = (k < 8) ? (b[96 + k] & 15) : (b[96 + k - 8] >> 4);
+      const int high = (b[104 + (k & 3)] >> (2 * (k >> 2))) & 3;
+      dl[s] = d * (float)((low | (high << 4)) - 32);
+    }
+#pragma unroll
+    for (int l = 0; l < 32; ++l) {
+      const int q = ((b[32 + 32 * h + l] >> (2 * g)) & 3) | (((b[l] >> (4 * h + g)) & 1) << 2);
+      v[l] = dl[l >> 4] * (float)q;
+    }
+  } else if constexpr (TY == Q4_0 || TY == Q4_1 || TY == Q5_0 || TY == Q5_1) {
     constexpr int QS = UnitLegacy<TY>::QS;
     const float d = half_val<float>(ld_u16(b));
     const uint32_t qh = (TY == Q5_0 || TY == Q5_1) ? ld_u32(b + QS - 4) : 0u;
@@ -1129,7 +1250,11 @@ int launch_tile_type(const TileArgs& ta, int ul, size_t smem, cudaStream_t strea
     return 1;
   }
   PYR_UM(1, 1) PYR_UM(1, 2) PYR_UM(1, 4) PYR_UM(1, 8) PYR_UM(2, 1) PYR_UM(2, 2) PYR_UM(2, 4)
-  PYR_UM(3, 1) PYR_UM(3, 2) PYR_UM(4, 1) PYR_UM(4, 2)
+  // three or four units per lane: only 32-value units reach them (rows of at
+  // most 32768 columns are at most 512 64-value units, two per lane)
+  if constexpr (UnitOf<TY>::T::VALS == 32) {
+    PYR_UM(3, 1) PYR_UM(3, 2) PYR_UM(4, 1) PYR_UM(4, 2)
+  }
 #undef PYR_UM
   return 1;
 }
@@ -1159,6 +1284,9 @@ bool lane_supported(int type_id, const uint8_t* w, size_t row_bytes, int cols) {
     // 18 / 22-byte blocks need 2-byte, 20 / 24-byte blocks 4-byte alignment
     case Q4_0: case Q5_0: case IQ4_NL: return (base & 1) == 0;
     case Q4_1: case Q5_1: return (base & 3) == 0;
+    // 84-byte Q2_K blocks keep word alignment; 110-byte Q3_K blocks need 2 bytes
+    case Q2_K: return (base & 3) == 0;
+    case Q3_K: return (base & 1) == 0;
     default: return false;
   }
 }
@@ -1175,7 +1303,7 @@ int launch_xprep(const float* x, long long ldx, int cols, int ncols, uint8_t* ws
 int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, int cols, const uint8_t* ws,
                    float* y, bool static_weights, cudaStream_t stream, bool accumulate, const PostArgs* post,
                    const ExpertArgs* ex, const XPrologue* xp) {
-  const int vals = (type_id == Q6_K || type_id == Q4_K || type_id == Q5_K) ? 64 : 32;
+  const int vals = (type_id == Q6_K || type_id == Q4_K || type_id == Q5_K || type_id == Q2_K || type_id == Q3_K) ? 64 : 32;
   const size_t xenc = xp ? ((lane_workspace_bytes(cols) + 255) & ~(size_t)255) : 0;
   const TilePlan p = plan_tile(row_bytes, rows, cols, vals, xenc);
   TileArgs ta{w, row_bytes, rows, cols, ws, y, p.rs, p.lps, p.m, p.stage_bytes, p.slots, static_weights ? 1 : 0,
@@ -1207,6 +1335,8 @@ int launch_mv_lane(int type_id, const uint8_t* w, size_t row_bytes, int rows, in
     case Q5_0: return launch_tile_type<Q5_0>(ta, p.ul, p.smem, stream);
     case Q5_1: return launch_tile_type<Q5_1>(ta, p.ul, p.smem, stream);
     case IQ4_NL: return launch_tile_type<IQ4_NL>(ta, p.ul, p.smem, stream);
+    case Q2_K: return launch_tile_type<Q2_K>(ta, p.ul, p.smem, stream);
+    case Q3_K: return launch_tile_type<Q3_K>(ta, p.ul, p.smem, stream);
     default: return 1;
   }
 }

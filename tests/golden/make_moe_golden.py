@@ -67,16 +67,42 @@ def main() -> None:
     cfg = RuntimeConfig(ram_budget_mb=32768, max_context_tokens=512, max_kv_tokens=512)
     top: list[list[list[float]]] = []
     experts: list[list[list[int]]] = []
+    # per pass and layer: the router logits' gap between the last chosen expert
+    # and the first one left out (softmax is monotone, so this is the routing
+    # decision's margin), and that runner-up expert
+    margins: list[list[float]] = []
+    order_margins: list[list[float]] = []  # smallest gap between consecutive chosen experts
+    runner_up: list[list[int]] = []
+    routers: dict[int, list[float]] = {}
+    k = spec.num_experts_per_tok
     with open_executor(path, config=cfg, sampler_seed=0) as ex:
         original = ex.logits
+        original_matvec = ex._tensor_matvec
+
+        def router_matvec(name, rows, cols, vector):
+            out = original_matvec(name, rows, cols, vector)
+            if name.endswith(".ffn_gate_inp.weight"):
+                routers[int(name.split(".")[1])] = list(out)
+            return out
 
         def recording(token_id: int, position: int) -> list[float]:
             out = original(token_id, position)
             order = sorted(range(len(out)), key=lambda i: -out[i])[:16]
             top.append([[i, out[i]] for i in order])
             experts.append([list(ex._last_experts.get(layer, ())) for layer in range(spec.num_hidden_layers)])
+            gaps, inner, nexts = [], [], []
+            for layer in range(spec.num_hidden_layers):
+                r = routers[layer]
+                ranked = sorted(range(len(r)), key=lambda e: (-r[e], e))
+                gaps.append(r[ranked[k - 1]] - r[ranked[k]])
+                inner.append(min(r[ranked[i]] - r[ranked[i + 1]] for i in range(k - 1)))
+                nexts.append(ranked[k])
+            margins.append(gaps)
+            order_margins.append(inner)
+            runner_up.append(nexts)
             return out
 
+        ex._tensor_matvec = router_matvec
         ex.logits = recording
         t1 = time.time()
         generated = ex.generate(ids, args.new, temperature=0.0)
@@ -87,6 +113,9 @@ def main() -> None:
         "generated": generated[len(ids):],
         "top_logits": top,
         "experts": experts,
+        "router_margin": margins,
+        "router_order_margin": order_margins,
+        "runner_up": runner_up,
         "reference_seconds": seconds,
         "reference_tokens_per_second": len(generated) / seconds,
         "generator": "tests/golden/make_moe_golden.py (reference pyrite.executor.open_executor, Qwen3MoEExecutor)",

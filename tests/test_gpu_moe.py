@@ -233,13 +233,51 @@ def _moe_spec(d):
     return MoESpec(**{k: v for k, v in d["spec"].items() if k in names})
 
 
-@pytest.mark.parametrize("golden", ["moe_tiny.json", "moe_c4_2l.json", "moe_c5_2l.json"])
+# Router-logit gap under which the reference's last chosen expert and its
+# runner-up are a tie at fp32 precision: the decode's hidden states differ from
+# the reference's fp64 ones by ~1e-5 relative, router logits are O(1).
+ROUTER_TIE = 1e-3
+
+
+def _tie_flip(route, g, step) -> bool:
+    """Compare one pass's routed experts with the reference's.  Equal lists
+    pass.  The same experts in another order must be a tie inside the top k
+    (the reference's smallest gap between consecutive chosen experts at most
+    ROUTER_TIE; the weighted sum is the same) and pass.  Any other difference
+    must be a tie at the top-k boundary -- the reference's margin between its
+    last chosen expert and the runner-up at most ROUTER_TIE, and the two
+    swapped -- and returns True: from there on (the later layers of the same
+    pass included, whose input the other experts changed) the two decodes
+    legitimately follow different branches, so the comparison stops (the
+    greedy ids of the whole window were compared already).  The margins come
+    from golden files that record them (``router_margin``,
+    ``router_order_margin``); without them any difference fails."""
+    want = g["experts"][step]
+    for layer, (a, b) in enumerate(zip(route, want)):
+        if a == b:
+            continue
+        assert "router_margin" in g, f"routing differs at pass {step}, layer {layer}: {a} vs {b}"
+        if sorted(a) == sorted(b):
+            gap = g["router_order_margin"][step][layer]
+            assert gap <= ROUTER_TIE, f"pass {step}, layer {layer}: order {a} vs {b} with a reference gap of {gap}"
+            continue
+        gap = g["router_margin"][step][layer]
+        assert gap <= ROUTER_TIE, f"routing differs at pass {step}, layer {layer} with a reference margin of {gap}"
+        assert sorted(a) == sorted(b[:-1] + [g["runner_up"][step][layer]]), \
+            f"pass {step}, layer {layer}: {a} is not the reference's choice {b} with its tie swapped"
+        return True
+    return False
+
+
+@pytest.mark.parametrize("golden", ["moe_tiny.json", "moe_c4_2l.json", "moe_c5_2l.json", "moe_c4_2l_w128.json",
+                                    "moe_c5_2l_w128.json"])
 def test_moe_decode_matches_reference(cuda_device, golden):
     """Greedy ids, routed experts of every layer of every pass and top logits;
     moe_c4_2l is configs[3] at full width (hidden 2048, 128 experts top-8,
     expert ffn 768, vocab 151936) with 2 layers, moe_c5_2l configs[4] at full
     width (hidden 4096, 64 q / 4 kv heads, 128 experts top-8, expert ffn 1536)
-    with 2 layers."""
+    with 2 layers; the _w128 files decode the same checkpoints over a
+    128-position window (120-token prompt, 8 greedy tokens)."""
     import torch
 
     from pyrite_b200.kernels import cuda as K
@@ -256,10 +294,14 @@ def test_moe_decode_matches_reference(cuda_device, golden):
     for step, top in enumerate(g["top_logits"][: len(prompt) + len(want) - 1]):
         dec.run_steps(1)
         torch.cuda.synchronize()
-        assert dec.route_log.cpu().tolist() == g["experts"][step], f"routing differs at pass {step}"
+        if _tie_flip(dec.route_log.cpu().tolist(), g, step):
+            break  # the state follows the other branch of a tie from here on
         logits = dec.logits.double().cpu()
         ids = [i for i, _ in top]
         vals = torch.tensor([v for _, v in top], dtype=torch.float64)
         assert int(torch.argmax(logits)) == ids[0]
         worst = max(worst, float((logits[ids] - vals).abs().max()))
-    assert worst <= 2e-3, f"max |logit - reference| = {worst}"
+    # the dense decoders' bound (tests/test_gpu_decode.py: the two-digit
+    # activation encoding carried through two layers of a 4096-wide model)
+    from tests.test_gpu_decode import LOGIT_TOL
+    assert worst <= LOGIT_TOL, f"max |logit - reference| = {worst}"

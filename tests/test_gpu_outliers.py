@@ -91,19 +91,22 @@ def test_matvec_and_prepared_with_outlier_channels(cuda_device, ggml_type, rows,
     check(ggml_type, payload, x, y2.cpu().numpy(), rows, cols, oc, "pyrite_cuda_matvec_prepared")
 
 
-LEGACY = [2, 3, 6, 7, 9, 20]  # Q4_0, Q4_1, Q5_0, Q5_1, Q8_1, IQ4_NL: 32-value blocks on the tile kernel
+# the other formats of the batch-1 tile kernel: Q4_0, Q4_1, Q5_0, Q5_1, Q8_1,
+# Q2_K, Q3_K, IQ4_NL
+MORE_TILE_TYPES = [2, 3, 6, 7, 9, 10, 11, 20]
 
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("rows,cols", [(256, 4096), (128, 14336), (96, 768)])
-@pytest.mark.parametrize("ggml_type", LEGACY)
-def test_legacy_blocks_with_outlier_channels(cuda_device, ggml_type, rows, cols):
-    """The 32-value block formats on the batch-1 tile kernel, whose wide-block
-    pass multiplies the third digits by d*q without the block's offset (-8,
-    -16 or m, applied to the exact fp32 sums of x).  Q4_0 and IQ4_NL weights
-    come from the package's quantizers with the outlier columns zeroed; the
-    formats without an encoder use seeded random blocks (non-zero weights on the
-    outlier columns, whose digits the encoding carries exactly)."""
+@pytest.mark.parametrize("ggml_type", MORE_TILE_TYPES)
+def test_more_tile_formats_with_outlier_channels(cuda_device, ggml_type, rows, cols):
+    """The other formats of the batch-1 tile kernel, whose wide-block pass
+    multiplies the third digits by the code part without the block's offset
+    (-8, -16, -4, m or dmin*m, applied to the exact fp32 sums of x).  Q4_0,
+    Q2_K, Q3_K and IQ4_NL weights come from the package's quantizers with the
+    outlier columns zeroed; the formats without an encoder use seeded random
+    blocks (non-zero weights on the outlier columns, whose digits the encoding
+    carries exactly)."""
     import torch
 
     from pyrite_b200.kernels import cuda as K

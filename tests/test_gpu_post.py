@@ -309,8 +309,8 @@ def test_matvec_transformed_rejects_bad_arguments(cuda_device):
                                               y.data_ptr(), 64, 256, 0, s) == -3
     assert lib.pyrite_cuda_matvec_transformed(8, w.data_ptr(), w.numel(), x.data_ptr(), 1, None, 1e-6, None, None, 0,
                                               y.data_ptr(), 64, 256, 0, s) == -3
-    w2, _, _ = _setup(10, 64, 256, 1)  # Q2_K: the warp-per-row kernel only
-    assert lib.pyrite_cuda_matvec_transformed(10, w2.data_ptr(), w2.numel(), x.data_ptr(), 2, None, 1e-6, None, None,
+    w2, _, _ = _setup(1, 64, 256, 1)  # F16: the warp-per-row kernel only
+    assert lib.pyrite_cuda_matvec_transformed(1, w2.data_ptr(), w2.numel(), x.data_ptr(), 2, None, 1e-6, None, None,
                                               0, y.data_ptr(), 64, 256, 0, s) == -3
 
 
