@@ -328,7 +328,9 @@ def run_ours(args) -> None:
            if (rank == 0 and not args.no_cpu) else None)
     decode = decode_leg(dev) if (rank == 0 and not args.no_decode) else None
     batched = batched_leg(dev, W, X, wl, stream) if (rank == 0 and not args.no_batched) else None
-    types = types_leg(dev, stream) if (rank == 0 and not args.no_types) else None
+    # one GPU only: under torchrun the other ranks already wait in the model
+    # legs' first collective while rank 0 runs its single-GPU legs
+    types = types_leg(dev, stream) if (rank == 0 and world == 1 and not args.no_types) else None
     del W, X, Y
     torch.cuda.empty_cache()
     models = None
