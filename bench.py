@@ -521,8 +521,8 @@ OTHER_TYPES = {"Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "Q8_1": 9, "IQ4_NL": 
 def other_payload(t: int, rows: int, cols: int, seed: int) -> bytes:
     """Seeded N(0, 0.02) weights in format t: the package's quantizer where it
     has one, a plain cast for the float formats, and seeded random blocks with
-    finite scales (tests/payloads.py) for Q4_1 / Q5_0 / Q5_1 / Q8_1, which have
-    no encoder here (the bytes streamed per row are the same either way)."""
+    finite scales (tests/payloads.py) for Q8_1, which has no encoder here (the
+    bytes streamed per row are the same either way)."""
     from pyrite_b200.quantize import quantize, quantize_types
     w = gaussian_weights(rows, cols, seed)
     if t in quantize_types():

@@ -212,8 +212,10 @@ int pyrite_cuda_status(int clear);
  * `dst` (dst_len == count / block_size * bytes_per_block), using `threads`
  * host threads (<= 0: all).  Q8_0 / Q4_0 reproduce the reference's fixture
  * encoders byte for byte (scripts/build_vocab_fixture.py:54-92), Q2_K..Q6_K
- * its naive K-quant encoders (tests/k_quant.py:61-285); IQ4_NL / IQ4_XS are
- * this library's own (the reference has no quantizer for them). */
+ * its naive K-quant encoders (tests/k_quant.py:61-285); Q4_1 / Q5_0 / Q5_1
+ * the gguf package's quantizers that the reference's tests use for those
+ * formats (float32 arithmetic on float32-rounded inputs); IQ4_NL / IQ4_XS
+ * are this library's own (the reference has no quantizer for them). */
 int pyrite_quantize(int type_id, const double *src, size_t count, uint8_t *dst, size_t dst_len,
                     int threads);
 

@@ -3,6 +3,7 @@
 // Byte-for-byte restatements of the fixture quantizers the reference tests and
 // scripts use, so the B200 inputs equal the reference's inputs:
 //   Q8_0, Q4_0    scripts/build_vocab_fixture.py:54-92
+//   Q4_1, Q5_0, Q5_1  the gguf package's quantizers (the reference's test oracle)
 //   Q2_K..Q6_K    tests/k_quant.py:61-285 (naive min/max scale choice)
 // plus IQ4_NL / IQ4_XS encoders of our own (the reference has none): a signed
 // per-(sub-)block scale that maps the value of largest magnitude onto the
@@ -89,6 +90,56 @@ void enc_q4_0(const double* v, uint8_t* o) {
     const long long hi = clampll((long long)(v[j + 16] * inv + 8.5), 0, 15);
     o[2 + j] = (uint8_t)(lo | (hi << 4));
   }
+}
+
+// ---- Q4_1, Q5_0, Q5_1 (the gguf package's numpy quantizers, gguf 0.19.0,
+// gguf/quants.py Q4_1 / Q5_0 / Q5_1 quantize_blocks: the test oracle the
+// reference uses for these formats) ----
+// Those run in float32 on float32 input: every step below is one rounded
+// float operation in the same order (no contraction: built with
+// -ffp-contract=off), truncation toward zero, then the uint8 clip.
+// MIN: offset formats (scale over max - min, stored min); otherwise the value
+// of largest magnitude (first on ties) maps to -half.  LEVELS: 15 or 31.
+template <bool MIN, int LEVELS>
+void enc_legacy(const double* v, uint8_t* o) {
+  float x[32];
+  for (int i = 0; i < 32; ++i) x[i] = (float)v[i];
+  float d, lo = 0.0f, bias;
+  if constexpr (MIN) {
+    float mx = x[0];
+    lo = x[0];
+    for (int i = 1; i < 32; ++i) {
+      mx = std::max(mx, x[i]);
+      lo = std::min(lo, x[i]);
+    }
+    d = (mx - lo) / (float)LEVELS;
+    bias = 0.5f;
+  } else {
+    int imax = 0;
+    for (int i = 1; i < 32; ++i)
+      if (std::fabs(x[i]) > std::fabs(x[imax])) imax = i;
+    d = x[imax] / -(float)((LEVELS + 1) / 2);
+    bias = (float)((LEVELS + 1) / 2) + 0.5f;
+  }
+  const float id = d == 0.0f ? 0.0f : 1.0f / d;
+  uint8_t q[32];
+  for (int i = 0; i < 32; ++i) {
+    const float t = MIN ? (x[i] - lo) * id + bias : x[i] * id + bias;
+    q[i] = (uint8_t)std::min<long long>(LEVELS, (long long)std::trunc(t));
+  }
+  int at = 2;
+  put16(o, to_half((double)d));
+  if constexpr (MIN) {
+    put16(o + 2, to_half((double)lo));
+    at = 4;
+  }
+  if constexpr (LEVELS == 31) {  // fifth bits, value i -> bit i (little-endian words)
+    uint32_t qh = 0;
+    for (int i = 0; i < 32; ++i) qh |= (uint32_t)((q[i] >> 4) & 1) << i;
+    for (int k = 0; k < 4; ++k) o[at + k] = (uint8_t)(qh >> (8 * k));
+    at += 4;
+  }
+  for (int j = 0; j < 16; ++j) o[at + j] = (uint8_t)((q[j] & 15) | ((q[j + 16] & 15) << 4));
 }
 
 // 8 (scale, min) 6-bit pairs -> 12 bytes (k_quant._pack_k4_scales)
@@ -325,7 +376,8 @@ void enc_iq4_xs(const double* v, uint8_t* o) {
 using EncFn = void (*)(const double*, uint8_t*);
 struct Enc { int id; int bs; int bpb; EncFn fn; };
 const Enc kEncoders[] = {
-    {2, 32, 18, enc_q4_0},   {8, 32, 34, enc_q8_0},       {10, 256, 84, enc_q2_k},   {11, 256, 110, enc_q3_k},
+    {2, 32, 18, enc_q4_0},   {3, 32, 20, enc_legacy<true, 15>}, {6, 32, 22, enc_legacy<false, 31>},
+    {7, 32, 24, enc_legacy<true, 31>}, {8, 32, 34, enc_q8_0},  {10, 256, 84, enc_q2_k},   {11, 256, 110, enc_q3_k},
     {12, 256, 144, enc_q45_k<15>}, {13, 256, 176, enc_q45_k<31>}, {14, 256, 210, enc_q6_k},
     {20, 32, 18, enc_iq4_nl}, {23, 256, 136, enc_iq4_xs},
 };

@@ -3,8 +3,9 @@
 ``quantize(type_id, values)`` returns the GGML payload bytes of ``values`` (a
 flat float array whose length is a multiple of the block size).  Q8_0 / Q4_0
 and Q2_K..Q6_K are byte-identical to the reference's fixture encoders
-(``scripts/build_vocab_fixture.py`` and ``tests/k_quant.py``); IQ4_NL / IQ4_XS
-use this package's own encoder.
+(``scripts/build_vocab_fixture.py`` and ``tests/k_quant.py``); Q4_1 / Q5_0 /
+Q5_1 to the gguf package's quantizers, which the reference's tests use for
+those formats; IQ4_NL / IQ4_XS use this package's own encoder.
 """
 from __future__ import annotations
 

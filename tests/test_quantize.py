@@ -3,7 +3,9 @@
 The golden bytes were written by the reference's own encoders
 (tests/k_quant.py for Q2_K..Q6_K, scripts/build_vocab_fixture.py for Q8_0 and
 Q4_0; see tests/golden/make_golden.py) over smooth, Gaussian N(0,0.02) and
-edge-case inputs (all-zero block, constant block, a lone spike).  IQ4_NL and
+edge-case inputs (all-zero block, constant block, a lone spike).  Q4_1, Q5_0
+and Q5_1, which the reference tests encode with the gguf package, are
+compared with that package's quantizers byte for byte.  IQ4_NL and
 IQ4_XS have no reference encoder; their bytes are checked for validity:
 decoded by the oracle they land near the input, and the independent gguf
 dequantizer decodes them identically.
@@ -20,7 +22,32 @@ REF_TYPES = [2, 8, 10, 11, 12, 13, 14]
 
 
 def test_quantizer_table():
-    assert set(quantize_types()) == {2, 8, 10, 11, 12, 13, 14, 20, 23}
+    assert set(quantize_types()) == {2, 3, 6, 7, 8, 10, 11, 12, 13, 14, 20, 23}
+
+
+def _gguf_inputs():
+    rng = np.random.default_rng(1)
+    return {
+        "gauss": rng.normal(0, 0.02, 32 * 2048).astype(np.float32),
+        "uniform": rng.uniform(-3, 3, 32 * 512).astype(np.float32),
+        "zeros": np.zeros(32 * 4, np.float32),
+        "constant": np.full(32 * 4, 0.25, np.float32),
+        "ties": np.tile(np.array([1.0, -1.0] * 16, np.float32), 4),
+        "huge": rng.normal(0, 3e4, 32 * 64).astype(np.float32),   # the stored min overflows binary16
+        "tiny": rng.normal(0, 1e-6, 32 * 64).astype(np.float32),  # subnormal scales
+    }
+
+
+@pytest.mark.filterwarnings("ignore::RuntimeWarning")
+@pytest.mark.parametrize("ggml_type,gname", [(3, "Q4_1"), (6, "Q5_0"), (7, "Q5_1")])
+def test_bytes_equal_the_gguf_quantizer(ggml_type, gname):
+    """Q4_1 / Q5_0 / Q5_1 against the gguf package's quantizers (gguf 0.19.0,
+    the reference's test oracle for these formats), byte for byte."""
+    quants = pytest.importorskip("gguf.quants")
+    qtype = getattr(quants.GGMLQuantizationType, gname)
+    for name, x in _gguf_inputs().items():
+        want = quants.quantize(x.reshape(1, -1), qtype).tobytes()
+        assert quantize(ggml_type, x) == want, f"{gname} on {name} inputs"
 
 
 @pytest.mark.parametrize("name", ["smooth", "gauss", "edge"])
