@@ -138,20 +138,29 @@ int pyrite_matvec(int type_id, const uint8_t* data, size_t data_len, const doubl
   // independent, so the results are the same bits as one launch over all rows.
   // (An event of the ring is recorded again only after the compute stream's
   // wait on its previous recording was enqueued, which is all a wait needs.)
-  if ((rc = cuda_code(cudaMemcpyAsync(dx, x, cols * sizeof(double), cudaMemcpyHostToDevice, st.copy)))) return rc;
+  // On an error, copies already queued may still read the caller's buffers:
+  // both streams are drained before returning, so nothing touches them after.
+  auto fail = [&](int code) {
+    cudaStreamSynchronize(st.copy);
+    cudaStreamSynchronize(st.stream);
+    cudaGetLastError();
+    return code;
+  };
+  if ((rc = cuda_code(cudaMemcpyAsync(dx, x, cols * sizeof(double), cudaMemcpyHostToDevice, st.copy))))
+    return fail(rc);
   const size_t chunk_rows = rb >= ((size_t)8 << 20) ? 1 : ((size_t)8 << 20) / rb;
   int k = 0;
   for (size_t r0 = 0; r0 < rows; r0 += chunk_rows, k = (k + 1) % kStageEvents) {
     const size_t n = rows - r0 < chunk_rows ? rows - r0 : chunk_rows;
     if ((rc = cuda_code(cudaMemcpyAsync(dw + r0 * rb, data + r0 * rb, n * rb, cudaMemcpyHostToDevice, st.copy))))
-      return rc;
-    if ((rc = cuda_code(cudaEventRecord(st.ev[k], st.copy)))) return rc;
-    if ((rc = cuda_code(cudaStreamWaitEvent(st.stream, st.ev[k], 0)))) return rc;
+      return fail(rc);
+    if ((rc = cuda_code(cudaEventRecord(st.ev[k], st.copy)))) return fail(rc);
+    if ((rc = cuda_code(cudaStreamWaitEvent(st.stream, st.ev[k], 0)))) return fail(rc);
     MatvecArgs<double> a{dw + r0 * rb, rb, (int)n, (int)cols, dx, 0, dy + r0, 0};
-    if ((rc = launch_mv_generic<double, 1>(type_id, a, st.stream))) return rc > 0 ? PYRITE_E_CUDA : rc;
+    if ((rc = launch_mv_generic<double, 1>(type_id, a, st.stream))) return fail(rc > 0 ? PYRITE_E_CUDA : rc);
   }
   if ((rc = cuda_code(cudaMemcpyAsync(out, dy, rows * sizeof(double), cudaMemcpyDeviceToHost, st.stream))))
-    return rc;
+    return fail(rc);
   return cuda_code(cudaStreamSynchronize(st.stream));
 }
 
@@ -169,12 +178,18 @@ int pyrite_dequantize_rows(int type_id, const uint8_t* data, size_t data_len, do
   if ((rc = stage_reserve(st, ooff + rows * cols * sizeof(double)))) return rc;
   uint8_t* dw = static_cast<uint8_t*>(st.buf);
   double* dout = reinterpret_cast<double*>(dw + ooff);
-  if ((rc = cuda_code(cudaMemcpyAsync(dw, data, data_len, cudaMemcpyHostToDevice, st.stream)))) return rc;
+  // as in pyrite_matvec: drain the stream before an error return
+  auto fail = [&](int code) {
+    cudaStreamSynchronize(st.stream);
+    cudaGetLastError();
+    return code;
+  };
+  if ((rc = cuda_code(cudaMemcpyAsync(dw, data, data_len, cudaMemcpyHostToDevice, st.stream)))) return fail(rc);
   if ((rc = launch_dq_generic<double>(type_id, dw, rb, (int)rows, (int)cols, dout, (long long)cols, st.stream)))
-    return rc > 0 ? PYRITE_E_CUDA : rc;
+    return fail(rc > 0 ? PYRITE_E_CUDA : rc);
   if ((rc = cuda_code(cudaMemcpyAsync(out, dout, rows * cols * sizeof(double), cudaMemcpyDeviceToHost,
                                       st.stream))))
-    return rc;
+    return fail(rc);
   return cuda_code(cudaStreamSynchronize(st.stream));
 }
 
